@@ -1,0 +1,340 @@
+// Shared device/host helpers for the sm_100a kernels of the H3 VAE INT8 path.
+//
+// Everything here is hand-written inline PTX for the Blackwell data-centre
+// tensor-core path: mbarriers, TMA (cp.async.bulk.tensor, no cluster
+// multicast anywhere), and the tcgen05 family (TMEM alloc, MMA, commit, ld).
+// Every spin-wait is bounded: after kSpinLimit polls it records an error code
+// in the caller-visible device error word and reports failure so the kernel
+// can unwind instead of hanging the GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <initializer_list>
+
+#include "../../../include/h3vae_b200.h"
+
+namespace h3b {
+
+// ---------------------------------------------------------------------------
+// Device error word.  Kernels OR a code into it when a bounded wait expires or
+// an internal invariant fails; the host reads it with h3b_device_error().
+// ---------------------------------------------------------------------------
+// Defined here: the library is built as one translation unit.
+__device__ unsigned int g_device_error = 0;
+
+enum DeviceErrorBits : unsigned int {
+  kErrBarrierTimeout = 1u << 0,
+  kErrTmemAlloc = 1u << 1,
+  kErrBadGeometry = 1u << 2,
+};
+
+// About 2^25 polls of try_wait (each suspends for a few hundred ns at most):
+// well above any legitimate wait, well below a watchdog.
+constexpr uint32_t kSpinLimit = 1u << 25;
+
+__device__ __forceinline__ void record_error(unsigned int bits) {
+  atomicOr(&g_device_error, bits);
+}
+
+// ---------------------------------------------------------------------------
+// Shared-memory address helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ bool elect_one_sync() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+// ---------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n\t}" ::"r"(smem_u32(bar)),
+      "r"(bytes)
+      : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded wait on a phase parity.  Returns false (and records the error) if
+// the phase never completes or if another role already aborted the CTA.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && abort_flag != nullptr && *abort_flag) return false;
+  }
+  record_error(kErrBarrierTimeout);
+  if (abort_flag != nullptr) *abort_flag = 1;
+  return false;
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tiled, no multicast)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1, int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_5d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0,
+                                            int c1, int c2, int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3),
+      "r"(c4)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: TMEM allocation, MMA issue, commit, loads
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, int8 x int8 -> int32.
+__device__ __forceinline__ void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A * B^T, fp16 x fp16 -> fp32.
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive on an mbarrier once all previously issued tcgen05 ops of this thread
+// have completed.
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit columns: each thread gets its lane's 32 words.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+        "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+        "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+        "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand tile stored in the
+// 128-byte swizzle canonical layout: rows of 128 bytes, 8-row atoms of 1024 B
+// (stride-byte-offset 1024), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);
+  d |= static_cast<uint64_t>(1u) << 16;              // leading byte offset (unused for swizzled K-major)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;      // stride byte offset: 8 rows x 128 B
+  d |= static_cast<uint64_t>(1u) << 46;              // descriptor version (Blackwell)
+  d |= static_cast<uint64_t>(2u) << 61;              // layout: SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: M=128, N=n, signed int8 A/B (K-major), int32 accumulate.
+__host__ __device__ constexpr uint32_t make_idesc_i8(uint32_t m, uint32_t n) {
+  return (2u << 4)            // D format: S32
+         | (1u << 7)          // A format: signed 8-bit
+         | (1u << 10)         // B format: signed 8-bit
+         | ((n >> 3) << 17)   // N >> 3
+         | ((m >> 4) << 24);  // M >> 4
+}
+
+// Instruction descriptor: fp16 A/B (K-major), fp32 accumulate.
+__host__ __device__ constexpr uint32_t make_idesc_f16(uint32_t m, uint32_t n) {
+  return (1u << 4)            // D format: F32
+         | (0u << 7)          // A format: F16
+         | (0u << 10)         // B format: F16
+         | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+// ---------------------------------------------------------------------------
+// Small numeric helpers shared by the epilogues and producers.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float round_fp16(float v) { return __half2float(__float2half_rn(v)); }
+
+// Half-away-from-zero rounding in the exact fp32 order the encoder quantizer
+// uses: floor(s + 0.5) for s >= 0, -floor(-s + 0.5) otherwise, clamp +-127.
+__device__ __forceinline__ int8_t quant_half_away(float x, float scale) {
+  float s = __fdiv_rn(x, scale);
+  float r = (s >= 0.0f) ? floorf(__fadd_rn(s, 0.5f)) : -floorf(__fadd_rn(-s, 0.5f));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return static_cast<int8_t>(static_cast<int>(r));
+}
+
+// Row quantization rule of the decoder's INT8 linears: divide in fp32 by the
+// fp16-rounded scale, round the quotient to fp16, then to nearest-even,
+// NaN -> -128, clamp to [-128, 127].
+__device__ __forceinline__ int8_t quant_row_ck(float act, float denom) {
+  float v = round_fp16(__fdiv_rn(act, denom));
+  v = rintf(v);
+  if (v != v) v = -128.0f;
+  v = fminf(127.0f, fmaxf(-128.0f, v));
+  return static_cast<int8_t>(static_cast<int>(v));
+}
+
+__device__ __forceinline__ float row_scale_ck(float amax) {
+  return fmaxf(__fmul_rn(amax, 1.0f / 127.0f), 1.0e-30f);
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Non-negative floats order like their bit patterns, so an unsigned atomicMax
+// on the bits is an exact float max for values >= 0 (NaN excluded).
+__device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
+  atomicMax(reinterpret_cast<unsigned int*>(addr), __float_as_uint(v));
+}
+
+// QK RMSNorm (fp32 statistics, no affine) + fp16 round + rotate-half rotary
+// embedding on the first R dims of one 64-wide head vector held in registers.
+// Products are rounded to fp16 individually before the fp32 sum, and the sum
+// is rounded to fp16 on store.  dst must be 16-byte aligned.
+__device__ __forceinline__ void qk_norm_rope_store(float (&x)[64], float eps, int R, const __half* cs,
+                                                   const __half* sn, __half* dst) {
+  float ss = 0.0f;
+#pragma unroll
+  for (int d = 0; d < 64; ++d) ss = __fmaf_rn(x[d], x[d], ss);
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / 64.0f), eps));
+#pragma unroll
+  for (int d = 0; d < 64; ++d) x[d] = round_fp16(__fmul_rn(x[d], inv));
+  const int half_r = R >> 1;
+  __align__(16) __half outv[64];
+#pragma unroll
+  for (int d = 0; d < 64; ++d) {
+    float o = x[d];
+    if (d < R) {
+      const float rot = (d < half_r) ? -x[d + half_r] : x[d - half_r];
+      const float a = round_fp16(__fmul_rn(x[d], __half2float(cs[d])));
+      const float b = round_fp16(__fmul_rn(rot, __half2float(sn[d])));
+      o = __fadd_rn(a, b);
+    }
+    outv[d] = __float2half_rn(o);
+  }
+#pragma unroll
+  for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(dst)[q] = reinterpret_cast<const uint4*>(outv)[q];
+}
+
+}  // namespace h3b
+
+// ---------------------------------------------------------------------------
+// Host-side helpers (error string, tensor-map encoding through the driver
+// entry point so the library does not link libcuda directly).
+// ---------------------------------------------------------------------------
+namespace h3b_host {
+
+int set_error(int code, const char* fmt, ...);
+int check_launch(const char* what);
+int encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, uint32_t rank, const void* gaddr,
+                 const uint64_t* dims, const uint64_t* strides_bytes /* rank-1 entries */,
+                 const uint32_t* box, const uint32_t* elem_strides, CUtensorMapSwizzle swizzle);
+int num_sms();
+
+}  // namespace h3b_host

@@ -1,0 +1,581 @@
+// Memory-bound encoder producers (HBM roofline kernels).
+//
+// All activations are NDHWC fp16 ("channels_last_3d").  One thread owns one
+// 16-byte vector of 8 consecutive channels, so every global access is a
+// coalesced 16-byte (fp16) or 8-byte (int8) transaction.
+//
+//   gn_partial_kernel   per (b, frame, chunk of positions): per-group chunk mean
+//                       and centred M2 (two passes over registers), the
+//                       statistic the GroupNorm merge consumes.
+//   gn_merge_kernel     Chan merge of the chunk partials -> (mean, rstd) per
+//                       (b, frame, group).
+//   norm_pack_kernel    GroupNorm affine -> fp16 -> SiLU -> fp16, reflect pad 1
+//                       in H/W and two zero frames in front; modes: absmax of the
+//                       interior, INT8 with the per-tensor scale, or fp16 output.
+//   residual_pack_kernel, quantize kernels, finalize_pixels_kernel.
+#include "common.cuh"
+
+namespace h3b {
+
+constexpr int kGroups = 32;
+constexpr int kVec = 8;            // fp16 channels per thread vector
+constexpr int kPackThreads = 256;
+constexpr int kStatThreads = 256;
+constexpr int kStatValuesPerThread = 64;  // 8 vectors of 8 channels
+constexpr int kStatElemsPerCta = kStatThreads * kStatValuesPerThread;
+
+struct NormShape {
+  int B, C, D, H, W;
+  int positions_per_chunk;  // P
+  int nchunks;              // ceil(H*W / P)
+};
+
+__device__ __forceinline__ void load_h8(const __half* src, float (&v)[8]) {
+  uint4 raw = *reinterpret_cast<const uint4*>(src);
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    float2 f = __half22float2(h[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+
+__device__ __forceinline__ void store_h8(__half* dst, const float (&v)[8]) {
+  __align__(16) __half2 h[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[2 * j], v[2 * j + 1]);
+  *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(h);
+}
+
+// ---------------------------------------------------------------------------
+// GroupNorm statistics, pass 1: chunk partials.
+// grid = (nchunks, B*D), block = 256.  The chunk covers P = 16384 / C positions
+// of one (b, frame); thread tid owns channel vector v = tid % (C/8) and the
+// positions tid / (C/8) + k * (256 / (C/8)).
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* __restrict__ x,
+                                                                  const __half* __restrict__ pre_bias,
+                                                                  NormShape s, float2* __restrict__ partials) {
+  __shared__ float red[kStatThreads * kVec];
+  __shared__ float group_mean[kGroups];
+  const int tid = threadIdx.x;
+  const int chunk = blockIdx.x;
+  const int bt = blockIdx.y;
+  const int vpp = s.C / kVec;                 // vectors per position
+  const int pos_per_iter = kStatThreads / vpp;
+  const int v = tid % vpp;
+  const int c0 = v * kVec;
+  const int HW = s.H * s.W;
+  const int p0 = chunk * s.positions_per_chunk;
+  const int valid_pos = min(s.positions_per_chunk, HW - p0);
+  const int cg = s.C / kGroups;
+
+  float pb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  if (pre_bias != nullptr) load_h8(pre_bias + c0, pb);
+
+  const __half* base = x + (static_cast<int64_t>(bt) * HW + p0) * s.C + c0;
+  float vals[kStatValuesPerThread];
+  int nvec = 0;
+  float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+  for (int k = 0; k < kStatValuesPerThread / kVec; ++k) {
+    const int p = tid / vpp + k * pos_per_iter;
+    float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (p < valid_pos) {
+      load_h8(base + static_cast<int64_t>(p) * s.C, f);
+      if (pre_bias != nullptr) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
+      }
+      ++nvec;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sum[j] = __fadd_rn(sum[j], f[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) vals[k * 8 + j] = f[j];
+  }
+  // Per-channel chunk sums -> per-group sums.
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[tid * 8 + j] = sum[j];
+  __syncthreads();
+  if (tid < kGroups) {
+    float acc = 0.0f;
+    for (int c = tid * cg; c < (tid + 1) * cg; ++c) {
+      const int vv = c / kVec, jj = c % kVec;
+      for (int t = vv; t < kStatThreads; t += vpp) acc += red[t * 8 + jj];
+    }
+    const float count = static_cast<float>(valid_pos) * cg;
+    group_mean[tid] = __fdiv_rn(acc, count);
+  }
+  __syncthreads();
+  // Centred second moment over the values held in registers.
+  float m2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+  for (int k = 0; k < kStatValuesPerThread / kVec; ++k) {
+    const int p = tid / vpp + k * pos_per_iter;
+    if (p < valid_pos) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float d = vals[k * 8 + j] - group_mean[(c0 + j) / cg];
+        m2[j] = __fmaf_rn(d, d, m2[j]);
+      }
+    }
+  }
+  (void)nvec;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[tid * 8 + j] = m2[j];
+  __syncthreads();
+  if (tid < kGroups) {
+    float acc = 0.0f;
+    for (int c = tid * cg; c < (tid + 1) * cg; ++c) {
+      const int vv = c / kVec, jj = c % kVec;
+      for (int t = vv; t < kStatThreads; t += vpp) acc += red[t * 8 + jj];
+    }
+    partials[(static_cast<int64_t>(bt) * s.nchunks + chunk) * kGroups + tid] = make_float2(group_mean[tid], acc);
+  }
+}
+
+// GroupNorm statistics, pass 2: one warp per group of one (b, frame).
+__global__ void gn_merge_kernel(const float2* __restrict__ partials, NormShape s, float eps,
+                                float2* __restrict__ stats) {
+  const int bt = blockIdx.x;
+  const int g = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int HW = s.H * s.W;
+  const int cg = s.C / kGroups;
+  const float total = static_cast<float>(HW) * cg;
+  const float2* part = partials + static_cast<int64_t>(bt) * s.nchunks * kGroups + g;
+  float wsum = 0.0f;
+  for (int i = lane; i < s.nchunks; i += 32) {
+    const float cnt = static_cast<float>(min(s.positions_per_chunk, HW - i * s.positions_per_chunk) * cg);
+    wsum = __fmaf_rn(part[i * kGroups].x, cnt, wsum);
+  }
+  const float mean = __fdiv_rn(warp_sum(wsum), total);
+  float m2 = 0.0f;
+  for (int i = lane; i < s.nchunks; i += 32) {
+    const float cnt = static_cast<float>(min(s.positions_per_chunk, HW - i * s.positions_per_chunk) * cg);
+    const float2 pm = part[i * kGroups];
+    const float delta = pm.x - mean;
+    m2 += pm.y + cnt * delta * delta;
+  }
+  const float var = __fdiv_rn(warp_sum(m2), total);
+  if (lane == 0) stats[static_cast<int64_t>(bt) * kGroups + g] = make_float2(mean, rsqrtf(fmaxf(var, 0.0f) + eps));
+}
+
+// ---------------------------------------------------------------------------
+// Norm -> SiLU -> pad producer.  MODE 0: absmax of the interior (atomic on
+// amax_out); MODE 1: INT8 output with scale from amax; MODE 2: fp16 output.
+// ---------------------------------------------------------------------------
+template <int MODE>
+__global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* __restrict__ x,
+                                                                 const __half* __restrict__ pre_bias,
+                                                                 const __half* __restrict__ gamma,
+                                                                 const __half* __restrict__ beta,
+                                                                 const float2* __restrict__ stats, NormShape s,
+                                                                 float* amax, float* scale_out, void* out) {
+  const int vpp = s.C / kVec;
+  const int Dp = s.D + 2, Hp = s.H + 2, Wp = s.W + 2;
+  const int cg = s.C / kGroups;
+  // MODE 0 only walks the interior; the padded ring duplicates interior values
+  // or is zero, so it cannot raise the maximum.
+  const int64_t positions = (MODE == 0) ? static_cast<int64_t>(s.B) * s.D * s.H * s.W
+                                        : static_cast<int64_t>(s.B) * Dp * Hp * Wp;
+  const int64_t total = positions * vpp;
+  float scale = 1.0f;
+  if (MODE == 1) {
+    const float m = *amax;
+    scale = __fmul_rn(m, 1.0f / 127.0f);
+    if (!(scale > 0.0f)) scale = 1.0f;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+  }
+  float local_max = 0.0f;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kPackThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kPackThreads) {
+    const int v = static_cast<int>(i % vpp);
+    int64_t pos = i / vpp;
+    int b, t, h, w;
+    bool inside;
+    if (MODE == 0) {
+      w = static_cast<int>(pos % s.W); pos /= s.W;
+      h = static_cast<int>(pos % s.H); pos /= s.H;
+      t = static_cast<int>(pos % s.D);
+      b = static_cast<int>(pos / s.D);
+      inside = true;
+    } else {
+      const int wp = static_cast<int>(pos % Wp); pos /= Wp;
+      const int hp = static_cast<int>(pos % Hp); pos /= Hp;
+      const int tp = static_cast<int>(pos % Dp);
+      b = static_cast<int>(pos / Dp);
+      t = tp - 2;
+      h = hp - 1;
+      w = wp - 1;
+      h = h < 0 ? -h : (h >= s.H ? 2 * s.H - 2 - h : h);
+      w = w < 0 ? -w : (w >= s.W ? 2 * s.W - 2 - w : w);
+      inside = t >= 0;
+    }
+    const int c0 = v * kVec;
+    float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (inside) {
+      float f[8], gm[8], bt[8];
+      load_h8(x + ((((static_cast<int64_t>(b) * s.D + t) * s.H + h) * s.W) + w) * s.C + c0, f);
+      load_h8(gamma + c0, gm);
+      load_h8(beta + c0, bt);
+      if (pre_bias != nullptr) {
+        float pb[8];
+        load_h8(pre_bias + c0, pb);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
+      }
+      const float2* st = stats + (static_cast<int64_t>(b) * s.D + t) * kGroups;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 mr = st[(c0 + j) / cg];
+        float y = __fmul_rn(__fsub_rn(f[j], mr.x), mr.y);
+        y = round_fp16(__fadd_rn(__fmul_rn(y, gm[j]), bt[j]));
+        z[j] = round_fp16(__fdiv_rn(y, __fadd_rn(1.0f, expf(-y))));
+      }
+    }
+    if (MODE == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) local_max = fmaxf(local_max, fabsf(z[j]));
+    } else if (MODE == 1) {
+      __align__(8) int8_t q[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[j] = quant_half_away(z[j], scale);
+      reinterpret_cast<uint2*>(out)[i] = *reinterpret_cast<const uint2*>(q);
+    } else {
+      store_h8(reinterpret_cast<__half*>(out) + i * kVec, z);
+    }
+  }
+  if (MODE == 0) {
+    __shared__ float wmax[kPackThreads / 32];
+    local_max = warp_max(local_max);
+    if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = local_max;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+      float m = threadIdx.x < kPackThreads / 32 ? wmax[threadIdx.x] : 0.0f;
+      m = warp_max(m);
+      if (threadIdx.x == 0) atomic_max_nonneg(amax, m);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Residual + bias pack with right/bottom reflect (+1) and two causal zero
+// frames: y = fp16(r + (x + bias)) in fp32.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(kPackThreads) residual_pack_kernel(const __half* __restrict__ x,
+                                                                     const __half* __restrict__ r,
+                                                                     const __half* __restrict__ bias, int B, int C,
+                                                                     int D, int H, int W, __half* __restrict__ y) {
+  const int vpp = C / kVec;
+  const int Dp = D + 2, Hp = H + 1, Wp = W + 1;
+  const int64_t total = static_cast<int64_t>(B) * Dp * Hp * Wp * vpp;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(kPackThreads) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * kPackThreads) {
+    const int v = static_cast<int>(i % vpp);
+    int64_t pos = i / vpp;
+    const int wp = static_cast<int>(pos % Wp); pos /= Wp;
+    const int hp = static_cast<int>(pos % Hp); pos /= Hp;
+    const int tp = static_cast<int>(pos % Dp);
+    const int b = static_cast<int>(pos / Dp);
+    const int t = tp - 2;
+    const int h = hp == H ? H - 2 : hp;
+    const int w = wp == W ? W - 2 : wp;
+    float out[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (t >= 0) {
+      const int64_t off = ((((static_cast<int64_t>(b) * D + t) * H + h) * W) + w) * C + v * kVec;
+      float fx[8], fr[8], fb[8];
+      load_h8(x + off, fx);
+      load_h8(r + off, fr);
+      load_h8(bias + v * kVec, fb);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) out[j] = __fadd_rn(fr[j], __fadd_rn(fx[j], fb[j]));
+    }
+    store_h8(y + i * kVec, out);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-tensor quantization of an arbitrary-strided fp16 [B,C,D,H,W] tensor into
+// NDHWC int8 (destination-ordered, like the reference's legacy kernel).
+// ---------------------------------------------------------------------------
+struct Strided5 {
+  int64_t n[5];  // B, C, D, H, W
+  int64_t s[5];
+};
+
+__device__ __forceinline__ int64_t strided_offset_ndhwc(const Strided5& t, int64_t i) {
+  const int64_t c = i % t.n[1];
+  int64_t r = i / t.n[1];
+  const int64_t w = r % t.n[4]; r /= t.n[4];
+  const int64_t h = r % t.n[3]; r /= t.n[3];
+  const int64_t d = r % t.n[2];
+  const int64_t b = r / t.n[2];
+  return b * t.s[0] + c * t.s[1] + d * t.s[2] + h * t.s[3] + w * t.s[4];
+}
+
+__global__ void tensor_absmax_kernel(const __half* __restrict__ x, Strided5 t, int64_t total, float* amax) {
+  float m = 0.0f;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    m = fmaxf(m, fabsf(__half2float(x[strided_offset_ndhwc(t, i)])));
+  __shared__ float wmax[32];
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) wmax[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < (blockDim.x >> 5) ? wmax[threadIdx.x] : 0.0f;
+    v = warp_max(v);
+    if (threadIdx.x == 0) atomic_max_nonneg(amax, v);
+  }
+}
+
+__global__ void tensor_quant_kernel(const __half* __restrict__ x, Strided5 t, int64_t total, const float* amax,
+                                    int8_t* __restrict__ q, float* scale_out) {
+  float scale = __fmul_rn(*amax, 1.0f / 127.0f);
+  if (!(scale > 0.0f)) scale = 1.0f;
+  if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    q[i] = quant_half_away(__half2float(x[strided_offset_ndhwc(t, i)]), scale);
+}
+
+// ---------------------------------------------------------------------------
+// Pixel finalization: clamp(x*std + mean, 0, 1) without FMA, NaN preserved.
+// ---------------------------------------------------------------------------
+template <typename T>
+__global__ void finalize_pixels_kernel(const T* __restrict__ x, Strided5 t, int64_t total,
+                                       const float* __restrict__ std3, const float* __restrict__ mean3,
+                                       float* __restrict__ out, int contiguous) {
+  const int64_t thw = t.n[2] * t.n[3] * t.n[4];
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>((i / thw) % 3);
+    int64_t off = i;
+    if (!contiguous) {
+      const int64_t w = i % t.n[4];
+      const int64_t h = (i / t.n[4]) % t.n[3];
+      const int64_t d = (i / (t.n[4] * t.n[3])) % t.n[2];
+      const int64_t b = i / (thw * 3);
+      off = b * t.s[0] + c * t.s[1] + d * t.s[2] + h * t.s[3] + w * t.s[4];
+    }
+    float v;
+    if constexpr (sizeof(T) == 2) v = __half2float(x[off]);
+    else v = x[off];
+    float value = __fadd_rn(__fmul_rn(v, std3[c]), mean3[c]);
+    value = value < 0.0f ? 0.0f : (value > 1.0f ? 1.0f : value);
+    out[i] = value;
+  }
+}
+
+}  // namespace h3b
+
+// ===========================================================================
+// Host entry points
+// ===========================================================================
+namespace {
+
+using namespace h3b;
+
+int grid_for(int64_t work_items, int threads) {
+  int64_t blocks = (work_items + threads - 1) / threads;
+  const int64_t cap = static_cast<int64_t>(h3b_host::num_sms()) * 16;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return static_cast<int>(blocks);
+}
+
+bool norm_shape(int64_t B, int64_t C, int64_t D, int64_t H, int64_t W, NormShape* s) {
+  if (B <= 0 || C <= 0 || D <= 0 || H < 2 || W < 2) return false;
+  if (C % kGroups != 0 || C % kVec != 0 || (kStatThreads % (C / kVec)) != 0) return false;
+  if (B * (D + 2) * (H + 2) * (W + 2) * C >= (int64_t(1) << 40)) return false;
+  s->B = (int)B; s->C = (int)C; s->D = (int)D; s->H = (int)H; s->W = (int)W;
+  s->positions_per_chunk = kStatElemsPerCta / (int)C;
+  s->nchunks = (int)((H * W + s->positions_per_chunk - 1) / s->positions_per_chunk);
+  return true;
+}
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+struct NormWorkspace {
+  float2* partials;
+  float2* stats;
+  float* amax;
+  size_t bytes;
+};
+
+NormWorkspace norm_workspace_layout(const NormShape& s, void* base) {
+  NormWorkspace w{};
+  const size_t part = align256(sizeof(float2) * (size_t)s.B * s.D * s.nchunks * kGroups);
+  const size_t st = align256(sizeof(float2) * (size_t)s.B * s.D * kGroups);
+  uint8_t* p = static_cast<uint8_t*>(base);
+  w.partials = reinterpret_cast<float2*>(p);
+  w.stats = reinterpret_cast<float2*>(p + part);
+  w.amax = reinterpret_cast<float*>(p + part + st);
+  w.bytes = part + st + 256;
+  return w;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int run_norm_stats(const void* x, const void* pre_bias, float eps, const NormShape& s, const NormWorkspace& w,
+                   cudaStream_t st, const char* name) {
+  dim3 grid(s.nchunks, s.B * s.D);
+  gn_partial_kernel<<<grid, kStatThreads, 0, st>>>(static_cast<const __half*>(x),
+                                                   static_cast<const __half*>(pre_bias), s, w.partials);
+  int rc = h3b_host::check_launch(name);
+  if (rc) return rc;
+  gn_merge_kernel<<<s.B * s.D, 32 * kGroups, 0, st>>>(w.partials, s, eps, w.stats);
+  return h3b_host::check_launch(name);
+}
+
+int check_norm_args(const void* x, const void* pre_bias, const void* gamma, const void* beta, const void* out,
+                    void* workspace, size_t workspace_bytes, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
+                    NormShape* s, NormWorkspace* w, const char* name) {
+  if (!x || !gamma || !beta || !out || !workspace) return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  if (!norm_shape(B, C, D, H, W, s))
+    return h3b_host::set_error(H3B_EUNSUPPORTED,
+                               "%s: unsupported shape B=%lld C=%lld D=%lld H=%lld W=%lld (need H,W>=2, C a power of "
+                               "two in [32, 2048])",
+                               name, (long long)B, (long long)C, (long long)D, (long long)H, (long long)W);
+  for (const void* p : std::initializer_list<const void*>{x, gamma, beta, out})
+    if (!aligned16(p)) return h3b_host::set_error(H3B_EINVAL, "%s: tensors must be 16-byte aligned", name);
+  if (pre_bias && !aligned16(pre_bias)) return h3b_host::set_error(H3B_EINVAL, "%s: pre_bias must be 16-byte aligned", name);
+  *w = norm_workspace_layout(*s, workspace);
+  if (workspace_bytes < w->bytes)
+    return h3b_host::set_error(H3B_EINVAL, "%s: workspace %zu bytes < required %zu", name, workspace_bytes, w->bytes);
+  return H3B_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t h3b_norm_workspace_size(int64_t B, int64_t C, int64_t D, int64_t H, int64_t W) {
+  NormShape s;
+  if (!norm_shape(B, C, D, H, W, &s)) return 0;
+  return norm_workspace_layout(s, nullptr).bytes;
+}
+
+int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W, const void* pre_bias,
+                       const void* gamma, const void* beta, float eps, int8_t* q, float* scale, void* workspace,
+                       size_t workspace_bytes, h3b_stream_t stream) {
+  const char* name = "h3b_norm_pad_quant";
+  NormShape s;
+  NormWorkspace w;
+  int rc = check_norm_args(x, pre_bias, gamma, beta, q, workspace, workspace_bytes, B, C, D, H, W, &s, &w, name);
+  if (rc) return rc;
+  if (!scale) return h3b_host::set_error(H3B_EINVAL, "%s: NULL scale", name);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = run_norm_stats(x, pre_bias, eps, s, w, st, name);
+  if (rc) return rc;
+  if (cudaMemsetAsync(w.amax, 0, sizeof(float), st) != cudaSuccess)
+    return h3b_host::set_error(H3B_ECUDA, "%s: memset failed", name);
+  const int vpp = (int)(C / kVec);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* pb = static_cast<const __half*>(pre_bias);
+  const __half* gh = static_cast<const __half*>(gamma);
+  const __half* bh = static_cast<const __half*>(beta);
+  norm_pack_kernel<0><<<grid_for(B * D * H * W * vpp, kPackThreads), kPackThreads, 0, st>>>(
+      xh, pb, gh, bh, w.stats, s, w.amax, nullptr, nullptr);
+  rc = h3b_host::check_launch(name);
+  if (rc) return rc;
+  norm_pack_kernel<1><<<grid_for(B * (D + 2) * (H + 2) * (W + 2) * vpp, kPackThreads), kPackThreads, 0, st>>>(
+      xh, pb, gh, bh, w.stats, s, w.amax, scale, q);
+  return h3b_host::check_launch(name);
+}
+
+int h3b_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W, const void* pre_bias,
+                     const void* gamma, const void* beta, float eps, void* y, void* workspace, size_t workspace_bytes,
+                     h3b_stream_t stream) {
+  const char* name = "h3b_norm_pad_f16";
+  NormShape s;
+  NormWorkspace w;
+  int rc = check_norm_args(x, pre_bias, gamma, beta, y, workspace, workspace_bytes, B, C, D, H, W, &s, &w, name);
+  if (rc) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = run_norm_stats(x, pre_bias, eps, s, w, st, name);
+  if (rc) return rc;
+  const int vpp = (int)(C / kVec);
+  norm_pack_kernel<2><<<grid_for(B * (D + 2) * (H + 2) * (W + 2) * vpp, kPackThreads), kPackThreads, 0, st>>>(
+      static_cast<const __half*>(x), static_cast<const __half*>(pre_bias), static_cast<const __half*>(gamma),
+      static_cast<const __half*>(beta), w.stats, s, nullptr, nullptr, y);
+  return h3b_host::check_launch(name);
+}
+
+int h3b_residual_pack(const void* x, const void* r, const void* bias, int64_t B, int64_t C, int64_t D, int64_t H,
+                      int64_t W, void* y, h3b_stream_t stream) {
+  const char* name = "h3b_residual_pack";
+  if (!x || !r || !bias || !y) return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  if (B <= 0 || C <= 0 || D <= 0 || H < 2 || W < 2 || C % kVec)
+    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: need H,W >= 2 and C %% 8 == 0", name);
+  for (const void* p : std::initializer_list<const void*>{x, r, bias, y})
+    if (!aligned16(p)) return h3b_host::set_error(H3B_EINVAL, "%s: tensors must be 16-byte aligned", name);
+  const int64_t total = B * (D + 2) * (H + 1) * (W + 1) * (C / kVec);
+  residual_pack_kernel<<<grid_for(total, kPackThreads), kPackThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), static_cast<const __half*>(r), static_cast<const __half*>(bias), (int)B, (int)C,
+      (int)D, (int)H, (int)W, static_cast<__half*>(y));
+  return h3b_host::check_launch(name);
+}
+
+size_t h3b_quantize_tensor_workspace_size(void) { return 256; }
+
+int h3b_quantize_tensor_i8(const void* x, const int64_t* dims5, const int64_t* strides5, int8_t* q, float* scale,
+                           void* workspace, size_t workspace_bytes, h3b_stream_t stream) {
+  const char* name = "h3b_quantize_tensor_i8";
+  if (!x || !dims5 || !strides5 || !q || !scale || !workspace)
+    return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  if (workspace_bytes < h3b_quantize_tensor_workspace_size())
+    return h3b_host::set_error(H3B_EINVAL, "%s: workspace too small", name);
+  Strided5 t{};
+  int64_t total = 1;
+  for (int i = 0; i < 5; ++i) {
+    t.n[i] = dims5[i];
+    t.s[i] = strides5[i];
+    if (dims5[i] <= 0) return h3b_host::set_error(H3B_EINVAL, "%s: activation must be nonempty", name);
+    total *= dims5[i];
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  float* amax = static_cast<float*>(workspace);
+  if (cudaMemsetAsync(amax, 0, sizeof(float), st) != cudaSuccess)
+    return h3b_host::set_error(H3B_ECUDA, "%s: memset failed", name);
+  tensor_absmax_kernel<<<grid_for(total, 256), 256, 0, st>>>(static_cast<const __half*>(x), t, total, amax);
+  int rc = h3b_host::check_launch(name);
+  if (rc) return rc;
+  tensor_quant_kernel<<<grid_for(total, 256), 256, 0, st>>>(static_cast<const __half*>(x), t, total, amax, q, scale);
+  return h3b_host::check_launch(name);
+}
+
+int h3b_finalize_pixels(const void* x, int x_is_fp16, const int64_t* dims5, const int64_t* strides5,
+                        const float* std3, const float* mean3, float* out, h3b_stream_t stream) {
+  const char* name = "h3b_finalize_pixels";
+  if (!x || !dims5 || !strides5 || !std3 || !mean3 || !out)
+    return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  if (dims5[1] != 3) return h3b_host::set_error(H3B_EINVAL, "%s: nonempty B,3,T,H,W tensor required", name);
+  Strided5 t{};
+  int64_t total = 1;
+  for (int i = 0; i < 5; ++i) {
+    t.n[i] = dims5[i];
+    t.s[i] = strides5[i];
+    if (dims5[i] <= 0) return h3b_host::set_error(H3B_EINVAL, "%s: nonempty B,3,T,H,W tensor required", name);
+    total *= dims5[i];
+  }
+  int64_t expect = 1;
+  int contiguous = 1;
+  for (int i = 4; i >= 0; --i) {
+    if (t.n[i] != 1 && t.s[i] != expect) contiguous = 0;
+    expect *= t.n[i];
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (x_is_fp16)
+    finalize_pixels_kernel<__half><<<grid_for(total, 256), 256, 0, st>>>(static_cast<const __half*>(x), t, total, std3,
+                                                                          mean3, out, contiguous);
+  else
+    finalize_pixels_kernel<float><<<grid_for(total, 256), 256, 0, st>>>(static_cast<const float*>(x), t, total, std3,
+                                                                         mean3, out, contiguous);
+  return h3b_host::check_launch(name);
+}
+
+}  // extern "C"

@@ -1,0 +1,410 @@
+"""Tensor-level wrappers over the C ABI.
+
+Each function validates dtypes / devices / layouts on the host (raising
+ValueError before any launch), allocates outputs and workspaces with the
+PyTorch caching allocator, and launches on the caller's current CUDA stream.
+These are the only functions in the package that touch the native library.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+F16 = torch.float16
+I8 = torch.int8
+F32 = torch.float32
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(*tensors: torch.Tensor | None) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if t.device.type != "cuda":
+            raise RuntimeError("h3vae_b200 kernels require CUDA tensors (no CPU fallback)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError("all tensors must be on the same CUDA device")
+    if dev is None:
+        raise ValueError("no tensor given")
+    return dev
+
+
+def _require(t: torch.Tensor | None, dtype: torch.dtype, name: str, contiguous: bool = True) -> None:
+    if t is None:
+        return
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if contiguous and not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def ndhwc(x: torch.Tensor) -> torch.Tensor:
+    """Return x in channels_last_3d layout (a copy only when needed)."""
+    return x.contiguous(memory_format=torch.channels_last_3d)
+
+
+def is_ndhwc(x: torch.Tensor) -> bool:
+    return x.ndim == 5 and x.is_contiguous(memory_format=torch.channels_last_3d)
+
+
+# ---------------------------------------------------------------------------
+# Encoder
+# ---------------------------------------------------------------------------
+def conv3d_i8(qx: torch.Tensor, x_scale: torch.Tensor, qweight: torch.Tensor, weight_scale: torch.Tensor,
+              bias: torch.Tensor | None, kernel: tuple[int, int, int], stride: tuple[int, int, int] = (1, 1, 1),
+              *, causal_zero_frames: int = 0, out: torch.Tensor | None = None,
+              acc_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Valid INT8 conv3d of a padded NDHWC int8 activation (logical [B,C,D,H,W])."""
+    dev = _require_cuda(qx, x_scale, qweight, weight_scale, bias, out, acc_out)
+    if qx.ndim != 5 or qx.dtype != I8 or not is_ndhwc(qx):
+        raise ValueError("qx must be a channels_last_3d int8 [B,C,D,H,W] tensor")
+    _require(qweight, I8, "qweight")
+    _require(weight_scale, F32, "weight_scale")
+    _require(bias, F16, "bias")
+    if x_scale.dtype != F32 or x_scale.numel() != 1:
+        raise ValueError("x_scale must be one fp32 value")
+    b, c, d, h, w = qx.shape
+    kd, kh, kw = (int(k) for k in kernel)
+    sd, sh, sw = (int(s) for s in stride)
+    o = qweight.shape[0]
+    if qweight.ndim != 2 or qweight.shape[1] != kd * kh * kw * c:
+        raise ValueError(f"qweight shape {tuple(qweight.shape)} != packed {(o, kd * kh * kw * c)}")
+    if weight_scale.shape != (o,) or (bias is not None and bias.shape != (o,)):
+        raise ValueError("weight_scale / bias must be [out_channels]")
+    do, ho, wo = (d - kd) // sd + 1, (h - kh) // sh + 1, (w - kw) // sw + 1
+    if min(do, ho, wo) <= 0:
+        raise ValueError(f"input shape {tuple(qx.shape)} is too small for valid conv")
+    if out is None:
+        out = torch.empty((b, o, do, ho, wo), device=dev, dtype=F16, memory_format=torch.channels_last_3d)
+    elif out.shape != (b, o, do, ho, wo) or out.dtype != F16 or out.stride(1) != 1:
+        raise ValueError("out must be fp16 [B,O,Do,Ho,Wo] with unit channel stride")
+    if acc_out is not None and (acc_out.dtype != torch.int32 or acc_out.shape != (b, o, do, ho, wo)
+                                or not is_ndhwc(acc_out)):
+        raise ValueError("acc_out must be a channels_last_3d int32 [B,O,Do,Ho,Wo] tensor")
+    lib = _lib.load()
+    _lib.check(lib.h3b_conv3d_i8(
+        qx.data_ptr(), _lib.i64_array((b, d, h, w, c)), qweight.data_ptr(), o, kd, kh, kw, sd, sh, sw,
+        x_scale.data_ptr(), weight_scale.data_ptr(), _ptr(bias), out.data_ptr(),
+        _lib.i64_array((out.stride(0), out.stride(2), out.stride(3), out.stride(4))), _ptr(acc_out),
+        int(causal_zero_frames), _stream(dev)))
+    return out
+
+
+def quantize_tensor_i8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-tensor half-away INT8 quantization of fp16 [B,C,D,H,W] (any strides) to NDHWC int8."""
+    dev = _require_cuda(x)
+    if x.ndim != 5:
+        raise ValueError("activation must be [B,C,D,H,W]")
+    if x.dtype != F16:
+        raise ValueError("INT8 quantization requires FP16 activations")
+    if x.numel() == 0:
+        raise ValueError("INT8 activation quantization requires a nonempty tensor")
+    lib = _lib.load()
+    q = torch.empty(x.shape, device=dev, dtype=I8, memory_format=torch.channels_last_3d)
+    scale = torch.empty((), device=dev, dtype=F32)
+    ws_bytes = int(lib.h3b_quantize_tensor_workspace_size())
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    _lib.check(lib.h3b_quantize_tensor_i8(x.data_ptr(), _lib.i64_array(x.shape), _lib.i64_array(x.stride()),
+                                          q.data_ptr(), scale.data_ptr(), ws.data_ptr(), ws_bytes, _stream(dev)))
+    return q, scale
+
+
+def _norm_common(x, pre_bias, gamma, beta):
+    dev = _require_cuda(x, pre_bias, gamma, beta)
+    if x.ndim != 5 or x.dtype != F16:
+        raise ValueError("norm producer requires an FP16 rank-5 input")
+    b, c, d, h, w = x.shape
+    for name, t in (("gamma", gamma), ("beta", beta), ("pre_bias", pre_bias)):
+        if t is not None and (t.shape != (c,) or t.dtype != F16 or not t.is_contiguous()):
+            raise ValueError(f"Expected contiguous FP16 channel vectors on input device ({name})")
+    x = ndhwc(x)
+    lib = _lib.load()
+    ws_bytes = int(lib.h3b_norm_workspace_size(b, c, d, h, w))
+    if ws_bytes == 0:
+        raise ValueError(f"unsupported norm producer shape {tuple(x.shape)} (H,W >= 2; C a power of two 32..2048)")
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    return dev, x, lib, ws, ws_bytes
+
+
+def norm_pad_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float,
+                   pre_bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """GroupNorm(32)->SiLU->reflect/causal pad->per-tensor INT8 (NDHWC [B,C,D+2,H+2,W+2])."""
+    dev, x, lib, ws, ws_bytes = _norm_common(x, pre_bias, gamma, beta)
+    b, c, d, h, w = x.shape
+    q = torch.empty((b, c, d + 2, h + 2, w + 2), device=dev, dtype=I8, memory_format=torch.channels_last_3d)
+    scale = torch.empty((), device=dev, dtype=F32)
+    _lib.check(lib.h3b_norm_pad_quant(x.data_ptr(), b, c, d, h, w, _ptr(pre_bias), gamma.data_ptr(),
+                                      beta.data_ptr(), float(eps), q.data_ptr(), scale.data_ptr(), ws.data_ptr(),
+                                      ws_bytes, _stream(dev)))
+    return q, scale
+
+
+def norm_pad_f16(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float,
+                 pre_bias: torch.Tensor | None = None) -> torch.Tensor:
+    """GroupNorm(32)->SiLU->reflect/causal pad, fp16 NDHWC [B,C,D+2,H+2,W+2]."""
+    dev, x, lib, ws, ws_bytes = _norm_common(x, pre_bias, gamma, beta)
+    b, c, d, h, w = x.shape
+    y = torch.empty((b, c, d + 2, h + 2, w + 2), device=dev, dtype=F16, memory_format=torch.channels_last_3d)
+    _lib.check(lib.h3b_norm_pad_f16(x.data_ptr(), b, c, d, h, w, _ptr(pre_bias), gamma.data_ptr(),
+                                    beta.data_ptr(), float(eps), y.data_ptr(), ws.data_ptr(), ws_bytes,
+                                    _stream(dev)))
+    return y
+
+
+def residual_pack(x: torch.Tensor, residual: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
+    """fp16(r + (x + bias)), right/bottom reflect +1, two causal zero frames; NDHWC [B,C,D+2,H+1,W+1]."""
+    dev = _require_cuda(x, residual, bias)
+    if x.ndim != 5 or x.dtype != F16 or residual.shape != x.shape or residual.dtype != F16:
+        raise ValueError("Residual must match input")
+    b, c, d, h, w = x.shape
+    if bias.shape != (c,) or bias.dtype != F16 or not bias.is_contiguous():
+        raise ValueError("Expected contiguous FP16 channel bias")
+    x, residual = ndhwc(x), ndhwc(residual)
+    y = torch.empty((b, c, d + 2, h + 1, w + 1), device=dev, dtype=F16, memory_format=torch.channels_last_3d)
+    _lib.check(_lib.load().h3b_residual_pack(x.data_ptr(), residual.data_ptr(), bias.data_ptr(), b, c, d, h, w,
+                                             y.data_ptr(), _stream(dev)))
+    return y
+
+
+def finalize_pixels(x: torch.Tensor, std: torch.Tensor, mean: torch.Tensor,
+                    out: torch.Tensor | None = None) -> torch.Tensor:
+    dev = _require_cuda(x, std, mean, out)
+    if x.ndim != 5 or x.shape[1] != 3 or x.numel() == 0:
+        raise ValueError("nonempty B,3,T,H,W tensor required")
+    if x.dtype not in (F16, F32):
+        raise ValueError("FP16 or FP32 decoded pixels required")
+    for v in (std, mean):
+        if v.numel() != 3 or v.dtype != F32 or not v.is_contiguous():
+            raise ValueError("three contiguous FP32 channel constants on same device required")
+    if out is None:
+        out = torch.empty(x.shape, device=dev, dtype=F32)
+    elif out.shape != x.shape or out.dtype != F32 or not out.is_contiguous():
+        raise ValueError("contiguous FP32 output with matching shape/device required")
+    _lib.check(_lib.load().h3b_finalize_pixels(x.data_ptr(), 1 if x.dtype == F16 else 0, _lib.i64_array(x.shape),
+                                               _lib.i64_array(x.stride()), std.data_ptr(), mean.data_ptr(),
+                                               out.data_ptr(), _stream(dev)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Decoder
+# ---------------------------------------------------------------------------
+def _rows(x: torch.Tensor) -> tuple[int, int]:
+    k = x.shape[-1]
+    return x.numel() // k, k
+
+
+def gemm_i8(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, weight_scale: torch.Tensor,
+            bias: torch.Tensor | None = None, *, out: torch.Tensor | None = None,
+            acc_out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M,N] = fp16(fma(acc*scale[m], weight_scale[n], bias[n])), int8 q [M,K] x qweight [N,K]^T."""
+    dev = _require_cuda(q, scale, qweight, weight_scale, bias, out, acc_out)
+    if q.ndim != 2 or qweight.ndim != 2 or q.shape[1] != qweight.shape[1]:
+        raise ValueError("INT8 matrix dimensions/types do not match")
+    _require(q, I8, "q")
+    _require(qweight, I8, "qweight")
+    _require(scale, F32, "scale")
+    _require(weight_scale, F32, "weight_scale")
+    _require(bias, F16, "bias")
+    m, k = q.shape
+    n = qweight.shape[0]
+    if scale.numel() != m or weight_scale.numel() != n or (bias is not None and bias.numel() != n):
+        raise ValueError("one scale per activation/weight row required")
+    if out is None:
+        out = torch.empty((m, n), device=dev, dtype=F16)
+    elif out.dtype != F16 or out.shape != (m, n) or out.stride(1) != 1:
+        raise ValueError("out must be fp16 [M,N] with unit column stride")
+    if acc_out is not None and (acc_out.dtype != torch.int32 or acc_out.shape != (m, n) or not acc_out.is_contiguous()):
+        raise ValueError("acc_out must be contiguous int32 [M,N]")
+    _lib.check(_lib.load().h3b_gemm_i8(q.data_ptr(), scale.data_ptr(), qweight.data_ptr(), weight_scale.data_ptr(),
+                                       _ptr(bias), m, n, k, out.data_ptr(), out.stride(0), _ptr(acc_out),
+                                       _stream(dev)))
+    return out
+
+
+def gemm_i8_swiglu(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, weight_scale: torch.Tensor,
+                   bias: torch.Tensor | None = None) -> torch.Tensor:
+    """FFN-up INT8 GEMM with the SwiGLU epilogue: returns fp16 act [M, F] for a [2F, K] weight."""
+    dev = _require_cuda(q, scale, qweight, weight_scale, bias)
+    _require(q, I8, "q")
+    _require(qweight, I8, "qweight")
+    _require(scale, F32, "scale")
+    _require(weight_scale, F32, "weight_scale")
+    _require(bias, F16, "bias")
+    m, k = q.shape
+    n2 = qweight.shape[0]
+    if qweight.shape[1] != k or n2 % 2 or scale.numel() != m or weight_scale.numel() != n2:
+        raise ValueError("INT8 FFN-up shapes do not match")
+    if bias is not None and bias.numel() != n2:
+        raise ValueError("FP16 bias matching output channels required")
+    f = n2 // 2
+    act = torch.empty((m, f), device=dev, dtype=F16)
+    _lib.check(_lib.load().h3b_gemm_i8_swiglu(q.data_ptr(), scale.data_ptr(), qweight.data_ptr(),
+                                              weight_scale.data_ptr(), _ptr(bias), m, f, k, act.data_ptr(),
+                                              _stream(dev)))
+    return act
+
+
+def gemm_i8_qkv_rope(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, weight_scale: torch.Tensor,
+                     bias: torch.Tensor | None, batch: int, tokens: int, heads: int, cos: torch.Tensor,
+                     sin: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """INT8 QKV GEMM with fused QK RMSNorm + RoPE; returns q, k, v as fp16 [batch, heads, tokens, 64]."""
+    dev = _require_cuda(q, scale, qweight, weight_scale, bias, cos, sin)
+    _require(q, I8, "q")
+    _require(qweight, I8, "qweight")
+    _require(cos, F16, "cos")
+    _require(sin, F16, "sin")
+    m, k = q.shape
+    if m != batch * tokens or qweight.shape != (heads * 192, k):
+        raise ValueError("QKV shapes do not match [heads*192, K] per-head layout")
+    r = cos.shape[-1]
+    if cos.numel() != m * r or sin.shape != cos.shape:
+        raise ValueError("cos/sin must be [batch, tokens, 1, R]")
+    qo = torch.empty((batch, heads, tokens, 64), device=dev, dtype=F16)
+    ko = torch.empty_like(qo)
+    vo = torch.empty_like(qo)
+    _lib.check(_lib.load().h3b_gemm_i8_qkv_rope(q.data_ptr(), scale.data_ptr(), qweight.data_ptr(),
+                                                weight_scale.data_ptr(), _ptr(bias), batch, tokens, heads, k,
+                                                cos.data_ptr(), sin.data_ptr(), r, float(eps), qo.data_ptr(),
+                                                ko.data_ptr(), vo.data_ptr(), _stream(dev)))
+    return qo, ko, vo
+
+
+def row_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """CK-contract per-row INT8 quantization of fp16 [..., K] -> (q [M,K], s [M,1])."""
+    dev = _require_cuda(x)
+    _require(x, F16, "x")
+    m, k = _rows(x)
+    q = torch.empty((m, k), device=dev, dtype=I8)
+    s = torch.empty((m, 1), device=dev, dtype=F32)
+    _lib.check(_lib.load().h3b_row_quant(x.data_ptr(), m, k, k, q.data_ptr(), s.data_ptr(), _stream(dev)))
+    return q, s
+
+
+def swiglu_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(x)
+    if x.dtype != F16 or x.ndim < 2 or not x.is_contiguous():
+        raise ValueError("contiguous FP16 input with at least two dimensions required")
+    if x.shape[-1] <= 0 or x.shape[-1] % 2 or x.numel() == 0:
+        raise ValueError("nonempty [gate | up] rows of even width required")
+    k = x.shape[-1] // 2
+    m = x.numel() // (2 * k)
+    q = torch.empty((m, k), device=dev, dtype=I8)
+    s = torch.empty((m, 1), device=dev, dtype=F32)
+    _lib.check(_lib.load().h3b_swiglu_quant(x.data_ptr(), m, k, q.data_ptr(), s.data_ptr(), _stream(dev)))
+    return q, s
+
+
+def residual_rms_quant(x: torch.Tensor, a: torch.Tensor, g: torch.Tensor, w: torch.Tensor, eps: float, *,
+                       round_stats: bool = False, h_out: torch.Tensor | None = None,
+                       return_norm: bool = False):
+    """raw=fma(a,g,x); h=fp16(raw); act=fp16(h*rsqrt(mean(stat^2)+eps)*w); row quant.
+
+    Returns (h, q, s[, norm]).  Pass h_out=x for the in-place residual update.
+    """
+    dev = _require_cuda(x, a, g, w, h_out)
+    for name, t in (("x", x), ("a", a), ("g", g), ("w", w)):
+        _require(t, F16, name)
+    m, k = _rows(x)
+    if a.shape != x.shape or g.shape != (k,) or w.shape != (k,):
+        raise ValueError("residual/scale/RMS weight shape mismatch")
+    h = torch.empty_like(x) if h_out is None else h_out
+    q = torch.empty((m, k), device=dev, dtype=I8)
+    s = torch.empty((m, 1), device=dev, dtype=F32)
+    norm = torch.empty_like(x) if return_norm else None
+    _lib.check(_lib.load().h3b_residual_rms_quant(x.data_ptr(), a.data_ptr(), g.data_ptr(), w.data_ptr(), m, k,
+                                                  float(eps), 1 if round_stats else 0, h.data_ptr(), q.data_ptr(),
+                                                  s.data_ptr(), _ptr(norm), _stream(dev)))
+    return (h, q, s, norm) if return_norm else (h, q, s)
+
+
+def rms_norm_f16(x: torch.Tensor, gamma: torch.Tensor, eps: float) -> torch.Tensor:
+    dev = _require_cuda(x, gamma)
+    _require(x, F16, "x")
+    _require(gamma, F16, "gamma")
+    m, k = _rows(x)
+    y = torch.empty_like(x, memory_format=torch.contiguous_format)
+    _lib.check(_lib.load().h3b_rms_norm_f16(x.data_ptr(), gamma.data_ptr(), m, k, float(eps), y.data_ptr(),
+                                            _stream(dev)))
+    return y
+
+
+def rms_quant(x: torch.Tensor, gamma: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(x, gamma)
+    _require(x, F16, "x")
+    _require(gamma, F16, "gamma")
+    m, k = _rows(x)
+    q = torch.empty((m, k), device=dev, dtype=I8)
+    s = torch.empty((m, 1), device=dev, dtype=F32)
+    _lib.check(_lib.load().h3b_rms_quant(x.data_ptr(), gamma.data_ptr(), m, k, float(eps), q.data_ptr(),
+                                         s.data_ptr(), _stream(dev)))
+    return q, s
+
+
+def final_residual_layernorm(h: torch.Tensor, o: torch.Tensor, gate: torch.Tensor, gamma: torch.Tensor,
+                             beta: torch.Tensor, eps: float) -> torch.Tensor:
+    dev = _require_cuda(h, o, gate, gamma, beta)
+    for name, t in (("h", h), ("o", o), ("gate", gate), ("gamma", gamma), ("beta", beta)):
+        _require(t, F16, name)
+    m, k = _rows(h)
+    if o.shape != h.shape or any(v.shape != (k,) for v in (gate, gamma, beta)):
+        raise ValueError("expected matching H/O and width-K vectors")
+    y = torch.empty_like(h, memory_format=torch.contiguous_format)
+    _lib.check(_lib.load().h3b_final_residual_layernorm(h.data_ptr(), o.data_ptr(), gate.data_ptr(),
+                                                        gamma.data_ptr(), beta.data_ptr(), m, k, float(eps),
+                                                        y.data_ptr(), _stream(dev)))
+    return y
+
+
+def qk_rope(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, heads: int,
+            eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+    dev = _require_cuda(qkv, cos, sin)
+    _require(qkv, F16, "qkv")
+    _require(cos, F16, "cos")
+    _require(sin, F16, "sin")
+    b, n, width = qkv.shape
+    if width != heads * 192:
+        raise ValueError("qkv width must be heads * 3 * 64")
+    r = cos.shape[-1]
+    if cos.shape != (b, n, 1, r) or sin.shape != cos.shape:
+        raise ValueError("cos/sin must be [b, n, 1, R]")
+    q = torch.empty((b, n, heads, 64), device=dev, dtype=F16)
+    k = torch.empty_like(q)
+    _lib.check(_lib.load().h3b_qk_rope(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), b, n, heads, r, float(eps),
+                                       q.data_ptr(), k.data_ptr(), _stream(dev)))
+    return q, k
+
+
+def attention_f16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+    """softmax(q k^T * scale) v for [B, H, S, 64] views (any batch/head/token strides, unit dim stride).
+
+    The result is written to `out` (default: a new [B, S, H, 64] fp16 tensor, returned as the
+    [B, H, S, 64] view of it).
+    """
+    dev = _require_cuda(q, k, v, out)
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        if t.dtype != F16 or t.ndim != 4 or t.shape[-1] != 64 or t.stride(-1) != 1:
+            raise ValueError(f"{name} must be fp16 [B,H,S,64] with unit dim stride")
+    bsz, heads, sq, _ = q.shape
+    skv = k.shape[2]
+    if k.shape != (bsz, heads, skv, 64) or v.shape != k.shape:
+        raise ValueError("k/v shape mismatch")
+    if out is None:
+        out = torch.empty((bsz, sq, heads, 64), device=dev, dtype=F16).transpose(1, 2)
+    strides = lambda t: _lib.i64_array((t.stride(0), t.stride(1), t.stride(2)))  # noqa: E731
+    _lib.check(_lib.load().h3b_attention_f16(q.data_ptr(), strides(q), k.data_ptr(), strides(k), v.data_ptr(),
+                                             strides(v), out.data_ptr(), strides(out), bsz, heads, sq, skv,
+                                             float(scale), _stream(dev)))
+    return out

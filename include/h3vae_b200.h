@@ -1,0 +1,212 @@
+/*
+ * h3vae_b200.h -- C ABI of the B200-native H3 video-VAE INT8 encode/decode path.
+ *
+ * Every entry point takes raw device pointers, int64 sizes, an explicit CUDA
+ * stream, and returns 0 on success or a negative H3B_E* status (the message is
+ * available from h3b_last_error()).  No entry point allocates device memory:
+ * producers that need scratch take a caller-provided workspace whose size is
+ * reported by the matching *_workspace_size query.  No C++ exception crosses
+ * this boundary.  Tensors are dense unless a stride argument says otherwise;
+ * "NDHWC" means PyTorch's channels_last_3d layout of a logical [B,C,D,H,W].
+ *
+ * Citations "ref: file:line" point into fishelegs/ComfyUI-H3VAE-PyOpt 0.2.0,
+ * the interface each function replaces.
+ */
+#ifndef H3VAE_B200_H_
+#define H3VAE_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
+
+enum {
+  H3B_OK = 0,
+  H3B_EINVAL = -1,      /* bad pointer / shape / stride / dtype contract  */
+  H3B_EUNSUPPORTED = -2, /* geometry outside the implemented contract     */
+  H3B_ECUDA = -3,       /* CUDA runtime or driver error                    */
+  H3B_EDEVICE = -4      /* device-side error word set (bounded wait expired) */
+};
+
+/* ---- library / error plumbing ------------------------------------------ */
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char* h3b_last_error(void);
+
+/* ABI version (major*100 + minor). */
+int h3b_abi_version(void);
+
+/* Reads (and with clear!=0 resets) the device error word of the current
+ * device.  Synchronizes the device.  *bits==0 means no kernel reported a
+ * timeout or invariant failure. */
+int h3b_device_error(unsigned int* bits, int clear);
+
+/* ---- (a4) INT8 implicit-GEMM 3-D convolution ---------------------------- */
+
+/* Valid (unpadded) 3-D convolution of an already padded, already quantized
+ * NDHWC int8 activation with packed int8 weights, int32 accumulation on the
+ * tcgen05 tensor cores (TMEM accumulators), and the dequantizing epilogue
+ *   out = fp16( fma(acc * x_scale, w_scale[n], bias[n]) )   (bias optional)
+ * written to an NDHWC fp16 tensor with caller strides (channel stride 1).
+ *   qx        int8  [B, D, H, W, C] contiguous (x_dims = {B, D, H, W, C})
+ *   qw        int8  [O, kd*kh*kw*C], tap-major / channel-minor packing
+ *   x_scale   fp32 scalar (per-tensor activation scale, device pointer)
+ *   w_scale   fp32 [O];  bias fp16 [O] or NULL
+ *   out       fp16, element strides out_strides = {sB, sD, sH, sW}
+ *   acc_out   optional int32 [B, Do, Ho, Wo, O] contiguous raw accumulators
+ *   causal_zero_frames: 2 when the producer guarantees that input frames 0
+ *     and 1 are exact zeros (the causal pad); the kernel then skips the
+ *     temporal taps that only read them.  0 = full reduction.
+ * ref: opt/encoder_int8.py:509-588 (_conv3d_from_quantized),
+ *      opt/encoder_int8_pipeline.py:16-121 (SKIP_CAUSAL_ZEROS kernel) */
+int h3b_conv3d_i8(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int64_t out_channels,
+                  int kd, int kh, int kw, int sd, int sh, int sw, const float* x_scale,
+                  const float* w_scale, const void* bias, void* out, const int64_t* out_strides,
+                  int32_t* acc_out, int causal_zero_frames, h3b_stream_t stream);
+
+/* ---- (a2) per-tensor activation quantization ---------------------------- */
+
+/* scale = max|x| * fp32(1/127) (0 -> 1);  q = clamp(half_away(x / scale), +-127)
+ * x: fp16 logical [B,C,D,H,W] with element strides; q: int8 NDHWC contiguous.
+ * workspace >= h3b_quantize_tensor_workspace_size() bytes.
+ * ref: opt/encoder_int8.py:384-426 (quantize_activation_tensor) */
+size_t h3b_quantize_tensor_workspace_size(void);
+int h3b_quantize_tensor_i8(const void* x, const int64_t* dims5, const int64_t* strides5, int8_t* q,
+                           float* scale, void* workspace, size_t workspace_bytes, h3b_stream_t stream);
+
+/* ---- (a3) GroupNorm(32) + SiLU + reflect/causal pad producers ----------- */
+
+/* Workspace for the per-frame GroupNorm statistics of x [B,C,D,H,W]. */
+size_t h3b_norm_workspace_size(int64_t B, int64_t C, int64_t D, int64_t H, int64_t W);
+
+/* INT8 producer.  x: fp16 NDHWC [B,D,H,W,C].  Optional pre_bias (fp16 [C])
+ * is added and rounded to fp16 first.  Per (b, frame, group) statistics;
+ * z = fp16(((v-mean)*rstd)*gamma+beta); s = fp16(silu(z)); reflect pad 1 in
+ * H and W, two zero frames in front; per-tensor scale = max|s| * fp32(1/127);
+ * q = half_away(s/scale).  Output q: int8 NDHWC [B, D+2, H+2, W+2, C].
+ * ref: opt/encoder_int8_norm.py:77-110 (quantized_temporal_norm_pad),
+ *      opt/encoder_int8_norm_recompute.py:11-49, opt/encoder_fused_temporal_norm.py:13-51 */
+int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
+                       const void* pre_bias, const void* gamma, const void* beta, float eps, int8_t* q,
+                       float* scale, void* workspace, size_t workspace_bytes, h3b_stream_t stream);
+
+/* FP16 producer with the same arithmetic, writing y: fp16 NDHWC
+ * [B, D+2, H+2, W+2, C] (padded) for the fp16 convolutions.
+ * ref: opt/encoder_fused_temporal_norm.py:54-80 (temporal_norm_pack),
+ *      opt/encoder_fused_norm_bias.py:43-99 (bias_temporal_norm_pack),
+ *      opt/encoder_fused_batched_norm.py:16-73 (batched_temporal_norm_pack) */
+int h3b_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
+                     const void* pre_bias, const void* gamma, const void* beta, float eps, void* y,
+                     void* workspace, size_t workspace_bytes, h3b_stream_t stream);
+
+/* ---- (a6) residual + bias + downsample pad pack ------------------------- */
+
+/* y = fp16(r + (x + bias)) computed in fp32; right/bottom reflect pad +1,
+ * two zero frames in front.  x, r: fp16 NDHWC [B,D,H,W,C]; y: fp16 NDHWC
+ * [B, D+2, H+1, W+1, C].
+ * ref: opt/encoder_fused_residual_pack.py:13-50 (residual_downsample_pack) */
+int h3b_residual_pack(const void* x, const void* r, const void* bias, int64_t B, int64_t C, int64_t D,
+                      int64_t H, int64_t W, void* y, h3b_stream_t stream);
+
+/* ---- (a9) INT8 GEMM family (decoder linears) ----------------------------- */
+
+/* out[m, n] = fp16( fma(acc[m,n] * a_scale[m], w_scale[n], bias[n]) )
+ * qa int8 [M,K] (row stride K), qw int8 [N,K], a_scale fp32 [M], w_scale fp32
+ * [N], bias fp16 [N] or NULL, out fp16 with row stride ldo.  K % 16 == 0.
+ * acc_out: optional int32 [M,N] raw accumulators.
+ * ref: opt/int8_swiglu_fused.py:78-107 (prequantized_linear, the CK
+ *      cutlass_int8_dequant contract restated at opt/int8_ffn_up_fused.py:78-84) */
+int h3b_gemm_i8(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale,
+                const void* bias, int64_t M, int64_t N, int64_t K, void* out, int64_t ldo,
+                int32_t* acc_out, h3b_stream_t stream);
+
+/* FFN-up GEMM with the SwiGLU epilogue.  qw is the unmodified [2F, K] weight
+ * (rows 0..F-1 gate, F..2F-1 up); per column j:
+ *   g = fp16(fma(acc_g*s, ws[j], b[j])), u = fp16(fma(acc_u*s, ws[F+j], b[F+j]))
+ *   act[m, j] = fp16( g / (1 + exp(-g)) * u )
+ * ref: opt/int8_ffn_up_fused.py:51-90 (up_swiglu) */
+int h3b_gemm_i8_swiglu(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale,
+                       const void* bias, int64_t M, int64_t F, int64_t K, void* act, h3b_stream_t stream);
+
+/* QKV GEMM with the fused per-head QK RMSNorm + rotary epilogue.  qw rows are
+ * laid out per head as [q(64) | k(64) | v(64)] (N = heads*192).  For each
+ * token m = b*tokens + t and head h:
+ *   qkv = fp16(fma(acc*s, ws, bias));  q' = fp16(q * rsqrt(mean(q^2) + eps))
+ *   q_out[d] = fp16(q'[d]*cos[d]) + fp16(rot(q')[d]*sin[d]) for d < R, q'[d] after
+ * (same for k), v passes through.  cos/sin: fp16 [M, R].  q/k/v outputs are
+ * fp16 [batch, heads, tokens, 64].
+ * ref: opt/decoder_fused_qk_rope.py:13-54 (_qk_rope / qk_rope) fused behind
+ *      opt/int8_qkv.py:33-41 (INT8 to_qkv) */
+int h3b_gemm_i8_qkv_rope(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale,
+                         const void* bias, int64_t batch, int64_t tokens, int64_t heads, int64_t K,
+                         const void* cos_t, const void* sin_t, int64_t rot_dims, float eps, void* q_out,
+                         void* k_out, void* v_out, h3b_stream_t stream);
+
+/* ---- (a12/a13) decoder row producers ------------------------------------ */
+
+/* Row quantization (CK contract): s = max(amax*fp32(1/127), 1e-30),
+ * q = clamp(rint(fp16(x / fp16(s))), -128, 127), NaN -> -128.
+ * x fp16 [M,K] row stride ldx.  ref: opt/int8_ffn_up_fused.py:92-105 */
+int h3b_row_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int8_t* q, float* s, h3b_stream_t stream);
+
+/* SwiGLU of [gate | up] rows then row quantization.
+ * ref: opt/int8_swiglu_fused.py:22-66 (quantize_swiglu) */
+int h3b_swiglu_quant(const void* x, int64_t M, int64_t K, int8_t* q, float* s, h3b_stream_t stream);
+
+/* raw = fma(a, g, x); h = fp16(raw); inv = rsqrt(mean(stat^2) + eps) with
+ * stat = round_stats ? h : raw; act = fp16(h*inv*w); row quantization of act.
+ * h may alias x (in-place residual).  norm_out (fp16 act) is optional.
+ * ref: opt/int8_norm_quant.py:23-70 (residual_quant),
+ *      opt/int8_norm1_producer.py:29-61 (residual_norm_quant) */
+int h3b_residual_rms_quant(const void* x, const void* a, const void* g, const void* w, int64_t M, int64_t K,
+                           float eps, int round_stats, void* h, int8_t* q, float* s, void* norm_out,
+                           h3b_stream_t stream);
+
+/* y = fp16(x * rsqrt(mean(x^2) + eps) * gamma).  ref: opt/decoder_block0_norm.py:39-59 */
+int h3b_rms_norm_f16(const void* x, const void* gamma, int64_t M, int64_t K, float eps, void* y,
+                     h3b_stream_t stream);
+
+/* RMSNorm followed by row quantization (block-0 norm1 feeding the INT8 QKV).
+ * ref: opt/decoder_block0_norm.py:39-59 then opt/kitchen_int8.py:20-37 */
+int h3b_rms_quant(const void* x, const void* gamma, int64_t M, int64_t K, float eps, int8_t* q, float* s,
+                  h3b_stream_t stream);
+
+/* raw = fma(o, gate, h); LayerNorm(raw) over K; y = fp16(fma(n, gamma, beta)).
+ * ref: opt/decoder_final_norm.py:35-72 (final_residual_ln_w8) */
+int h3b_final_residual_layernorm(const void* h, const void* o, const void* gate, const void* gamma,
+                                 const void* beta, int64_t M, int64_t K, float eps, void* y,
+                                 h3b_stream_t stream);
+
+/* Standalone QK RMSNorm + rotary on a [b, n, 3*H*D] qkv tensor (D = 64),
+ * writing q, k as fp16 [b, n, H, D].  ref: opt/decoder_fused_qk_rope.py:13-54 */
+int h3b_qk_rope(const void* qkv, const void* cos_t, const void* sin_t, int64_t batch, int64_t tokens,
+                int64_t heads, int64_t rot_dims, float eps, void* q_out, void* k_out, h3b_stream_t stream);
+
+/* ---- (a11) attention ----------------------------------------------------- */
+
+/* Non-causal softmax(q k^T * scale) v, fp16 in/out, fp32 softmax, head dim 64.
+ * q/k/v: fp16 with element strides {batch, head, token} (dim stride 1);
+ * out: fp16 with element strides {batch, head, token}.
+ * ref: opt/decoder_fused_qk_rope.py:73 (perform_attention -> PyTorch SDPA) */
+int h3b_attention_f16(const void* q, const int64_t* q_strides, const void* k, const int64_t* k_strides,
+                      const void* v, const int64_t* v_strides, void* out, const int64_t* out_strides,
+                      int64_t batch, int64_t heads, int64_t q_len, int64_t kv_len, float scale,
+                      h3b_stream_t stream);
+
+/* ---- (a15) pixel finalization ------------------------------------------- */
+
+/* out = clamp(x*std[c] + mean[c], 0, 1) in fp32 without FMA, NaN preserved.
+ * x: fp16 (x_is_fp16=1) or fp32 logical [B,3,T,H,W] with element strides;
+ * out: fp32 contiguous.  ref: opt/fp16_finalize.py:24-54 (finalize_pixels) */
+int h3b_finalize_pixels(const void* x, int x_is_fp16, const int64_t* dims5, const int64_t* strides5,
+                        const float* std3, const float* mean3, float* out, h3b_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3VAE_B200_H_ */

@@ -1,0 +1,435 @@
+"""CPU oracle for the H3 video-VAE INT8 encode/decode hot path.
+
+TEST INFRASTRUCTURE ONLY.  This module is a CPU restatement (numpy + CPU
+PyTorch, float64 where an exact integer result is needed) of the reference
+algorithm of fishelegs/ComfyUI-H3VAE-PyOpt 0.2.0.  Only the tests, the smoke
+check of __graft_entry__ and bench.py's CPU-baseline leg may import it; the
+product path never does (its kernels live in libh3vae_b200.so and fail loudly
+when that library is missing).
+
+Every function names the reference file:line it follows.  fp16 rounding
+points are reproduced with numpy float16 casts (round-to-nearest-even, the
+same rule as CUDA's __float2half_rn); fp32 arithmetic is done in numpy
+float32, one IEEE rounding per operation, in the reference's order.
+Integer accumulators are exact (float64 convolution/matmul of int8 values:
+|sum| < 2^31 << 2^53).
+
+Pinning: tests/test_oracle_golden.py checks this module against vectors the
+reference's own CPU functions produced (tests/golden/make_golden.py) and
+against the known-answer vectors in the reference's tests.
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+F16 = np.float16
+F32 = np.float32
+RECIP_127 = F32(1.0) / F32(127.0)  # fp32-rounded reciprocal, as the CUDA path uses
+
+
+def f16(x) -> np.ndarray:
+    """Round to fp16 and back to fp32 (one fp16 rounding point)."""
+    return np.asarray(x, dtype=F32).astype(F16).astype(F32)
+
+
+def fma32(a, b, c) -> np.ndarray:
+    """fp32 fused multiply-add: the fp32 product is exact in float64, one final rounding to fp32
+    (float64 sum rounding first; differs from a true fma only in rare double-rounding ties)."""
+    return (np.asarray(a, np.float64) * np.asarray(b, np.float64) + np.asarray(c, np.float64)).astype(F32)
+
+
+# ---------------------------------------------------------------------------
+# (a1) weight packing / quantization
+# ---------------------------------------------------------------------------
+def int32_accumulator_bound(in_channels: int, kernel_size) -> int:
+    """ref: opt/encoder_int8.py:54-58."""
+    return in_channels * math.prod(kernel_size) * 127 * 127
+
+
+def prepare_int8_weight(weight: torch.Tensor):
+    """Pack [O,C,kd,kh,kw] -> [O, kd*kh*kw*C] (tap-major, channel-minor) and quantize per output
+    channel: scale = amax / 127 (0 -> 1), q = round_half_even(w / scale) clamped to +-127.
+    Evaluated with the same torch expression on the weight's own device.
+    ref: opt/encoder_int8.py:303-327."""
+    if weight.ndim != 5 or weight.numel() == 0:
+        raise ValueError("weight must be a non-empty [O,C,kd,kh,kw] tensor")
+    source = weight.detach().float().contiguous()
+    o = source.shape[0]
+    packed = source.permute(0, 2, 3, 4, 1).reshape(o, -1)
+    scale = packed.abs().amax(dim=1).div(127.0)
+    scale = torch.where(scale > 0, scale, torch.ones_like(scale))
+    q = torch.round(packed / scale[:, None]).clamp(-127, 127).to(torch.int8)
+    return q.contiguous(), scale.float().contiguous()
+
+
+def quantize_rowwise_weight(weight: torch.Tensor):
+    """Static per-output-row INT8 weight quantization with the semantics the reference pins for
+    comfy-kitchen 0.2.34's quantize_int8_rowwise: scale = max(amax / 127, 1e-30), q = round, clamp
+    [-128, 127]; an all-zero row is normalized to q = 0, scale = 1.
+    ref: tests/test_kitchen_int8.py:19-26 (fake CK quantizer), opt/kitchen_int8.py:131-145."""
+    w = weight.detach().float()
+    scale = (w.abs().amax(dim=-1, keepdim=True) / 127.0).clamp(min=1e-30)
+    q = (w / scale).round().clamp(-128, 127).to(torch.int8)
+    scale = scale.reshape(-1).contiguous()
+    zero = torch.all(w == 0, dim=1)
+    if bool(zero.any()):
+        q = q.clone()
+        scale = scale.clone()
+        q[zero] = 0
+        scale[zero] = 1.0
+    return q.contiguous(), scale
+
+
+# ---------------------------------------------------------------------------
+# (a2) per-tensor activation quantization
+# ---------------------------------------------------------------------------
+def tensor_scale(absmax: float, *, true_division: bool = False) -> np.float32:
+    """scale = absmax * fp32(1/127) (the CUDA kernels; ref: opt/encoder_int8.py:356-364) or the true
+    fp32 division of the CPU reference (ref: opt/encoder_int8.py:601-602); 0 -> 1."""
+    a = F32(absmax)
+    s = (a / F32(127.0)) if true_division else (a * RECIP_127)
+    s = F32(s)
+    return s if s > 0 else F32(1.0)
+
+
+def quant_half_away(x, scale) -> np.ndarray:
+    """q = clamp(half_away(x / scale), +-127) with fp32 ops in the kernel's order.
+    ref: opt/encoder_int8.py:367-378 (also :147-154 and the CPU oracle :603-609)."""
+    s = np.asarray(x, F32) / F32(scale)
+    r = np.where(s >= 0, np.floor(s + F32(0.5)), -np.floor(-s + F32(0.5)))
+    return np.clip(r, -127, 127).astype(np.int8)
+
+
+def quantize_activation_tensor(x: np.ndarray, *, true_division: bool = False):
+    """fp16 [B,C,D,H,W] -> (int8 [B,C,D,H,W], fp32 scale).  ref: opt/encoder_int8.py:384-426."""
+    xf = np.asarray(x).astype(F32)
+    if xf.size == 0:
+        raise ValueError("INT8 activation quantization requires a nonempty tensor")
+    scale = tensor_scale(np.fmax.reduce(np.abs(xf), axis=None), true_division=true_division)
+    return quant_half_away(xf, scale), scale
+
+
+# ---------------------------------------------------------------------------
+# (a4) valid implicit-GEMM conv3d: exact int32 accumulators + epilogue
+# ---------------------------------------------------------------------------
+def unpack_weight(qweight: np.ndarray, in_channels: int, kernel) -> np.ndarray:
+    """[O, kd*kh*kw*C] -> [O, C, kd, kh, kw].  ref: opt/encoder_int8.py:611-618."""
+    kd, kh, kw = kernel
+    o = qweight.shape[0]
+    return np.asarray(qweight).reshape(o, kd, kh, kw, in_channels).transpose(0, 4, 1, 2, 3)
+
+
+def conv3d_int_acc(qx: np.ndarray, qweight: np.ndarray, kernel, stride=(1, 1, 1)) -> np.ndarray:
+    """Exact int32 accumulators of the valid conv (logical [B,C,D,H,W] int8 input).
+    ref: opt/encoder_int8_pipeline.py:83-100 (the reduction), opt/encoder_int8.py:210-249."""
+    c = qx.shape[1]
+    w = unpack_weight(qweight, c, kernel)
+    acc = F.conv3d(torch.from_numpy(np.asarray(qx, np.float64)), torch.from_numpy(w.astype(np.float64)),
+                   stride=tuple(stride))
+    out = acc.numpy()
+    assert np.all(np.abs(out) < 2**31)
+    return np.rint(out).astype(np.int32)
+
+
+def conv_epilogue(acc: np.ndarray, x_scale, w_scale: np.ndarray, bias: np.ndarray | None,
+                  channel_axis: int = 1) -> np.ndarray:
+    """fp16(fma(acc * x_scale, w_scale[n], bias[n])) or fp16((acc * x_scale) * w_scale[n]).
+    ref: opt/encoder_int8_pipeline.py:101-106 (Triton contracts the bias add into an fma)."""
+    shape = [1] * acc.ndim
+    shape[channel_axis] = -1
+    v = acc.astype(F32) * np.asarray(x_scale, F32)
+    ws = np.asarray(w_scale, F32).reshape(shape)
+    if bias is None:
+        out = v * ws
+    else:
+        out = fma32(v, ws, f16(bias).reshape(shape))
+    return out.astype(F16)
+
+
+def int8_valid_conv3d(x: np.ndarray, qweight: np.ndarray, w_scale: np.ndarray, kernel, stride=(1, 1, 1),
+                      bias=None, *, true_division: bool = False) -> np.ndarray:
+    """Quantize (per tensor) + conv + epilogue, fp16 [B,O,Do,Ho,Wo].  ref: opt/encoder_int8.py:454-506."""
+    qx, sx = quantize_activation_tensor(x, true_division=true_division)
+    acc = conv3d_int_acc(qx, qweight, kernel, stride)
+    return conv_epilogue(acc, sx, w_scale, bias)
+
+
+def int8_valid_conv3d_dequant_fp32(x: np.ndarray, weight: torch.Tensor, bias=None, stride=(1, 1, 1)) -> np.ndarray:
+    """fp32 output of dequantized operands (conv of deq_x with deq_w, + bias), the arithmetic of the
+    reference's CPU oracle.  ref: opt/encoder_int8.py:591-619."""
+    qw, ws = prepare_int8_weight(weight)
+    c = x.shape[1]
+    kernel = tuple(weight.shape[-3:])
+    qx, sx = quantize_activation_tensor(x, true_division=True)
+    deq_x = torch.from_numpy(qx.astype(F32)) * torch.tensor(sx)
+    packed = qw.float() * ws[:, None]
+    unpacked = packed.reshape(qw.shape[0], *kernel, c).permute(0, 4, 1, 2, 3)
+    b = None if bias is None else torch.as_tensor(bias).float()
+    return F.conv3d(deq_x, unpacked, b, stride=tuple(stride), padding=0).numpy()
+
+
+# ---------------------------------------------------------------------------
+# (a3) GroupNorm(32) + SiLU + reflect/causal pad producer
+# ---------------------------------------------------------------------------
+def gn_stats(x: np.ndarray, eps: float, pre_bias=None, groups: int = 32):
+    """Per (b, frame, group) mean and rstd = rsqrt(max(var,0)+eps) of fp16 [B,C,D,H,W]
+    (after the optional fp16(x + pre_bias)).  Statistics in float64 (the reference's chunked
+    Chan merge is a summation-order choice; it differs from exact by O(1e-7) relative).
+    ref: opt/encoder_fused_temporal_norm.py:13-51, opt/encoder_fused_norm_bias.py:15-40."""
+    v = np.asarray(x).astype(F32)
+    if pre_bias is not None:
+        v = f16(v + np.asarray(pre_bias, F32).reshape(1, -1, 1, 1, 1))
+    b, c, d, h, w = v.shape
+    g = v.reshape(b, groups, c // groups, d, h, w).transpose(0, 3, 1, 2, 4, 5).reshape(b, d, groups, -1)
+    g64 = g.astype(np.float64)
+    mean = g64.mean(axis=-1)
+    var = g64.var(axis=-1)
+    rstd = 1.0 / np.sqrt(np.maximum(var, 0.0) + eps)
+    return mean.astype(F32), rstd.astype(F32), v
+
+
+def silu_f32(z: np.ndarray) -> np.ndarray:
+    """z / (1 + exp(-z)) in fp32.  ref: opt/encoder_int8_norm_recompute.py:38."""
+    z = np.asarray(z, F32)
+    with np.errstate(over="ignore"):
+        return z / (F32(1.0) + np.exp(-z))
+
+
+def norm_silu(x: np.ndarray, gamma, beta, eps: float, pre_bias=None, groups: int = 32) -> np.ndarray:
+    """Unpadded fp16 GroupNorm -> fp16 -> SiLU -> fp16, [B,C,D,H,W] (fp32 values of fp16 numbers).
+    ref: opt/encoder_int8_norm_recompute.py:27-39, opt/encoder_fused_temporal_norm.py:54-56."""
+    mean, rstd, v = gn_stats(x, eps, pre_bias, groups)
+    b, c, d, h, w = v.shape
+    cg = c // groups
+    mean_c = np.repeat(mean, cg, axis=2).transpose(0, 2, 1)[..., None, None]  # [B,C,D,1,1]
+    rstd_c = np.repeat(rstd, cg, axis=2).transpose(0, 2, 1)[..., None, None]
+    gm = f16(gamma).reshape(1, -1, 1, 1, 1)
+    bt = f16(beta).reshape(1, -1, 1, 1, 1)
+    z = f16(((v - mean_c) * rstd_c) * gm + bt)
+    return f16(silu_f32(z))
+
+
+def pad_reflect_causal(z: np.ndarray) -> np.ndarray:
+    """Reflect pad 1 in H and W, two zero frames in front: [B,C,D+2,H+2,W+2].
+    ref: opt/encoder_int8_norm_recompute.py:25-31, opt/encoder_int8.py:622-650."""
+    zp = np.pad(z, ((0, 0), (0, 0), (0, 0), (1, 1), (1, 1)), mode="reflect")
+    return np.pad(zp, ((0, 0), (0, 0), (2, 0), (0, 0), (0, 0)))
+
+
+def norm_pad_f16(x, gamma, beta, eps, pre_bias=None) -> np.ndarray:
+    """ref: opt/encoder_fused_temporal_norm.py:54-80 / opt/encoder_fused_norm_bias.py:43-72."""
+    return pad_reflect_causal(norm_silu(x, gamma, beta, eps, pre_bias)).astype(F16)
+
+
+def norm_pad_quant(x, gamma, beta, eps, pre_bias=None):
+    """INT8 producer: per-tensor scale of the padded fp16 values, half-away quantization.
+    ref: opt/encoder_int8_norm.py:198-231, opt/encoder_int8_norm_recompute.py:40-49."""
+    y = pad_reflect_causal(norm_silu(x, gamma, beta, eps, pre_bias))
+    scale = tensor_scale(np.abs(y).max())
+    return quant_half_away(y, scale), scale
+
+
+# ---------------------------------------------------------------------------
+# (a6) residual + bias + downsample pad pack
+# ---------------------------------------------------------------------------
+def residual_pack(x, r, bias) -> np.ndarray:
+    """fp16(r + (x + bias)) in fp32; right/bottom reflect +1; two zero frames.
+    ref: opt/encoder_fused_residual_pack.py:13-32."""
+    xf = np.asarray(x).astype(F32)
+    rf = np.asarray(r).astype(F32)
+    y = rf + (xf + f16(bias).reshape(1, -1, 1, 1, 1))
+    b, c, d, h, w = xf.shape
+    out = np.zeros((b, c, d + 2, h + 1, w + 1), F32)
+    out[:, :, 2:, :h, :w] = y
+    out[:, :, 2:, h, :w] = y[:, :, :, h - 2, :]
+    out[:, :, 2:, :h, w] = y[:, :, :, :, w - 2]
+    out[:, :, 2:, h, w] = y[:, :, :, h - 2, w - 2]
+    return out.astype(F16)
+
+
+# ---------------------------------------------------------------------------
+# (a9, a12, a13) decoder row producers and INT8 linears (CK contract)
+# ---------------------------------------------------------------------------
+def row_quant_ck(act: np.ndarray):
+    """s = max(amax * fp32(1/127), 1e-30); q = clamp(rint(fp16(act / fp16(s))), -128, 127), NaN->-128.
+    ref: opt/int8_swiglu_fused.py:28-38, opt/int8_ffn_up_fused.py:92-105, opt/int8_norm_quant.py:31-44."""
+    a = np.asarray(act, F32)
+    # max / maximum drop NaN operands like the kernels' fmaxf reductions
+    amax = np.fmax.reduce(np.abs(a), axis=-1, keepdims=True).astype(F32)
+    scale = np.fmax(amax * RECIP_127, F32(1e-30)).astype(F32)
+    with np.errstate(over="ignore", divide="ignore", invalid="ignore"):
+        denom = f16(scale)
+        v = f16(a / denom)
+    v = np.rint(v)
+    v = np.where(np.isnan(v), F32(-128), v)
+    return np.clip(v, -128, 127).astype(np.int8), scale.astype(F32)
+
+
+def linear_acc(q: np.ndarray, qweight: np.ndarray) -> np.ndarray:
+    """Exact int32 q[M,K] @ qweight[N,K]^T."""
+    acc = np.asarray(q, np.float64) @ np.asarray(qweight, np.float64).T
+    assert np.all(np.abs(acc) < 2**31)
+    return np.rint(acc).astype(np.int32)
+
+
+def linear_epilogue(acc: np.ndarray, a_scale: np.ndarray, w_scale: np.ndarray, bias=None) -> np.ndarray:
+    """fp16(fma(acc * sx[m], sw[n], b[n])) / fp16((acc * sx[m]) * sw[n]).
+    ref: opt/int8_ffn_up_fused.py:76-84 (restating the CK cutlass_int8_dequant contract)."""
+    v = acc.astype(F32) * np.asarray(a_scale, F32).reshape(-1, 1)
+    ws = np.asarray(w_scale, F32).reshape(1, -1)
+    if bias is None:
+        return (v * ws).astype(F16)
+    return fma32(v, ws, f16(bias).reshape(1, -1)).astype(F16)
+
+
+def prequantized_linear(q, s, qweight, w_scale, bias=None) -> np.ndarray:
+    """ref: opt/int8_swiglu_fused.py:78-107."""
+    return linear_epilogue(linear_acc(q, qweight), s, w_scale, bias)
+
+
+def int8_linear(x: np.ndarray, qweight, w_scale, bias=None) -> np.ndarray:
+    """Dynamic per-row activation quantization + INT8 GEMM.  ref: opt/kitchen_int8.py:20-37."""
+    q, s = row_quant_ck(np.asarray(x).astype(F32).reshape(-1, x.shape[-1]))
+    return prequantized_linear(q, s, qweight, w_scale, bias).reshape(*x.shape[:-1], -1)
+
+
+def swiglu_act(gate: np.ndarray, up: np.ndarray) -> np.ndarray:
+    """fp16(silu(gate) * up) with no intermediate rounding of silu.  ref: opt/int8_swiglu_fused.py:27."""
+    g = np.asarray(gate, F32)
+    with np.errstate(over="ignore"):
+        return f16((g / (F32(1.0) + np.exp(-g))) * np.asarray(up, F32))
+
+
+def quantize_swiglu(x: np.ndarray):
+    """ref: opt/int8_swiglu_fused.py:22-66."""
+    xf = np.asarray(x).astype(F32)
+    k = xf.shape[-1] // 2
+    act = swiglu_act(xf[..., :k], xf[..., k:]).reshape(-1, k)
+    return row_quant_ck(act)
+
+
+def ffn_up_swiglu(q, s, qweight, w_scale, bias=None) -> np.ndarray:
+    """INT8 FFN-up with paired gate/up columns (rows 0..F-1 gate, F..2F-1 up), fp16 rounding of each
+    linear value, then SwiGLU.  ref: opt/int8_ffn_up_fused.py:51-90."""
+    lin = prequantized_linear(q, s, qweight, w_scale, bias).astype(F32)
+    f = lin.shape[1] // 2
+    return swiglu_act(lin[:, :f], lin[:, f:]).astype(F16)
+
+
+def residual_rms_quant(x, a, g, w, eps, round_stats=False):
+    """raw = fma(a,g,x); h = fp16(raw); inv = rsqrt(sum(stat^2) * (1/K) + eps); act = fp16(h*inv*w);
+    row quantization.  ref: opt/int8_norm_quant.py:23-44 (and opt/int8_norm1_producer.py:29-61)."""
+    xf, af = np.asarray(x).astype(F32), np.asarray(a).astype(F32)
+    k = xf.shape[-1]
+    raw = fma32(af, f16(g), xf)
+    h = f16(raw)
+    stat = h if round_stats else raw
+    ss = np.sum(stat.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    inv = (1.0 / np.sqrt(ss / k + eps)).astype(F32)
+    act = f16((h * inv) * f16(w))
+    q, s = row_quant_ck(act.reshape(-1, k))
+    return h.astype(F16), q, s, act.astype(F16)
+
+
+def rms_norm_f16(x, gamma, eps) -> np.ndarray:
+    """fp16(x * rsqrt(sum(x^2)/K + eps) * gamma).  ref: opt/decoder_block0_norm.py:39-59."""
+    xf = np.asarray(x).astype(F32)
+    ss = np.sum(xf.astype(np.float64) ** 2, axis=-1, keepdims=True)
+    inv = (1.0 / np.sqrt(ss / xf.shape[-1] + eps)).astype(F32)
+    return ((xf * inv) * f16(gamma)).astype(F16)
+
+
+def final_residual_layernorm(h, o, gate, gamma, beta, eps) -> np.ndarray:
+    """raw = fma(o, gate, h); LayerNorm; fp16(fma(n, gamma, beta)).  ref: opt/decoder_final_norm.py:35-56."""
+    raw = fma32(np.asarray(o).astype(F32), f16(gate), np.asarray(h).astype(F32))
+    r64 = raw.astype(np.float64)
+    mean = r64.mean(axis=-1, keepdims=True)
+    var = r64.var(axis=-1, keepdims=True)
+    inv = (1.0 / np.sqrt(var + eps)).astype(F32)
+    n = ((raw - mean.astype(F32)) * inv).astype(F32)
+    return fma32(n, f16(gamma), f16(beta)).astype(F16)
+
+
+def qk_rope(qkv: np.ndarray, cos: np.ndarray, sin: np.ndarray, heads: int, eps: float):
+    """Per (token, head): q/k RMSNorm (fp32 stats) -> fp16 -> rotate-half RoPE on the first R dims,
+    each product rounded to fp16 before the fp32 sum.  qkv [b,n,H*192] laid out per head as
+    [q(64) | k(64) | v(64)]; cos/sin [b,n,1,R].  ref: opt/decoder_fused_qk_rope.py:13-35."""
+    b, n, _ = qkv.shape
+    x = np.asarray(qkv).astype(F32).reshape(b, n, heads, 3, 64)
+    c = np.asarray(cos).astype(F32).reshape(b, n, 1, -1)
+    s = np.asarray(sin).astype(F32).reshape(b, n, 1, -1)
+    r = c.shape[-1]
+    outs = []
+    for part in (0, 1):
+        v = x[:, :, :, part, :]
+        ss = np.sum(v.astype(np.float64) ** 2, axis=-1, keepdims=True)
+        inv = (1.0 / np.sqrt(ss / 64.0 + eps)).astype(F32)
+        v = f16(v * inv)
+        rot = np.concatenate([-v[..., r // 2:r], v[..., : r // 2]], axis=-1)
+        rope = f16(v[..., :r] * c) + f16(rot * s)
+        outs.append(np.concatenate([rope, v[..., r:]], axis=-1).astype(F16))
+    return outs[0], outs[1], x[:, :, :, 2, :].astype(F16)
+
+
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.ndarray:
+    """softmax(q k^T * scale) v in float64 for [B,H,S,D] fp16 inputs (non-causal, no mask).
+    ref: opt/decoder_fused_qk_rope.py:73 (PyTorch SDPA)."""
+    qf, kf, vf = (torch.from_numpy(np.asarray(t).astype(np.float64)) for t in (q, k, v))
+    p = torch.softmax((qf @ kf.transpose(-1, -2)) * scale, dim=-1)
+    return (p @ vf).numpy()
+
+
+# ---------------------------------------------------------------------------
+# (a15) pixel finalization, (a8) tile planner and blend
+# ---------------------------------------------------------------------------
+def finalize_pixels(x: np.ndarray, std, mean) -> np.ndarray:
+    """clamp(x*std + mean, 0, 1) in fp32 without FMA, NaN preserved.  ref: opt/fp16_finalize.py:249-265."""
+    xf = np.asarray(x).astype(F32)
+    v = xf * np.asarray(std, F32).reshape(1, 3, 1, 1, 1) + np.asarray(mean, F32).reshape(1, 3, 1, 1, 1)
+    v = np.where(v < 0, F32(0), np.where(v > 1, F32(1), v))
+    return v.astype(F32)
+
+
+def split_tiles(length: int, tile_size: int, overlap_min: int, ratio: int):
+    """Encoder spatial tile split: (starts, sizes, overlaps).  ref: h3vae_runtime.py:584-603."""
+    if tile_size <= overlap_min:
+        raise ValueError("encoder tile must exceed its minimum overlap")
+    if tile_size >= length:
+        return [0], [length], []
+    count = math.ceil(length / tile_size)
+    while True:
+        overlaps = [overlap_min] * (count - 1)
+        remaining = tile_size * count - sum(overlaps) - length
+        if remaining >= 0:
+            break
+        count += 1
+    for i in range(remaining // ratio):
+        overlaps[i % (count - 1)] += ratio
+    starts = [0]
+    for ov in overlaps:
+        starts.append(starts[-1] + tile_size - ov)
+    return starts, [tile_size] * count, overlaps
+
+
+def blend_linear(a: np.ndarray, b: np.ndarray, overlap: int, axis: int) -> np.ndarray:
+    """Blend the last `overlap` entries of a into the first of b with a linear ramp
+    w_i = i / overlap (i = 0..overlap-1): b[i] = a[-overlap + i]*(1-w_i) + b[i]*w_i.
+    (The reference's core.blend is external; this is the linear overlap blend the benchmark
+    configuration specifies.)"""
+    if overlap <= 0:
+        return b
+    b = np.array(b, copy=True)
+    w = (np.arange(overlap, dtype=np.float64) / overlap)
+    shape = [1] * b.ndim
+    shape[axis] = overlap
+    w = w.reshape(shape)
+    sl_a = [slice(None)] * a.ndim
+    sl_a[axis] = slice(a.shape[axis] - overlap, None)
+    sl_b = [slice(None)] * b.ndim
+    sl_b[axis] = slice(0, overlap)
+    b[tuple(sl_b)] = (a[tuple(sl_a)] * (1 - w) + b[tuple(sl_b)] * w).astype(b.dtype)
+    return b

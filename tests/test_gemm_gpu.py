@@ -1,0 +1,78 @@
+"""INT8 decoder GEMM family on the B200 vs the CPU oracle (CK contract restated from
+opt/int8_ffn_up_fused.py:76-90 and opt/decoder_fused_qk_rope.py:13-35).  int32 accumulators are
+bit-exact; fp16 outputs within max-abs 1e-2 / rel 1e-3."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import h3vae_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _close(got, ref, atol=1e-2, rtol=1e-3):
+    got = np.asarray(got, np.float32)
+    ref = np.asarray(ref, np.float32)
+    diff = np.abs(got - ref)
+    assert np.all(diff <= atol + rtol * np.abs(ref)), (diff.max(), np.unravel_index(diff.argmax(), diff.shape))
+
+
+def _rand_operands(rng, m, n, k):
+    q = rng.integers(-127, 128, size=(m, k), dtype=np.int8)
+    s = (rng.random((m, 1), dtype=np.float32) * 0.02 + 0.001).astype(np.float32)
+    w = rng.integers(-127, 128, size=(n, k), dtype=np.int8)
+    ws = (rng.random(n, dtype=np.float32) * 0.001 + 0.0001).astype(np.float32)
+    b = (rng.standard_normal(n) * 0.5).astype(np.float16)
+    return q, s, w, ws, b
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1024, 1024), (17, 3072, 1024), (129, 2048, 2048), (300, 136, 256),
+                                   (4096, 1024, 1024), (4096, 1024, 4096), (7188, 2048, 2048)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_gemm_i8(cuda_lib, m, n, k, with_bias):
+    from h3vae_b200 import kernels as K
+    rng = np.random.default_rng(m * 31 + n + k)
+    q, s, w, ws, b = _rand_operands(rng, m, n, k)
+    bias = b if with_bias else None
+    acc = torch.empty((m, n), dtype=torch.int32, device="cuda")
+    out = K.gemm_i8(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(), torch.from_numpy(w).cuda(),
+                    torch.from_numpy(ws).cuda(), None if bias is None else torch.from_numpy(bias).cuda(), acc_out=acc)
+    ref_acc = O.linear_acc(q, w)
+    assert np.array_equal(acc.cpu().numpy(), ref_acc)
+    _close(out.cpu().numpy(), O.linear_epilogue(ref_acc, s, ws, bias))
+
+
+@pytest.mark.parametrize("m,f,k", [(1, 4096, 1024), (17, 4096, 1024), (129, 8192, 2048), (4096, 4096, 1024),
+                                   (200, 136, 256)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_ffn_up_swiglu(cuda_lib, m, f, k, with_bias):
+    from h3vae_b200 import kernels as K
+    rng = np.random.default_rng(m + f + k)
+    q, s, w, ws, b = _rand_operands(rng, m, 2 * f, k)
+    bias = b if with_bias else None
+    act = K.gemm_i8_swiglu(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(), torch.from_numpy(w).cuda(),
+                           torch.from_numpy(ws).cuda(), None if bias is None else torch.from_numpy(bias).cuda())
+    _close(act.cpu().numpy(), O.ffn_up_swiglu(q, s, w, ws, bias), atol=2e-2)
+
+
+@pytest.mark.parametrize("batch,tokens,heads,k,r", [(4, 1024, 16, 1024, 48), (2, 300, 4, 256, 48),
+                                                    (1, 129, 2, 512, 64), (1, 64, 1, 128, 0)])
+def test_qkv_rope(cuda_lib, batch, tokens, heads, k, r):
+    from h3vae_b200 import kernels as K
+    rng = np.random.default_rng(batch * tokens + heads)
+    m = batch * tokens
+    q, s, w, ws, b = _rand_operands(rng, m, heads * 192, k)
+    ang = rng.random((batch, tokens, 1, max(r, 2)), dtype=np.float32)[..., :r] * 6.28
+    cos = np.cos(ang).astype(np.float16)
+    sin = np.sin(ang).astype(np.float16)
+    eps = 1e-6
+    qo, ko, vo = K.gemm_i8_qkv_rope(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(),
+                                    torch.from_numpy(w).cuda(), torch.from_numpy(ws).cuda(),
+                                    torch.from_numpy(b).cuda(), batch, tokens, heads,
+                                    torch.from_numpy(cos).cuda(), torch.from_numpy(sin).cuda(), eps)
+    qkv = O.prequantized_linear(q, s, w, ws, b).reshape(batch, tokens, heads * 192)
+    rq, rk, rv = O.qk_rope(qkv, cos, sin, heads, eps)
+    # kernel layout is [b, H, n, 64]; oracle returns [b, n, H, 64]
+    _close(qo.permute(0, 2, 1, 3).cpu().numpy(), rq, atol=1e-2)
+    _close(ko.permute(0, 2, 1, 3).cpu().numpy(), rk, atol=1e-2)
+    _close(vo.permute(0, 2, 1, 3).cpu().numpy(), rv, atol=1e-2)
