@@ -1,0 +1,398 @@
+"""Benchmark: BASELINE config 5, the full-video INT8 round trip (768x1344x124, tile256).
+
+One step = encode + decode of the synthetic video through H3VAEPyOptRuntime (the reference's
+first_stage_model API): 24 spatial tiles (tile 256, 32-px minimum overlap) x 8 causal 17-frame
+clips, encoded 4 clips per call (config 3 shape [4,3,17,256,256], every 3x3x3 residual conv on the
+INT8 tcgen05 kernel) and decoded 4 tiles per call (config 4 shape [4,16,5,32,32], 6 INT8
+transformer blocks), blended linearly and finalized to fp32 RGB.  With torchrun (one process per
+GPU) the tile batches are sharded over the ranks and the blend canvases are summed on rank 0
+with one NCCL reduce.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line (rank 0).  `value` is seconds per round trip with the input already in HBM
+(device-timed with CUDA events, max over ranks); `e2e` is the same call with the video in pinned
+host memory, the host->device copy and the device->host copy of the fp32 result inside the
+timed region.  Inputs (768 MB video, 1.7 GB canvas) are larger than L2.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "comfyui-h3vae-pyopt_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+import torch  # noqa: E402
+
+VIDEO_SHAPE = (1, 3, 124, 768, 1344)
+TILE = 256
+OVERLAP = 32
+METRIC = "768x1344x124 tile256 encode+decode round-trip seconds"
+UNIT = "s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------------------
+# Synthetic input: smooth low-frequency noise (Gaussian-blurred N(0,1), sigma 8 px / 2 frames),
+# renormalized and clipped to [-1, 1].  Generated on the GPU, seeded.
+# ---------------------------------------------------------------------------
+def _gauss(sigma: float, device) -> torch.Tensor:
+    r = int(3 * sigma)
+    x = torch.arange(-r, r + 1, dtype=torch.float32, device=device)
+    k = torch.exp(-0.5 * (x / sigma) ** 2)
+    return k / k.sum()
+
+
+def synthetic_video(device, seed: int = 0) -> torch.Tensor:
+    g = torch.Generator(device=device).manual_seed(seed)
+    b, c, t, h, w = VIDEO_SHAPE
+    out = torch.empty(VIDEO_SHAPE, dtype=torch.float16, device=device)
+    ks, kt = _gauss(8.0, device), _gauss(2.0, device)
+    for ci in range(c):
+        v = torch.randn((t, h, w), generator=g, device=device)
+        v = torch.nn.functional.conv1d(v.reshape(-1, 1, w), ks.view(1, 1, -1), padding=ks.numel() // 2).view(t, h, w)
+        v = torch.nn.functional.conv1d(v.transpose(1, 2).reshape(-1, 1, h), ks.view(1, 1, -1),
+                                       padding=ks.numel() // 2).view(t, w, h).transpose(1, 2)
+        v = torch.nn.functional.conv1d(v.permute(1, 2, 0).reshape(-1, 1, t), kt.view(1, 1, -1),
+                                       padding=kt.numel() // 2).view(h, w, t).permute(2, 0, 1)
+        v = v / v.std()
+        out[0, ci] = v.clamp(-1, 1).half()
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Clock sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        os.unlink(self.path)
+        load = [s for s in sm if smax and s > 0.5 * smax] or sm
+        return {"sm_mhz": statistics.median(load) if load else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the oracle port on the host cores, on a bounded sample
+# ---------------------------------------------------------------------------
+def int8_ops_per_round_trip(cfg=None, dcfg=None) -> tuple[float, float]:
+    """(INT8 ops, fp16 attention flops) of one round trip on the config-5 video, from the tile and
+    clip counts and the per-call algorithmic counts of configs 3 and 4 (causal taps skipped)."""
+    from h3vae_b200 import tiling
+    from h3vae_b200.model import DecoderConfig, EncoderConfig
+    cfg = cfg or EncoderConfig()
+    dcfg = dcfg or DecoderConfig()
+    b, c, t, h, w = VIDEO_SHAPE
+    plan = tiling.TilePlan.build(h, w, TILE, OVERLAP, cfg.spatial_ratio)
+    tiles = plan.rows * plan.cols
+    clips = -(-t // 17)
+    enc = 0.0
+    d, hh, ww = 17, TILE, TILE
+    for s, ch in enumerate(cfg.channels):
+        cin = cfg.channels[s - 1] if s else ch
+        for j in range(cfg.blocks_per_stage):
+            ci = cin if j == 0 else ch
+            taps = sum(min(x + 1, 3) for x in range(d)) * 9
+            if s in cfg.int8_stages:
+                enc += 2 * hh * ww * taps * (ci * ch + ch * ch)
+        if cfg.spatial_down[s]:
+            hh, ww = hh // 2, ww // 2
+        if cfg.temporal_down[s]:
+            d = (d - 1) // 2 + 1
+    enc *= tiles * clips
+    ratio = 2 ** sum(dcfg.up_spatial)
+    tokens_t = 17
+    for down in cfg.temporal_down:
+        if down:
+            tokens_t = (tokens_t - 1) // 2 + 1
+    tok = tokens_t * (TILE // ratio) ** 2
+    per_tile = dcfg.blocks * 2 * tok * dcfg.hidden * (3 * dcfg.hidden + dcfg.hidden + 2 * dcfg.ffn + dcfg.ffn)
+    attn = dcfg.blocks * 4 * tok * tok * dcfg.hidden
+    lplan = plan.scaled(ratio)
+    dec_tasks = lplan.rows * lplan.cols * clips
+    return enc + per_tile * dec_tasks, attn * dec_tasks
+
+
+def cpu_conv_sample(seconds_budget: float = 15.0) -> dict:
+    """Time the oracle's INT8 conv (per-tensor quantization + exact integer conv + epilogue) on the
+    config-1 tensor [1,128,9,64,64] with all host threads; returns INT8 ops/s."""
+    import numpy as np
+    from oracle import h3vae_oracle as O
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    x = torch.randn(1, 128, 11, 66, 66, generator=g).half().numpy()
+    w = torch.randn(128, 128, 3, 3, 3, generator=g) / 3456 ** 0.5
+    qw, ws = O.prepare_int8_weight(w)
+    qwn, wsn = qw.numpy(), ws.numpy()
+    ops = 2 * 9 * 64 * 64 * 128 * 128 * 27
+    times = []
+    t_end = time.perf_counter() + seconds_budget
+    while time.perf_counter() < t_end or not times:
+        t0 = time.perf_counter()
+        O.int8_valid_conv3d(x, qwn, wsn, (3, 3, 3), bias=None)
+        times.append(time.perf_counter() - t0)
+        if len(times) >= 20:
+            break
+    best = float(np.median(times))
+    return {"ops_per_s": ops / best, "seconds_per_sample": best, "samples": len(times),
+            "cores": torch.get_num_threads()}
+
+
+# ---------------------------------------------------------------------------
+def init_dist(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+        return dist.group.WORLD, dist.get_rank(), world, local
+    torch.cuda.set_device(0)
+    return None, 0, 1, 0
+
+
+def max_over_ranks(v: float, pg) -> float:
+    if pg is None:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=pg)
+    return float(t.item())
+
+
+def barrier(pg):
+    if pg is not None:
+        import torch.distributed as dist
+        dist.barrier(group=pg)
+    torch.cuda.synchronize()
+
+
+def run_reference(args):
+    """The reference arm: the reference's own CPU implementation of the path is not runnable as a
+    whole (its model code is not distributed and its kernels are Triton/CK), so the oracle port of
+    its INT8 conv arithmetic is timed on the host cores on a bounded sample and extrapolated to the
+    round trip's INT8 op count."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    samples = []
+    for _ in range(args.warmup):
+        cpu_conv_sample(2.0)
+    for _ in range(args.steps):
+        samples.append(cpu_conv_sample(5.0))
+    ops_s = statistics.median(s["ops_per_s"] for s in samples)
+    int8_ops, attn = int8_ops_per_round_trip()
+    value = (int8_ops + attn) / ops_s
+    line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": value * 1e3, "higher_is_better": False,
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp16", "data": "synthetic",
+            "config": {"workload": "config5 full-video round trip (extrapolated from a CPU sample)",
+                       "video": list(VIDEO_SHAPE)},
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": samples[0]["cores"], "kind": "port",
+                             "sample": "oracle INT8 conv (per-tensor quant + exact int conv + epilogue) on the "
+                                       "config-1 tensor [1,128,9,64,64], extrapolated by the round trip's "
+                                       f"{int8_ops / 1e15:.3f} POP INT8 + {attn / 1e15:.3f} PFLOP attention"},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+        return
+    from h3vae_b200 import kernels as K
+    from h3vae_b200.runtime import H3VAEPyOptRuntime
+
+    pg, rank, world, local = init_dist(args)
+    dev = torch.device("cuda", local)
+    runtime = H3VAEPyOptRuntime(device=str(dev), int8_encode=True, int8_decode=True, decode_fusions=True,
+                                tile_batch=4, encoder_staged_batch=4, log_calls=False, compile_decoder=False,
+                                compile_encoder=False, decoder_tile_size=TILE, tile_overlap_min=OVERLAP,
+                                process_group=pg)
+    video = synthetic_video(dev) if rank == 0 else None
+    torch.cuda.synchronize()
+
+    def step(x):
+        lat = runtime.encode(x)
+        return lat, runtime.decode(lat)
+
+    for _ in range(args.warmup):
+        step(video)
+    barrier(pg)
+
+    # ---- timed region (inputs resident in HBM) ----
+    stream = torch.cuda.current_stream()
+    enc_ms, dec_ms, tot_ms = [], [], []
+    K.CONV_TIMING = []
+    launches0 = K.LAUNCHES["count"]
+    with ClockSampler(local) as clocks:
+        barrier(pg)
+        for _ in range(args.steps):
+            e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+            e0.record(stream)
+            lat = runtime.encode(video)
+            e1.record(stream)
+            runtime.decode(lat)
+            e2.record(stream)
+            torch.cuda.synchronize()
+            enc_ms.append(e0.elapsed_time(e1))
+            dec_ms.append(e1.elapsed_time(e2))
+            tot_ms.append(e0.elapsed_time(e2))
+        barrier(pg)
+    launches = K.LAUNCHES["count"] - launches0
+    conv_events = K.CONV_TIMING
+    K.CONV_TIMING = None
+    step_s = max_over_ranks(statistics.mean(tot_ms) / 1e3, pg)
+    enc_s = max_over_ranks(statistics.mean(enc_ms) / 1e3, pg)
+    dec_s = max_over_ranks(statistics.mean(dec_ms) / 1e3, pg)
+
+    # roofline of the dominant INT8 kernel (the tcgen05 implicit-GEMM conv), live CUDA events
+    conv_ms = sum(a.elapsed_time(b) for a, b, _ in conv_events)
+    conv_ops = sum(o for _, _, o in conv_events)
+    conv_launches = len(conv_events)
+    a_ = torch.randint(-127, 127, (8192, 8192), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a_, a_.t())
+    torch.cuda.synchronize()
+    p0, p1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    p0.record()
+    for _ in range(10):
+        torch._int_mm(a_, a_.t())
+    p1.record()
+    torch.cuda.synchronize()
+    int8_peak = 2 * 8192 ** 3 * 10 / (p0.elapsed_time(p1) * 1e-3) / 1e12
+    del a_
+    conv_tops = conv_ops / (conv_ms * 1e-3) / 1e12 if conv_ms > 0 else 0.0
+
+    # ---- end-to-end through the public API with host buffers ----
+    e2e = None
+    if not args.no_e2e:
+        host_video = video.cpu().pin_memory() if rank == 0 else None
+        out_shape = runtime.decode_output_shape((1, runtime.latent_channels, runtime._tokens_from_frames(124),
+                                                 VIDEO_SHAPE[3] // 8, VIDEO_SHAPE[4] // 8))
+        host_out = torch.empty(out_shape, dtype=torch.float32).pin_memory() if rank == 0 else None
+        e2e_ms = []
+        barrier(pg)
+        for _ in range(max(1, args.steps)):
+            t0 = torch.cuda.Event(enable_timing=True)
+            t1 = torch.cuda.Event(enable_timing=True)
+            t0.record(stream)
+            lat = runtime.encode(host_video)
+            pix = runtime.decode(lat)
+            if rank == 0:
+                host_out.copy_(pix, non_blocking=True)
+            t1.record(stream)
+            torch.cuda.synchronize()
+            e2e_ms.append(t0.elapsed_time(t1))
+        barrier(pg)
+        e2e_s = max_over_ranks(statistics.mean(e2e_ms) / 1e3, pg)
+        e2e = {"value": e2e_s, "unit": UNIT,
+               "h2d_bytes_per_step": int(video.numel() * video.element_size()) if rank == 0 else 0,
+               "d2h_bytes_per_step": int(host_out.numel() * 4) if rank == 0 else 0}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        s = cpu_conv_sample(15.0)
+        int8_ops, attn = int8_ops_per_round_trip(runtime.encoder.cfg, runtime.decoder.cfg)
+        cpu = {"value": (int8_ops + attn) / s["ops_per_s"], "unit": UNIT, "cores": s["cores"], "kind": "port",
+               "sample": f"oracle INT8 conv on the config-1 tensor [1,128,9,64,64] ({s['samples']} runs, "
+                         f"{s['seconds_per_sample']:.2f} s each), extrapolated to the round trip's "
+                         f"{int8_ops / 1e15:.3f} POP INT8 + {attn / 1e15:.3f} PFLOP attention"}
+
+    if rank == 0:
+        cl = clocks.summary()
+        int8_ops, attn = int8_ops_per_round_trip(runtime.encoder.cfg, runtime.decoder.cfg)
+        line = {
+            "metric": METRIC, "value": step_s, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "int8 (conv/linear), fp16 (attention, fp16 convs)",
+            "data": "synthetic (seeded Gaussian-blurred noise video; random-init H3-structured weights)",
+            "config": {"workload": "config5 full-video round trip: encode (config3 tiles, all 3x3x3 residual convs "
+                                   "INT8) + decode (config4 tiles, 6 INT8 blocks) + linear overlap blend",
+                       "video": list(VIDEO_SHAPE), "tile": TILE, "overlap_min": OVERLAP, "clip": 17,
+                       "encoder_batch": 4, "decoder_tile_batch": 4, "parallelism": f"tile-dp{world}",
+                       "l2": "inputs larger than L2 (768 MB video, 1.7 GB canvas)"},
+            "encode_s": enc_s, "decode_s": dec_s,
+            "int8_ops_per_step": int8_ops, "attention_flops_per_step": attn,
+            "roofline": {"bound": "tensor", "kernel": "h3b conv3d_i8 (tcgen05 kind::i8 implicit GEMM)",
+                         "achieved": conv_tops, "peak": int8_peak, "unit": "TFLOP/s",
+                         "peak_source": "INT8 ops/s of torch._int_mm 8192^3 measured live on this GPU "
+                                        "(MEASURED_PEAKS.json has no INT8 entry)",
+                         "frac": conv_tops / int8_peak if int8_peak else None, "traffic": None,
+                         "launches": conv_launches, "ms_total": conv_ms},
+            "e2e": e2e, "cpu_baseline": cpu, "clocks": cl, "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -428,7 +428,8 @@ int h3b_final_residual_layernorm(const void* h, const void* o, const void* gate,
 int h3b_qk_rope(const void* qkv, const void* cos_t, const void* sin_t, int64_t batch, int64_t tokens, int64_t heads,
                 int64_t rot_dims, float eps, void* q_out, void* k_out, h3b_stream_t stream) {
   const char* name = "h3b_qk_rope";
-  if (!qkv || !cos_t || !sin_t || !q_out || !k_out) return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  if (!qkv || !q_out || !k_out || (rot_dims > 0 && (!cos_t || !sin_t)))
+    return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
   if (batch <= 0 || tokens <= 0 || heads <= 0) return h3b_host::set_error(H3B_EINVAL, "%s: empty input", name);
   if (rot_dims < 0 || rot_dims > 64 || rot_dims % 2) return h3b_host::set_error(H3B_EINVAL, "%s: bad rotary dims", name);
   for (const void* p : std::initializer_list<const void*>{qkv, q_out, k_out})

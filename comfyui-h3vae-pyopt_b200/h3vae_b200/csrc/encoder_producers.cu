@@ -166,6 +166,9 @@ __global__ void gn_merge_kernel(const float2* __restrict__ partials, NormShape s
 // ---------------------------------------------------------------------------
 // Norm -> SiLU -> pad producer.  MODE 0: absmax of the interior (atomic on
 // amax_out); MODE 1: INT8 output with scale from amax; MODE 2: fp16 output.
+// One CTA per output row (b, frame, h): the row's (w, channel-vector) pairs are
+// walked with shifts only (C/8 is a power of two), so the kernel is bound by
+// HBM, not by index arithmetic.
 // ---------------------------------------------------------------------------
 template <int MODE>
 __global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* __restrict__ x,
@@ -175,50 +178,42 @@ __global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* _
                                                                  const float2* __restrict__ stats, NormShape s,
                                                                  float* amax, float* scale_out, void* out) {
   const int vpp = s.C / kVec;
-  const int Dp = s.D + 2, Hp = s.H + 2, Wp = s.W + 2;
+  const int vshift = __ffs(vpp) - 1;
   const int cg = s.C / kGroups;
-  // MODE 0 only walks the interior; the padded ring duplicates interior values
-  // or is zero, so it cannot raise the maximum.
-  const int64_t positions = (MODE == 0) ? static_cast<int64_t>(s.B) * s.D * s.H * s.W
-                                        : static_cast<int64_t>(s.B) * Dp * Hp * Wp;
-  const int64_t total = positions * vpp;
+  // MODE 0 walks the interior rows only: the padded ring duplicates interior
+  // values or is zero, so it cannot raise the maximum.
+  const int Hr = (MODE == 0) ? s.H : s.H + 2;
+  const int Wr = (MODE == 0) ? s.W : s.W + 2;
+  const int Dr = (MODE == 0) ? s.D : s.D + 2;
+  int row = blockIdx.x;
+  const int hr = row % Hr;
+  row /= Hr;
+  const int tr = row % Dr;
+  const int b = row / Dr;
+  const int t = (MODE == 0) ? tr : tr - 2;
+  int h = (MODE == 0) ? hr : hr - 1;
+  h = h < 0 ? -h : (h >= s.H ? 2 * s.H - 2 - h : h);
+  const bool frame_ok = t >= 0;
   float scale = 1.0f;
   if (MODE == 1) {
-    const float m = *amax;
-    scale = __fmul_rn(m, 1.0f / 127.0f);
+    scale = __fmul_rn(*amax, 1.0f / 127.0f);
     if (!(scale > 0.0f)) scale = 1.0f;
     if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
   }
+  const int row_vecs = Wr * vpp;
+  const __half* xrow = x + ((static_cast<int64_t>(b) * s.D + (frame_ok ? t : 0)) * s.H + h) * s.W * s.C;
+  const float2* st = stats + (static_cast<int64_t>(b) * s.D + (frame_ok ? t : 0)) * kGroups;
+  const int64_t out_row = static_cast<int64_t>(blockIdx.x) * row_vecs;
   float local_max = 0.0f;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(kPackThreads) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * kPackThreads) {
-    const int v = static_cast<int>(i % vpp);
-    int64_t pos = i / vpp;
-    int b, t, h, w;
-    bool inside;
-    if (MODE == 0) {
-      w = static_cast<int>(pos % s.W); pos /= s.W;
-      h = static_cast<int>(pos % s.H); pos /= s.H;
-      t = static_cast<int>(pos % s.D);
-      b = static_cast<int>(pos / s.D);
-      inside = true;
-    } else {
-      const int wp = static_cast<int>(pos % Wp); pos /= Wp;
-      const int hp = static_cast<int>(pos % Hp); pos /= Hp;
-      const int tp = static_cast<int>(pos % Dp);
-      b = static_cast<int>(pos / Dp);
-      t = tp - 2;
-      h = hp - 1;
-      w = wp - 1;
-      h = h < 0 ? -h : (h >= s.H ? 2 * s.H - 2 - h : h);
-      w = w < 0 ? -w : (w >= s.W ? 2 * s.W - 2 - w : w);
-      inside = t >= 0;
-    }
+  for (int i = threadIdx.x; i < row_vecs; i += kPackThreads) {
+    const int v = i & (vpp - 1);
+    int w = (i >> vshift) - ((MODE == 0) ? 0 : 1);
+    w = w < 0 ? -w : (w >= s.W ? 2 * s.W - 2 - w : w);
     const int c0 = v * kVec;
     float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (inside) {
+    if (frame_ok) {
       float f[8], gm[8], bt[8];
-      load_h8(x + ((((static_cast<int64_t>(b) * s.D + t) * s.H + h) * s.W) + w) * s.C + c0, f);
+      load_h8(xrow + static_cast<int64_t>(w) * s.C + c0, f);
       load_h8(gamma + c0, gm);
       load_h8(beta + c0, bt);
       if (pre_bias != nullptr) {
@@ -227,7 +222,6 @@ __global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* _
 #pragma unroll
         for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
       }
-      const float2* st = stats + (static_cast<int64_t>(b) * s.D + t) * kGroups;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
         const float2 mr = st[(c0 + j) / cg];
@@ -243,9 +237,9 @@ __global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* _
       __align__(8) int8_t q[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) q[j] = quant_half_away(z[j], scale);
-      reinterpret_cast<uint2*>(out)[i] = *reinterpret_cast<const uint2*>(q);
+      reinterpret_cast<uint2*>(out)[out_row + i] = *reinterpret_cast<const uint2*>(q);
     } else {
-      store_h8(reinterpret_cast<__half*>(out) + i * kVec, z);
+      store_h8(reinterpret_cast<__half*>(out) + (out_row + i) * kVec, z);
     }
   }
   if (MODE == 0) {
@@ -263,7 +257,7 @@ __global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* _
 
 // ---------------------------------------------------------------------------
 // Residual + bias pack with right/bottom reflect (+1) and two causal zero
-// frames: y = fp16(r + (x + bias)) in fp32.
+// frames: y = fp16(r + (x + bias)) in fp32.  One CTA per output row.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kPackThreads) residual_pack_kernel(const __half* __restrict__ x,
                                                                      const __half* __restrict__ r,
@@ -271,21 +265,23 @@ __global__ void __launch_bounds__(kPackThreads) residual_pack_kernel(const __hal
                                                                      int D, int H, int W, __half* __restrict__ y) {
   const int vpp = C / kVec;
   const int Dp = D + 2, Hp = H + 1, Wp = W + 1;
-  const int64_t total = static_cast<int64_t>(B) * Dp * Hp * Wp * vpp;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(kPackThreads) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * kPackThreads) {
-    const int v = static_cast<int>(i % vpp);
-    int64_t pos = i / vpp;
-    const int wp = static_cast<int>(pos % Wp); pos /= Wp;
-    const int hp = static_cast<int>(pos % Hp); pos /= Hp;
-    const int tp = static_cast<int>(pos % Dp);
-    const int b = static_cast<int>(pos / Dp);
-    const int t = tp - 2;
-    const int h = hp == H ? H - 2 : hp;
+  int row = blockIdx.x;
+  const int hp = row % Hp;
+  row /= Hp;
+  const int tp = row % Dp;
+  const int b = row / Dp;
+  const int t = tp - 2;
+  const int h = hp == H ? H - 2 : hp;
+  const int row_vecs = Wp * vpp;
+  const int64_t in_row = ((static_cast<int64_t>(b) * D + (t >= 0 ? t : 0)) * H + h) * W * C;
+  const int64_t out_row = static_cast<int64_t>(blockIdx.x) * row_vecs;
+  for (int i = threadIdx.x; i < row_vecs; i += kPackThreads) {
+    const int v = i % vpp;
+    const int wp = i / vpp;
     const int w = wp == W ? W - 2 : wp;
     float out[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (t >= 0) {
-      const int64_t off = ((((static_cast<int64_t>(b) * D + t) * H + h) * W) + w) * C + v * kVec;
+      const int64_t off = in_row + static_cast<int64_t>(w) * C + v * kVec;
       float fx[8], fr[8], fb[8];
       load_h8(x + off, fx);
       load_h8(r + off, fr);
@@ -293,7 +289,7 @@ __global__ void __launch_bounds__(kPackThreads) residual_pack_kernel(const __hal
 #pragma unroll
       for (int j = 0; j < 8; ++j) out[j] = __fadd_rn(fr[j], __fadd_rn(fx[j], fb[j]));
     }
-    store_h8(y + i * kVec, out);
+    store_h8(y + (out_row + i) * kVec, out);
   }
 }
 
@@ -473,17 +469,16 @@ int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H
   if (rc) return rc;
   if (cudaMemsetAsync(w.amax, 0, sizeof(float), st) != cudaSuccess)
     return h3b_host::set_error(H3B_ECUDA, "%s: memset failed", name);
-  const int vpp = (int)(C / kVec);
   const __half* xh = static_cast<const __half*>(x);
   const __half* pb = static_cast<const __half*>(pre_bias);
   const __half* gh = static_cast<const __half*>(gamma);
   const __half* bh = static_cast<const __half*>(beta);
-  norm_pack_kernel<0><<<grid_for(B * D * H * W * vpp, kPackThreads), kPackThreads, 0, st>>>(
-      xh, pb, gh, bh, w.stats, s, w.amax, nullptr, nullptr);
+  norm_pack_kernel<0><<<(unsigned)(B * D * H), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax, nullptr,
+                                                                      nullptr);
   rc = h3b_host::check_launch(name);
   if (rc) return rc;
-  norm_pack_kernel<1><<<grid_for(B * (D + 2) * (H + 2) * (W + 2) * vpp, kPackThreads), kPackThreads, 0, st>>>(
-      xh, pb, gh, bh, w.stats, s, w.amax, scale, q);
+  norm_pack_kernel<1><<<(unsigned)(B * (D + 2) * (H + 2)), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax,
+                                                                                  scale, q);
   return h3b_host::check_launch(name);
 }
 
@@ -498,8 +493,7 @@ int h3b_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   rc = run_norm_stats(x, pre_bias, eps, s, w, st, name);
   if (rc) return rc;
-  const int vpp = (int)(C / kVec);
-  norm_pack_kernel<2><<<grid_for(B * (D + 2) * (H + 2) * (W + 2) * vpp, kPackThreads), kPackThreads, 0, st>>>(
+  norm_pack_kernel<2><<<(unsigned)(B * (D + 2) * (H + 2)), kPackThreads, 0, st>>>(
       static_cast<const __half*>(x), static_cast<const __half*>(pre_bias), static_cast<const __half*>(gamma),
       static_cast<const __half*>(beta), w.stats, s, nullptr, nullptr, y);
   return h3b_host::check_launch(name);
@@ -513,8 +507,7 @@ int h3b_residual_pack(const void* x, const void* r, const void* bias, int64_t B,
     return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: need H,W >= 2 and C %% 8 == 0", name);
   for (const void* p : std::initializer_list<const void*>{x, r, bias, y})
     if (!aligned16(p)) return h3b_host::set_error(H3B_EINVAL, "%s: tensors must be 16-byte aligned", name);
-  const int64_t total = B * (D + 2) * (H + 1) * (W + 1) * (C / kVec);
-  residual_pack_kernel<<<grid_for(total, kPackThreads), kPackThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  residual_pack_kernel<<<(unsigned)(B * (D + 2) * (H + 1)), kPackThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       static_cast<const __half*>(x), static_cast<const __half*>(r), static_cast<const __half*>(bias), (int)B, (int)C,
       (int)D, (int)H, (int)W, static_cast<__half*>(y));
   return h3b_host::check_launch(name);

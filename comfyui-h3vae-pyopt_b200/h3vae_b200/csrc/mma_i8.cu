@@ -42,6 +42,7 @@ struct MmaParams {
   int64_t ldo;           // GEMM row stride of out
   int64_t osB, osD, osH, osW;
   int32_t* acc_out;
+  const __half* residual;  // conv: optional fp16 tensor added after the fp16 rounding (same strides as out)
   // SwiGLU
   int F;
   // QKV + RoPE
@@ -92,6 +93,25 @@ __device__ __forceinline__ void store_row_chunk(__half* dst, const float (&v)[32
 
 __device__ __forceinline__ void store_acc_chunk(int32_t* dst, const uint32_t (&r)[32], int valid_cols) {
   for (int j = 0; j < 32 && j < valid_cols; ++j) dst[j] = static_cast<int32_t>(r[j]);
+}
+
+// v = fp16(fp16(v) + residual): the residual block's `x + h` on fp16 tensors.
+__device__ __forceinline__ void add_residual_chunk(float (&v)[32], const __half* res, int valid_cols, bool vec_ok) {
+  if (valid_cols >= 32 && vec_ok) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 raw = *reinterpret_cast<const uint4*>(res + q * 8);
+      const __half2* h = reinterpret_cast<const __half2*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(h[j]);
+        v[q * 8 + 2 * j] = __fadd_rn(round_fp16(v[q * 8 + 2 * j]), f.x);
+        v[q * 8 + 2 * j + 1] = __fadd_rn(round_fp16(v[q * 8 + 2 * j + 1]), f.y);
+      }
+    }
+  } else {
+    for (int j = 0; j < 32 && j < valid_cols; ++j) v[j] = __fadd_rn(round_fp16(v[j]), __half2float(res[j]));
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -305,6 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int n = min(n0 + j, p.N - 1);
               v[j] = dequant(r[j], sx, p.w_scale[n], p.bias, n);
             }
+            if (p.residual != nullptr) add_residual_chunk(v, p.residual + obase + n0, valid_cols, vec_ok);
             store_row_chunk(p.out + obase + n0, v, valid_cols, vec_ok);
             if (p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
           }
@@ -394,7 +415,7 @@ __global__ void conv3d_i8_simt_kernel(const int8_t* __restrict__ qx, int B, int 
                                       int sh, int sw, int Do, int Ho, int Wo, const float* x_scale,
                                       const float* __restrict__ w_scale, const __half* __restrict__ bias,
                                       __half* out, int64_t osB, int64_t osD, int64_t osH, int64_t osW,
-                                      int32_t* acc_out) {
+                                      int32_t* acc_out, const __half* residual) {
   const int64_t total = static_cast<int64_t>(B) * Do * Ho * Wo * O;
   const int64_t ktot = static_cast<int64_t>(kd) * kh * kw * C;
   const float sx = *x_scale;
@@ -419,7 +440,9 @@ __global__ void conv3d_i8_simt_kernel(const int8_t* __restrict__ qx, int B, int 
         }
     float v = __fmul_rn(static_cast<float>(acc), sx);
     v = (bias != nullptr) ? __fmaf_rn(v, w_scale[n], __half2float(bias[n])) : __fmul_rn(v, w_scale[n]);
-    out[b * osB + od * osD + oh * osH + ow * osW + n] = __float2half_rn(v);
+    const int64_t o_off = b * osB + od * osD + oh * osH + ow * osW + n;
+    if (residual != nullptr) v = __fadd_rn(round_fp16(v), __half2float(residual[o_off]));
+    out[o_off] = __float2half_rn(v);
     if (acc_out != nullptr) acc_out[pos * O + n] = acc;
   }
 }
@@ -483,8 +506,8 @@ extern "C" {
 
 int h3b_conv3d_i8(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int64_t out_channels, int kd, int kh,
                   int kw, int sd, int sh, int sw, const float* x_scale, const float* w_scale, const void* bias,
-                  void* out, const int64_t* out_strides, int32_t* acc_out, int causal_zero_frames,
-                  h3b_stream_t stream) {
+                  void* out, const int64_t* out_strides, const void* residual, int32_t* acc_out,
+                  int causal_zero_frames, h3b_stream_t stream) {
   const char* name = "h3b_conv3d_i8";
   if (!qx || !x_dims || !qw || !x_scale || !w_scale || !out || !out_strides)
     return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
@@ -518,7 +541,8 @@ int h3b_conv3d_i8(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int
     if (blocks > 65535LL * 16) blocks = 65535LL * 16;
     conv3d_i8_simt_kernel<<<static_cast<unsigned>(blocks), threads, 0, st>>>(
         qx, (int)B, (int)D, (int)H, (int)W, (int)C, qw, (int)O, kd, kh, kw, sd, sh, sw, (int)Do, (int)Ho, (int)Wo,
-        x_scale, w_scale, bias_h, out_h, out_strides[0], out_strides[1], out_strides[2], out_strides[3], acc_out);
+        x_scale, w_scale, bias_h, out_h, out_strides[0], out_strides[1], out_strides[2], out_strides[3], acc_out,
+        static_cast<const __half*>(residual));
     return h3b_host::check_launch(name);
   }
 
@@ -540,6 +564,9 @@ int h3b_conv3d_i8(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int
   p.out = out_h;
   p.osB = out_strides[0]; p.osD = out_strides[1]; p.osH = out_strides[2]; p.osW = out_strides[3];
   p.acc_out = acc_out;
+  p.residual = static_cast<const __half*>(residual);
+  if (residual != nullptr && (reinterpret_cast<uintptr_t>(residual) & 15u) != (reinterpret_cast<uintptr_t>(out) & 15u))
+    return h3b_host::set_error(H3B_EINVAL, "%s: residual and out must share 16-byte alignment", name);
 
   CUtensorMap ma, mb;
   uint64_t adims[5] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)D, (uint64_t)B};
@@ -622,7 +649,8 @@ int h3b_gemm_i8_qkv_rope(const int8_t* qa, const float* a_scale, const int8_t* q
   const int64_t M = batch * tokens, N = heads * 192;
   int rc = check_gemm_common(qa, a_scale, qw, w_scale, M, N, K, name);
   if (rc) return rc;
-  if (!cos_t || !sin_t || !q_out || !k_out || !v_out) return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  if (!q_out || !k_out || !v_out || (rot_dims > 0 && (!cos_t || !sin_t)))
+    return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
   if (rot_dims < 0 || rot_dims > 64 || rot_dims % 2)
     return h3b_host::set_error(H3B_EINVAL, "%s: rotary dims must be even and <= 64", name);
   for (const void* ptr : std::initializer_list<const void*>{q_out, k_out, v_out})

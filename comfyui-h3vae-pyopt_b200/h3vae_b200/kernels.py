@@ -15,6 +15,26 @@ F16 = torch.float16
 I8 = torch.int8
 F32 = torch.float32
 
+# Kernel-launch accounting (bench.py reads it): number of library kernels each wrapper launches.
+LAUNCHES = {"count": 0}
+# Optional per-call CUDA-event timing of the INT8 conv (bench.py's live roofline measurement):
+# when CONV_TIMING is a list, conv3d_i8 appends (start_event, end_event, int8_ops) per launch.
+CONV_TIMING: list | None = None
+
+
+def _count(n: int) -> None:
+    LAUNCHES["count"] += n
+
+
+def conv3d_int8_ops(b, c, d_out, h_out, w_out, o, kernel, causal_zero_frames) -> int:
+    """Algorithmic INT8 ops (2 per MAC) of one conv launch, excluding the skipped causal taps."""
+    kd, kh, kw = kernel
+    if causal_zero_frames == 2 and kd == 3:
+        taps = sum(min(t + 1, 3) for t in range(d_out)) * kh * kw
+    else:
+        taps = d_out * kd * kh * kw
+    return 2 * b * h_out * w_out * o * c * taps
+
 
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
@@ -64,9 +84,12 @@ def is_ndhwc(x: torch.Tensor) -> bool:
 def conv3d_i8(qx: torch.Tensor, x_scale: torch.Tensor, qweight: torch.Tensor, weight_scale: torch.Tensor,
               bias: torch.Tensor | None, kernel: tuple[int, int, int], stride: tuple[int, int, int] = (1, 1, 1),
               *, causal_zero_frames: int = 0, out: torch.Tensor | None = None,
-              acc_out: torch.Tensor | None = None) -> torch.Tensor:
-    """Valid INT8 conv3d of a padded NDHWC int8 activation (logical [B,C,D,H,W])."""
-    dev = _require_cuda(qx, x_scale, qweight, weight_scale, bias, out, acc_out)
+              residual: torch.Tensor | None = None, acc_out: torch.Tensor | None = None) -> torch.Tensor:
+    """Valid INT8 conv3d of a padded NDHWC int8 activation (logical [B,C,D,H,W]).
+
+    With `residual` (fp16, same shape and strides as the output) the epilogue returns
+    fp16(fp16(conv) + residual), the residual block's skip add."""
+    dev = _require_cuda(qx, x_scale, qweight, weight_scale, bias, out, acc_out, residual)
     if qx.ndim != 5 or qx.dtype != I8 or not is_ndhwc(qx):
         raise ValueError("qx must be a channels_last_3d int8 [B,C,D,H,W] tensor")
     _require(qweight, I8, "qweight")
@@ -92,12 +115,23 @@ def conv3d_i8(qx: torch.Tensor, x_scale: torch.Tensor, qweight: torch.Tensor, we
     if acc_out is not None and (acc_out.dtype != torch.int32 or acc_out.shape != (b, o, do, ho, wo)
                                 or not is_ndhwc(acc_out)):
         raise ValueError("acc_out must be a channels_last_3d int32 [B,O,Do,Ho,Wo] tensor")
+    if residual is not None and (residual.dtype != F16 or residual.shape != out.shape
+                                 or residual.stride() != out.stride()):
+        raise ValueError("residual must be fp16 with the output's shape and strides")
     lib = _lib.load()
+    timing = CONV_TIMING
+    if timing is not None:
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
     _lib.check(lib.h3b_conv3d_i8(
         qx.data_ptr(), _lib.i64_array((b, d, h, w, c)), qweight.data_ptr(), o, kd, kh, kw, sd, sh, sw,
         x_scale.data_ptr(), weight_scale.data_ptr(), _ptr(bias), out.data_ptr(),
-        _lib.i64_array((out.stride(0), out.stride(2), out.stride(3), out.stride(4))), _ptr(acc_out),
-        int(causal_zero_frames), _stream(dev)))
+        _lib.i64_array((out.stride(0), out.stride(2), out.stride(3), out.stride(4))), _ptr(residual),
+        _ptr(acc_out), int(causal_zero_frames), _stream(dev)))
+    _count(1)
+    if timing is not None:
+        ev1.record()
+        timing.append((ev0, ev1, conv3d_int8_ops(b, c, do, ho, wo, o, (kd, kh, kw), causal_zero_frames)))
     return out
 
 
@@ -117,6 +151,7 @@ def quantize_tensor_i8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
     _lib.check(lib.h3b_quantize_tensor_i8(x.data_ptr(), _lib.i64_array(x.shape), _lib.i64_array(x.stride()),
                                           q.data_ptr(), scale.data_ptr(), ws.data_ptr(), ws_bytes, _stream(dev)))
+    _count(2)
     return q, scale
 
 
@@ -147,6 +182,7 @@ def norm_pad_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps
     _lib.check(lib.h3b_norm_pad_quant(x.data_ptr(), b, c, d, h, w, _ptr(pre_bias), gamma.data_ptr(),
                                       beta.data_ptr(), float(eps), q.data_ptr(), scale.data_ptr(), ws.data_ptr(),
                                       ws_bytes, _stream(dev)))
+    _count(4)
     return q, scale
 
 
@@ -159,6 +195,7 @@ def norm_pad_f16(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: 
     _lib.check(lib.h3b_norm_pad_f16(x.data_ptr(), b, c, d, h, w, _ptr(pre_bias), gamma.data_ptr(),
                                     beta.data_ptr(), float(eps), y.data_ptr(), ws.data_ptr(), ws_bytes,
                                     _stream(dev)))
+    _count(3)
     return y
 
 
@@ -174,6 +211,7 @@ def residual_pack(x: torch.Tensor, residual: torch.Tensor, bias: torch.Tensor) -
     y = torch.empty((b, c, d + 2, h + 1, w + 1), device=dev, dtype=F16, memory_format=torch.channels_last_3d)
     _lib.check(_lib.load().h3b_residual_pack(x.data_ptr(), residual.data_ptr(), bias.data_ptr(), b, c, d, h, w,
                                              y.data_ptr(), _stream(dev)))
+    _count(1)
     return y
 
 
@@ -194,6 +232,7 @@ def finalize_pixels(x: torch.Tensor, std: torch.Tensor, mean: torch.Tensor,
     _lib.check(_lib.load().h3b_finalize_pixels(x.data_ptr(), 1 if x.dtype == F16 else 0, _lib.i64_array(x.shape),
                                                _lib.i64_array(x.stride()), std.data_ptr(), mean.data_ptr(),
                                                out.data_ptr(), _stream(dev)))
+    _count(1)
     return out
 
 
@@ -230,6 +269,7 @@ def gemm_i8(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, weight_
     _lib.check(_lib.load().h3b_gemm_i8(q.data_ptr(), scale.data_ptr(), qweight.data_ptr(), weight_scale.data_ptr(),
                                        _ptr(bias), m, n, k, out.data_ptr(), out.stride(0), _ptr(acc_out),
                                        _stream(dev)))
+    _count(1)
     return out
 
 
@@ -253,6 +293,7 @@ def gemm_i8_swiglu(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, 
     _lib.check(_lib.load().h3b_gemm_i8_swiglu(q.data_ptr(), scale.data_ptr(), qweight.data_ptr(),
                                               weight_scale.data_ptr(), _ptr(bias), m, f, k, act.data_ptr(),
                                               _stream(dev)))
+    _count(1)
     return act
 
 
@@ -278,6 +319,7 @@ def gemm_i8_qkv_rope(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor
                                                 weight_scale.data_ptr(), _ptr(bias), batch, tokens, heads, k,
                                                 cos.data_ptr(), sin.data_ptr(), r, float(eps), qo.data_ptr(),
                                                 ko.data_ptr(), vo.data_ptr(), _stream(dev)))
+    _count(1)
     return qo, ko, vo
 
 
@@ -289,6 +331,7 @@ def row_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     q = torch.empty((m, k), device=dev, dtype=I8)
     s = torch.empty((m, 1), device=dev, dtype=F32)
     _lib.check(_lib.load().h3b_row_quant(x.data_ptr(), m, k, k, q.data_ptr(), s.data_ptr(), _stream(dev)))
+    _count(1)
     return q, s
 
 
@@ -303,6 +346,7 @@ def swiglu_quant(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     q = torch.empty((m, k), device=dev, dtype=I8)
     s = torch.empty((m, 1), device=dev, dtype=F32)
     _lib.check(_lib.load().h3b_swiglu_quant(x.data_ptr(), m, k, q.data_ptr(), s.data_ptr(), _stream(dev)))
+    _count(1)
     return q, s
 
 
@@ -326,6 +370,7 @@ def residual_rms_quant(x: torch.Tensor, a: torch.Tensor, g: torch.Tensor, w: tor
     _lib.check(_lib.load().h3b_residual_rms_quant(x.data_ptr(), a.data_ptr(), g.data_ptr(), w.data_ptr(), m, k,
                                                   float(eps), 1 if round_stats else 0, h.data_ptr(), q.data_ptr(),
                                                   s.data_ptr(), _ptr(norm), _stream(dev)))
+    _count(1)
     return (h, q, s, norm) if return_norm else (h, q, s)
 
 
@@ -337,6 +382,7 @@ def rms_norm_f16(x: torch.Tensor, gamma: torch.Tensor, eps: float) -> torch.Tens
     y = torch.empty_like(x, memory_format=torch.contiguous_format)
     _lib.check(_lib.load().h3b_rms_norm_f16(x.data_ptr(), gamma.data_ptr(), m, k, float(eps), y.data_ptr(),
                                             _stream(dev)))
+    _count(1)
     return y
 
 
@@ -349,6 +395,7 @@ def rms_quant(x: torch.Tensor, gamma: torch.Tensor, eps: float) -> tuple[torch.T
     s = torch.empty((m, 1), device=dev, dtype=F32)
     _lib.check(_lib.load().h3b_rms_quant(x.data_ptr(), gamma.data_ptr(), m, k, float(eps), q.data_ptr(),
                                          s.data_ptr(), _stream(dev)))
+    _count(1)
     return q, s
 
 
@@ -364,6 +411,7 @@ def final_residual_layernorm(h: torch.Tensor, o: torch.Tensor, gate: torch.Tenso
     _lib.check(_lib.load().h3b_final_residual_layernorm(h.data_ptr(), o.data_ptr(), gate.data_ptr(),
                                                         gamma.data_ptr(), beta.data_ptr(), m, k, float(eps),
                                                         y.data_ptr(), _stream(dev)))
+    _count(1)
     return y
 
 
@@ -383,6 +431,7 @@ def qk_rope(qkv: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, heads: int,
     k = torch.empty_like(q)
     _lib.check(_lib.load().h3b_qk_rope(qkv.data_ptr(), cos.data_ptr(), sin.data_ptr(), b, n, heads, r, float(eps),
                                        q.data_ptr(), k.data_ptr(), _stream(dev)))
+    _count(1)
     return q, k
 
 
@@ -407,4 +456,5 @@ def attention_f16(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: floa
     _lib.check(_lib.load().h3b_attention_f16(q.data_ptr(), strides(q), k.data_ptr(), strides(k), v.data_ptr(),
                                              strides(v), out.data_ptr(), strides(out), bsz, heads, sq, skv,
                                              float(scale), _stream(dev)))
+    _count(1)
     return out

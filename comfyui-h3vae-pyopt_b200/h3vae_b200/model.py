@@ -1,0 +1,419 @@
+"""H3-structured video VAE assembled from the sm_100a kernels.
+
+The reference wraps the external klvae model (video_vae.klvae, not distributed).  This module
+re-creates the parts of its structure that the INT8 hot path exercises, with random-init weights
+(no checkpoint is available), following the reference's block contracts:
+
+Encoder (ref: opt/encoder_fused_norm_bias.py:108-140, opt/encoder_fused_residual_pack.py:57-85,
+opt/encoder_int8_integration.py:32-52,350-459):
+  conv_in (fp16) -> stages of residual blocks
+     block: q1 = norm_pad_quant(x; GN1)           [temporal-isolated GroupNorm(32), SiLU, reflect/causal pad, INT8]
+            h  = conv1_i8(q1)                     [bias deferred: becomes GN2's pre_bias]
+            q2 = norm_pad_quant(h; GN2, pre_bias=b1)
+            y  = conv2_i8(q2) + b2 + shortcut(x)  [skip add fused in the conv epilogue]
+     a stage that downsamples ends with residual_pack(h, x, b2) feeding a strided fp16 conv
+  norm_out + SiLU + conv_out (fp16) -> quant_conv (1x1x1) -> moments (mean = first half).
+
+Decoder (ref: opt/int8_norm1_quant.py:185-252, opt/int8_ffn_up_fused.py:133-160,
+opt/decoder_fused_qk_rope.py:56-74, opt/decoder_final_norm.py:35-72):
+  conv_in (fp16) -> tokens; per block with the (h, out, scale2) carry:
+     norm1 producer (residual + RMSNorm + row INT8) -> INT8 QKV GEMM with fused QK RMSNorm + RoPE
+     -> fp16 attention -> row INT8 -> INT8 out-proj -> residual + RMSNorm + row INT8
+     -> INT8 FFN-up GEMM with fused SwiGLU -> row INT8 -> INT8 down-proj
+  final residual + LayerNorm -> causal conv3d upsampling stages (fp16) -> RGB.
+
+INT8 convolutions and linears run on the tcgen05 kernels; the fp16 convolutions outside the
+INT8 scope (conv_in, strided downsamples, 1x1x1 shortcuts, conv_out and the decoder's
+upsampling convs, which the reference also leaves in fp16) use cuDNN through torch.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+
+import torch
+import torch.nn.functional as F
+
+from . import kernels as K
+
+CL3 = torch.channels_last_3d
+
+
+# ---------------------------------------------------------------------------
+# Load-time weight quantizers (not on the timed path)
+# ---------------------------------------------------------------------------
+def prepare_int8_weight(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """[O,C,kd,kh,kw] -> int8 [O, kd*kh*kw*C] (tap-major, channel-minor) + fp32 per-channel scale
+    amax/127 (0 -> 1), round-half-even, clamp +-127.  ref: opt/encoder_int8.py:303-327."""
+    source = weight.detach().float().contiguous()
+    packed = source.permute(0, 2, 3, 4, 1).reshape(source.shape[0], -1)
+    scale = packed.abs().amax(dim=1).div(127.0)
+    scale = torch.where(scale > 0, scale, torch.ones_like(scale))
+    q = torch.round(packed / scale[:, None]).clamp(-127, 127).to(torch.int8)
+    return q.contiguous(), scale.float().contiguous()
+
+
+def quantize_rowwise_weight(weight: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Static per-output-row weight quantization (the comfy-kitchen rowwise contract the reference
+    uses): scale = max(amax/127, 1e-30), round, clamp [-128,127]; a zero row -> q 0, scale 1.
+    ref: opt/kitchen_int8.py:88-145, tests/test_kitchen_int8.py:19-26."""
+    w = weight.detach().float()
+    scale = (w.abs().amax(dim=-1, keepdim=True) / 127.0).clamp(min=1e-30)
+    q = (w / scale).round().clamp(-128, 127).to(torch.int8)
+    scale = scale.reshape(-1).contiguous()
+    zero = torch.all(w == 0, dim=1)
+    q = torch.where(zero[:, None], torch.zeros_like(q), q)
+    scale = torch.where(zero, torch.ones_like(scale), scale)
+    return q.contiguous(), scale.contiguous()
+
+
+# ---------------------------------------------------------------------------
+# fp16 helpers (cuDNN convolutions outside the INT8 scope)
+# ---------------------------------------------------------------------------
+def causal_reflect_pad(x: torch.Tensor) -> torch.Tensor:
+    """Reflect pad 1 in H/W, two zero frames in front (the causal 3x3x3 conv input)."""
+    x = F.pad(x, (1, 1, 1, 1, 0, 0), mode="reflect") if min(x.shape[-2:]) > 1 else F.pad(x, (1, 1, 1, 1, 0, 0))
+    return F.pad(x, (0, 0, 0, 0, 2, 0)).contiguous(memory_format=CL3)
+
+
+def conv_f16(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, stride=(1, 1, 1)) -> torch.Tensor:
+    return F.conv3d(x, w, b, stride=stride).contiguous(memory_format=CL3)
+
+
+def _randn(gen, shape, std, device, dtype=torch.float16):
+    return (torch.randn(*shape, generator=gen) * std).to(device=device, dtype=dtype)
+
+
+# ---------------------------------------------------------------------------
+# Encoder
+# ---------------------------------------------------------------------------
+@dataclass
+class EncoderConfig:
+    """Config 3 by default: stages 128/256/512/512, 2 residual blocks per stage, spatial /2 after
+    stages 1-3 and temporal /2 (causal) after stages 2-3, 16-channel latent."""
+    in_channels: int = 3
+    channels: tuple[int, ...] = (128, 256, 512, 512)
+    blocks_per_stage: int = 2
+    spatial_down: tuple[bool, ...] = (True, True, True, False)
+    temporal_down: tuple[bool, ...] = (False, True, True, False)
+    latent_channels: int = 16
+    groups: int = 32
+    eps: float = 1e-6
+    int8_stages: tuple[int, ...] = (0, 1, 2, 3)   # "reference" scope is (0, 1): the 8 prefix convs
+
+    @property
+    def spatial_ratio(self) -> int:
+        return 2 ** sum(self.spatial_down)
+
+    @property
+    def temporal_ratio(self) -> int:
+        return 2 ** sum(self.temporal_down)
+
+
+class _ResBlock:
+    def __init__(self, cin, cout, int8, gen, device, cfg: EncoderConfig):
+        self.cin, self.cout, self.int8, self.eps = cin, cout, int8, cfg.eps
+        std1 = 1.0 / math.sqrt(cin * 27)
+        std2 = 1.0 / math.sqrt(cout * 27)
+        self.gn1_w = (1.0 + 0.1 * torch.randn(cin, generator=gen)).half().to(device)
+        self.gn1_b = (0.1 * torch.randn(cin, generator=gen)).half().to(device)
+        self.gn2_w = (1.0 + 0.1 * torch.randn(cout, generator=gen)).half().to(device)
+        self.gn2_b = (0.1 * torch.randn(cout, generator=gen)).half().to(device)
+        self.w1 = _randn(gen, (cout, cin, 3, 3, 3), std1, device).contiguous(memory_format=CL3)
+        self.b1 = _randn(gen, (cout,), 0.02, device)
+        self.w2 = _randn(gen, (cout, cout, 3, 3, 3), std2, device).contiguous(memory_format=CL3)
+        self.b2 = _randn(gen, (cout,), 0.02, device)
+        self.nin_w = None
+        self.nin_b = None
+        if cin != cout:
+            self.nin_w = _randn(gen, (cout, cin, 1, 1, 1), 1.0 / math.sqrt(cin), device).contiguous(memory_format=CL3)
+            self.nin_b = _randn(gen, (cout,), 0.02, device)
+        if int8:
+            self.q1, self.s1 = prepare_int8_weight(self.w1)
+            self.q2, self.s2 = prepare_int8_weight(self.w2)
+
+    def shortcut(self, x):
+        if self.nin_w is None:
+            return x
+        return conv_f16(x, self.nin_w, self.nin_b)
+
+    def __call__(self, x: torch.Tensor, *, pack_for_downsample: bool) -> torch.Tensor:
+        """Returns the block output, or when pack_for_downsample the residual-packed (padded) tensor
+        [B,C,D+2,H+1,W+1] that the strided downsample conv consumes."""
+        skip = self.shortcut(x)
+        if self.int8:
+            q1, s1 = K.norm_pad_quant(x, self.gn1_w, self.gn1_b, self.eps)
+            h = K.conv3d_i8(q1, s1, self.q1, self.s1, None, (3, 3, 3), causal_zero_frames=2)
+            q2, s2 = K.norm_pad_quant(h, self.gn2_w, self.gn2_b, self.eps, pre_bias=self.b1)
+            if pack_for_downsample:
+                h2 = K.conv3d_i8(q2, s2, self.q2, self.s2, None, (3, 3, 3), causal_zero_frames=2)
+                return K.residual_pack(h2, skip, self.b2)
+            return K.conv3d_i8(q2, s2, self.q2, self.s2, self.b2, (3, 3, 3), causal_zero_frames=2, residual=skip)
+        y1 = K.norm_pad_f16(x, self.gn1_w, self.gn1_b, self.eps)
+        h = conv_f16(y1, self.w1, None)
+        y2 = K.norm_pad_f16(h, self.gn2_w, self.gn2_b, self.eps, pre_bias=self.b1)
+        if pack_for_downsample:
+            return K.residual_pack(conv_f16(y2, self.w2, None), skip, self.b2)
+        return (conv_f16(y2, self.w2, self.b2) + skip).contiguous(memory_format=CL3)
+
+
+class H3Encoder:
+    """Synthetic H3-structured causal video encoder (random init, seeded)."""
+
+    def __init__(self, cfg: EncoderConfig | None = None, device="cuda", seed: int = 0):
+        self.cfg = cfg = cfg or EncoderConfig()
+        gen = torch.Generator().manual_seed(seed)
+        c0 = cfg.channels[0]
+        self.conv_in_w = _randn(gen, (c0, cfg.in_channels, 3, 3, 3), 1.0 / math.sqrt(cfg.in_channels * 27),
+                                device).contiguous(memory_format=CL3)
+        self.conv_in_b = _randn(gen, (c0,), 0.02, device)
+        self.stages: list[list[_ResBlock]] = []
+        self.down: list[tuple | None] = []
+        cin = c0
+        for s, cout in enumerate(cfg.channels):
+            blocks = []
+            for j in range(cfg.blocks_per_stage):
+                blocks.append(_ResBlock(cin if j == 0 else cout, cout, s in cfg.int8_stages, gen, device, cfg))
+            cin = cout
+            self.stages.append(blocks)
+            if cfg.spatial_down[s] or cfg.temporal_down[s]:
+                stride = (2 if cfg.temporal_down[s] else 1, 2 if cfg.spatial_down[s] else 1,
+                          2 if cfg.spatial_down[s] else 1)
+                w = _randn(gen, (cout, cout, 3, 3, 3), 1.0 / math.sqrt(cout * 27), device).contiguous(memory_format=CL3)
+                self.down.append((w, _randn(gen, (cout,), 0.02, device), stride))
+            else:
+                self.down.append(None)
+        cl = cfg.channels[-1]
+        self.norm_out_w = (1.0 + 0.1 * torch.randn(cl, generator=gen)).half().to(device)
+        self.norm_out_b = (0.1 * torch.randn(cl, generator=gen)).half().to(device)
+        self.conv_out_w = _randn(gen, (2 * cfg.latent_channels, cl, 3, 3, 3), 1.0 / math.sqrt(cl * 27),
+                                 device).contiguous(memory_format=CL3)
+        self.conv_out_b = _randn(gen, (2 * cfg.latent_channels,), 0.02, device)
+        lc = 2 * cfg.latent_channels
+        self.quant_w = _randn(gen, (lc, lc, 1, 1, 1), 1.0 / math.sqrt(lc), device).contiguous(memory_format=CL3)
+        self.quant_b = _randn(gen, (lc,), 0.02, device)
+
+    @property
+    def int8_conv_count(self) -> int:
+        return sum(2 for blocks in self.stages for b in blocks if b.int8)
+
+    @torch.no_grad()
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """x: fp16 [B,3,T,H,W] ImageNet-normalized pixels of one causal clip -> moments
+        [B, 2*latent, T', H/ratio, W/ratio] (fp16)."""
+        if x.device.type != "cuda":
+            raise RuntimeError("H3Encoder requires CUDA input (no CPU fallback)")
+        h = conv_f16(causal_reflect_pad(x.half()), self.conv_in_w, self.conv_in_b)
+        for blocks, down in zip(self.stages, self.down):
+            for j, blk in enumerate(blocks):
+                last = j == len(blocks) - 1
+                h = blk(h, pack_for_downsample=last and down is not None)
+            if down is not None:
+                # h is the residual-packed [B,C,D+2,H+1,W+1] tensor: valid strided conv
+                w, b, stride = down
+                h = conv_f16(h, w, b, stride)
+        y = K.norm_pad_f16(h, self.norm_out_w, self.norm_out_b, self.cfg.eps)
+        moments = conv_f16(y, self.conv_out_w, self.conv_out_b)
+        return conv_f16(moments, self.quant_w, self.quant_b)
+
+
+# ---------------------------------------------------------------------------
+# Decoder
+# ---------------------------------------------------------------------------
+@dataclass
+class DecoderConfig:
+    """Config 4 by default: 16-ch latent, conv-in to hidden 1024, 6 blocks (16 heads x 64, FFN
+    2 x 4096 SwiGLU), then causal upsampling stages 512/256/128 to RGB."""
+    latent_channels: int = 16
+    hidden: int = 1024
+    heads: int = 16
+    blocks: int = 6
+    ffn: int = 4096
+    rot_dims: int = 48
+    up_channels: tuple[int, ...] = (512, 256, 128)
+    up_spatial: tuple[bool, ...] = (True, True, True)
+    up_temporal: tuple[bool, ...] = (True, True, False)
+    out_channels: int = 3
+    eps: float = 1e-5
+    qk_eps: float = 1e-6
+    gn_eps: float = 1e-6
+
+
+def rope_tables(t: int, h: int, w: int, rot_dims: int, device, base: float = 10000.0):
+    """3-axis rotary tables over a (t, h, w) token grid: the first rot_dims dims of each head are
+    split evenly over the three axes (rot_dims/3 dims, rot_dims/6 frequencies each) in the
+    rotate-half convention (pairs d, d + rot_dims/2).  Returns cos, sin fp16 [t*h*w, rot_dims]."""
+    if rot_dims == 0:
+        z = torch.empty(t * h * w, 0, dtype=torch.float16, device=device)
+        return z, z
+    assert rot_dims % 6 == 0
+    nf = rot_dims // 6
+    inv = 1.0 / (base ** (torch.arange(nf, dtype=torch.float64) / nf))
+    tt, hh, ww = torch.meshgrid(torch.arange(t), torch.arange(h), torch.arange(w), indexing="ij")
+    angles = torch.cat([p.reshape(-1, 1).double() * inv for p in (tt, hh, ww)], dim=1)  # [n, rot/2]
+    angles = torch.cat([angles, angles], dim=1)
+    return angles.cos().half().to(device), angles.sin().half().to(device)
+
+
+class _DecoderBlock:
+    def __init__(self, cfg: DecoderConfig, gen, device):
+        d, f, H = cfg.hidden, cfg.ffn, cfg.heads
+        assert d == H * 64
+        std = 0.02
+        self.norm1_w = (1.0 + 0.1 * torch.randn(d, generator=gen)).half().to(device)
+        self.norm2_w = (1.0 + 0.1 * torch.randn(d, generator=gen)).half().to(device)
+        self.scale1 = (0.5 + 0.1 * torch.randn(d, generator=gen)).half().to(device)
+        self.scale2 = (0.5 + 0.1 * torch.randn(d, generator=gen)).half().to(device)
+        # to_qkv rows are laid out per head as [q(64) | k(64) | v(64)]
+        self.qkv_w = _randn(gen, (3 * d, d), std, device)
+        self.qkv_b = _randn(gen, (3 * d,), std, device)
+        self.out_w = _randn(gen, (d, d), std, device)
+        self.out_b = _randn(gen, (d,), std, device)
+        self.up_w = _randn(gen, (2 * f, d), std, device)      # rows 0..f-1 gate, f..2f-1 up
+        self.up_b = _randn(gen, (2 * f,), std, device)
+        self.down_w = _randn(gen, (d, f), std, device)
+        self.down_b = _randn(gen, (d,), std, device)
+        self.qkv_q, self.qkv_s = quantize_rowwise_weight(self.qkv_w)
+        self.out_q, self.out_s = quantize_rowwise_weight(self.out_w)
+        self.up_q, self.up_s = quantize_rowwise_weight(self.up_w)
+        self.down_q, self.down_s = quantize_rowwise_weight(self.down_w)
+
+
+class H3Decoder:
+    """Synthetic H3-structured decoder (random init, seeded).  int8=True runs the fused INT8 block
+    chain (the int8_decode + decode_fusions profile); int8=False runs the fp16 profile: cuBLAS fp16
+    linears and PyTorch SDPA around the fused QK RMSNorm + RoPE and RMSNorm kernels."""
+
+    def __init__(self, cfg: DecoderConfig | None = None, device="cuda", seed: int = 1, int8: bool = True):
+        self.cfg = cfg = cfg or DecoderConfig()
+        self.int8 = bool(int8)
+        gen = torch.Generator().manual_seed(seed)
+        self.device = torch.device(device)
+        lc, d = cfg.latent_channels, cfg.hidden
+        self.conv_in_w = _randn(gen, (d, lc, 3, 3, 3), 1.0 / math.sqrt(lc * 27), device).contiguous(memory_format=CL3)
+        self.conv_in_b = _randn(gen, (d,), 0.02, device)
+        self.blocks = [_DecoderBlock(cfg, gen, device) for _ in range(cfg.blocks)]
+        self.ln_w = (1.0 + 0.1 * torch.randn(d, generator=gen)).half().to(device)
+        self.ln_b = (0.1 * torch.randn(d, generator=gen)).half().to(device)
+        self.up = []
+        cin = d
+        for cout in cfg.up_channels:
+            gw = (1.0 + 0.1 * torch.randn(cin, generator=gen)).half().to(device)
+            gb = (0.1 * torch.randn(cin, generator=gen)).half().to(device)
+            w = _randn(gen, (cout, cin, 3, 3, 3), 1.0 / math.sqrt(cin * 27), device).contiguous(memory_format=CL3)
+            b = _randn(gen, (cout,), 0.02, device)
+            self.up.append((gw, gb, w, b))
+            cin = cout
+        self.out_gn_w = (1.0 + 0.1 * torch.randn(cin, generator=gen)).half().to(device)
+        self.out_gn_b = (0.1 * torch.randn(cin, generator=gen)).half().to(device)
+        self.conv_out_w = _randn(gen, (cfg.out_channels, cin, 3, 3, 3), 1.0 / math.sqrt(cin * 27),
+                                 device).contiguous(memory_format=CL3)
+        self.conv_out_b = _randn(gen, (cfg.out_channels,), 0.02, device)
+        self._rope_cache: dict = {}
+
+    @property
+    def spatial_ratio(self) -> int:
+        return 2 ** sum(self.cfg.up_spatial)
+
+    @property
+    def temporal_ratio(self) -> int:
+        return 2 ** sum(self.cfg.up_temporal)
+
+    def frames_for(self, tokens_t: int) -> int:
+        f = tokens_t
+        for up in self.cfg.up_temporal:
+            if up:
+                f = 1 + 2 * (f - 1)
+        return f
+
+    def _rope(self, b, t, h, w):
+        key = (t, h, w)
+        if key not in self._rope_cache:
+            self._rope_cache[key] = rope_tables(t, h, w, self.cfg.rot_dims, self.device)
+        cos, sin = self._rope_cache[key]
+        n = t * h * w
+        return (cos.view(1, n, 1, -1).expand(b, n, 1, cos.shape[-1]).contiguous(),
+                sin.view(1, n, 1, -1).expand(b, n, 1, sin.shape[-1]).contiguous())
+
+    def transformer_fp16(self, x: torch.Tensor, grid: tuple[int, int, int]) -> torch.Tensor:
+        """fp16 profile of the block chain (ref: opt/int8_norm_quant.py:106-124 block structure with
+        the fp16 linears of the default decoder)."""
+        cfg = self.cfg
+        b, n, d = x.shape
+        cos, sin = self._rope(b, *grid)
+        x = x.reshape(b * n, d).contiguous()
+        for blk in self.blocks:
+            n1 = K.rms_norm_f16(x, blk.norm1_w, cfg.eps)
+            qkv = F.linear(n1, blk.qkv_w, blk.qkv_b).view(b, n, 3 * d)
+            q, k = K.qk_rope(qkv, cos, sin, cfg.heads, cfg.qk_eps)
+            v = qkv.view(b, n, cfg.heads, 192)[..., 128:]
+            y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
+                                               scale=1.0 / 8.0)
+            a = F.linear(y.transpose(1, 2).reshape(b * n, d), blk.out_w, blk.out_b)
+            h = torch.addcmul(x.float(), a.float(), blk.scale1.float()).half()
+            n2 = K.rms_norm_f16(h, blk.norm2_w, cfg.eps)
+            ff = F.linear(n2, blk.up_w, blk.up_b).float()
+            g, u = ff[:, : cfg.ffn], ff[:, cfg.ffn:]
+            act = (g.half().float() * torch.sigmoid(g.half().float()) * u.half().float()).half()
+            out = F.linear(act, blk.down_w, blk.down_b)
+            x = torch.addcmul(h.float(), out.float(), blk.scale2.float()).half()
+        y = F.layer_norm(x.float(), (d,), self.ln_w.float(), self.ln_b.float(), cfg.eps).half()
+        return y.view(b, n, d)
+
+    def transformer(self, x: torch.Tensor, grid: tuple[int, int, int]) -> torch.Tensor:
+        """x: fp16 [B, n, hidden] tokens -> fp16 [B, n, hidden] after the blocks and final LayerNorm."""
+        if not self.int8:
+            return self.transformer_fp16(x, grid)
+        cfg = self.cfg
+        b, n, d = x.shape
+        cos, sin = self._rope(b, *grid)
+        x = x.reshape(b * n, d).contiguous()
+        h_state = x
+        out = None
+        prev_scale2 = None
+        for i, blk in enumerate(self.blocks):
+            if i == 0:
+                q1, s1 = K.rms_quant(x, blk.norm1_w, cfg.eps)
+            else:
+                # norm1 producer: x = h + out * scale2 (in place), RMSNorm, row INT8
+                h_state, q1, s1 = K.residual_rms_quant(h_state, out, prev_scale2, blk.norm1_w, cfg.eps, h_out=h_state)
+                x = h_state
+            q, k, v = K.gemm_i8_qkv_rope(q1, s1, blk.qkv_q, blk.qkv_s, blk.qkv_b, b, n, cfg.heads, cos, sin,
+                                         cfg.qk_eps)
+            y = K.attention_f16(q, k, v, 1.0 / 8.0)            # [B, n, H, 64] storage
+            qy, sy = K.row_quant(y.transpose(1, 2).reshape(b * n, d))
+            a = K.gemm_i8(qy, sy, blk.out_q, blk.out_s, blk.out_b)
+            h_state, q2, s2 = K.residual_rms_quant(x, a, blk.scale1, blk.norm2_w, cfg.eps)
+            act = K.gemm_i8_swiglu(q2, s2, blk.up_q, blk.up_s, blk.up_b)
+            qf, sf = K.row_quant(act)
+            out = K.gemm_i8(qf, sf, blk.down_q, blk.down_s, blk.down_b)
+            prev_scale2 = blk.scale2
+        y = K.final_residual_layernorm(h_state, out, prev_scale2, self.ln_w, self.ln_b, cfg.eps)
+        return y.view(b, n, d)
+
+    @torch.no_grad()
+    def __call__(self, z: torch.Tensor) -> torch.Tensor:
+        """z: fp16 [B, latent, t, h, w] -> raw decoder output fp16 [B, 3, T, H, W] (before finalize)."""
+        if z.device.type != "cuda":
+            raise RuntimeError("H3Decoder requires CUDA input (no CPU fallback)")
+        cfg = self.cfg
+        b, _, t, h, w = z.shape
+        feat = conv_f16(causal_reflect_pad(z.half()), self.conv_in_w, self.conv_in_b)   # NDHWC [B,d,t,h,w]
+        tokens = feat.permute(0, 2, 3, 4, 1).reshape(b, t * h * w, cfg.hidden)        # a view of NDHWC storage
+        y = self.transformer(tokens, (t, h, w))
+        x = y.view(b, t, h, w, cfg.hidden).permute(0, 4, 1, 2, 3)                      # NDHWC logical [B,d,t,h,w]
+        for (gw, gb, wt, bs), sp, tp in zip(self.up, cfg.up_spatial, cfg.up_temporal):
+            x = conv_f16(K.norm_pad_f16(x, gw, gb, cfg.gn_eps), wt, bs)
+            x = upsample(x, temporal=tp, spatial=sp)
+        x = conv_f16(K.norm_pad_f16(x, self.out_gn_w, self.out_gn_b, cfg.gn_eps), self.conv_out_w, self.conv_out_b)
+        return x
+
+
+def upsample(x: torch.Tensor, *, temporal: bool, spatial: bool) -> torch.Tensor:
+    """Nearest x2 spatial upsampling and causal x2 temporal upsampling (frame 0 kept once, every
+    later frame repeated: t -> 1 + 2 (t - 1)), NDHWC in and out."""
+    if temporal and x.shape[2] > 1:
+        x = torch.cat([x[:, :, :1], x[:, :, 1:].repeat_interleave(2, dim=2)], dim=2)
+    if spatial:
+        x = x.repeat_interleave(2, dim=3).repeat_interleave(2, dim=4)
+    return x.contiguous(memory_format=CL3)

@@ -57,6 +57,8 @@ int h3b_device_error(unsigned int* bits, int clear);
  *   x_scale   fp32 scalar (per-tensor activation scale, device pointer)
  *   w_scale   fp32 [O];  bias fp16 [O] or NULL
  *   out       fp16, element strides out_strides = {sB, sD, sH, sW}
+ *   residual  optional fp16 tensor with the strides of out: out = fp16(fp16(conv) + residual),
+ *             the residual block's `x + h` (ref: opt/encoder_fused_norm_bias.py:140) fused in
  *   acc_out   optional int32 [B, Do, Ho, Wo, O] contiguous raw accumulators
  *   causal_zero_frames: 2 when the producer guarantees that input frames 0
  *     and 1 are exact zeros (the causal pad); the kernel then skips the
@@ -66,7 +68,7 @@ int h3b_device_error(unsigned int* bits, int clear);
 int h3b_conv3d_i8(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int64_t out_channels,
                   int kd, int kh, int kw, int sd, int sh, int sw, const float* x_scale,
                   const float* w_scale, const void* bias, void* out, const int64_t* out_strides,
-                  int32_t* acc_out, int causal_zero_frames, h3b_stream_t stream);
+                  const void* residual, int32_t* acc_out, int causal_zero_frames, h3b_stream_t stream);
 
 /* ---- (a2) per-tensor activation quantization ---------------------------- */
 

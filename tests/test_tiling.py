@@ -1,0 +1,62 @@
+"""Tile planner, overlap blend and GPU work split (CPU)."""
+import json
+
+import pytest
+import torch
+
+from h3vae_b200 import tiling
+
+
+def test_split_matches_reference_goldens(golden):
+    for c in json.loads(bytes(golden["split_tiles_json"]).decode()):
+        assert tiling.split_tiles(*c["case"]) == (c["starts"], c["sizes"], c["overlaps"])
+    for conf, h, w, expect in golden["select_tile"].tolist():
+        assert tiling.select_encoder_tile(conf, h, w) == expect
+
+
+def test_split_rejects_tile_not_larger_than_overlap():
+    with pytest.raises(ValueError):
+        tiling.split_tiles(768, 64, 64, 16)
+
+
+@pytest.mark.parametrize("h,w,tile,ov,ratio", [(768, 1344, 256, 32, 8), (96, 160, 64, 16, 2), (300, 257, 128, 24, 4),
+                                               (64, 64, 64, 16, 2)])
+def test_weighted_accumulation_equals_sequential_blend(h, w, tile, ov, ratio):
+    plan = tiling.TilePlan.build(h, w, tile, ov, ratio)
+    g = torch.Generator().manual_seed(h + w)
+    tiles = {(i, j): torch.randn(2, plan.hs[i], plan.ws[j], generator=g, dtype=torch.float64) for i, j in plan.tiles()}
+    ref = tiling.blend_sequential(tiles, plan)
+    canvas = torch.zeros(2, plan.height, plan.width, dtype=torch.float64)
+    for (i, j), t in tiles.items():
+        tiling.accumulate_tile(canvas, t, plan, i, j)
+    assert ref.shape == canvas.shape == (2, h, w)
+    assert torch.allclose(ref, canvas, atol=1e-12)
+
+
+def test_weights_partition_unity():
+    plan = tiling.TilePlan.build(768, 1344, 256, 32, 8)
+    canvas = torch.zeros(768, 1344, dtype=torch.float64)
+    for i, j in plan.tiles():
+        tiling.accumulate_tile(canvas, torch.ones(plan.hs[i], plan.ws[j], dtype=torch.float64), plan, i, j)
+    assert torch.allclose(canvas, torch.ones_like(canvas))
+    assert (plan.rows, plan.cols) == (4, 6)
+
+
+def test_scaled_plan_in_latent_units():
+    plan = tiling.TilePlan.build(768, 1344, 256, 32, 8)
+    lp = plan.scaled(8)
+    assert lp.height == 96 and lp.width == 168 and lp.hs[0] == 32
+    with pytest.raises(ValueError):
+        tiling.TilePlan.build(768, 1344, 256, 32, 8).scaled(7)
+
+
+@pytest.mark.parametrize("n,world", [(48, 1), (48, 2), (48, 8), (49, 4), (3, 8), (0, 2)])
+def test_shard_range_partitions(n, world):
+    seen = []
+    sizes = []
+    for r in range(world):
+        rr = tiling.shard_range(n, world, r)
+        seen.extend(rr)
+        sizes.append(len(rr))
+    assert seen == list(range(n))
+    assert max(sizes) - min(sizes) <= 1
