@@ -278,9 +278,13 @@ def main():
     video = synthetic_video(dev) if rank == 0 else None
     torch.cuda.synchronize()
 
+    def fp16(lat):
+        # ComfyUI hands latents to the VAE in its working dtype (fp16 for the INT8 modes)
+        return None if lat is None else lat.half()
+
     def step(x):
         lat = runtime.encode(x)
-        return lat, runtime.decode(lat)
+        return lat, runtime.decode(fp16(lat))
 
     for _ in range(args.warmup):
         step(video)
@@ -298,7 +302,7 @@ def main():
             e0.record(stream)
             lat = runtime.encode(video)
             e1.record(stream)
-            runtime.decode(lat)
+            runtime.decode(fp16(lat))
             e2.record(stream)
             torch.cuda.synchronize()
             enc_ms.append(e0.elapsed_time(e1))
@@ -344,7 +348,7 @@ def main():
             t1 = torch.cuda.Event(enable_timing=True)
             t0.record(stream)
             lat = runtime.encode(host_video)
-            pix = runtime.decode(lat)
+            pix = runtime.decode(fp16(lat))
             if rank == 0:
                 host_out.copy_(pix, non_blocking=True)
             t1.record(stream)
