@@ -49,6 +49,9 @@ def parse_args():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=("video", "tile"), default="video",
+                    help="video: the config-5 round trip (the bench line); tile: one config-3 encoder call and "
+                         "one config-4 decoder call per step (small enough for ncu captures)")
     return ap.parse_args()
 
 
@@ -261,10 +264,42 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_tile(args):
+    """One config-3 encoder call ([4,3,17,256,256]) + one config-4 decoder call ([4,16,5,32,32]) per
+    step through the model objects (no tiling / blend); prints per-call milliseconds."""
+    from h3vae_b200.runtime import H3VAEPyOptRuntime
+    torch.cuda.set_device(0)
+    rt = H3VAEPyOptRuntime(int8_encode=True, int8_decode=True, decode_fusions=True, log_calls=False,
+                           compile_decoder=False, compile_encoder=False)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.rand((4, 3, 17, 256, 256), generator=g, device="cuda") * 2 - 1).half()
+    z = torch.randn((4, 16, 5, 32, 32), generator=g, device="cuda").half()
+    for _ in range(args.warmup):
+        rt.encoder(x)
+        rt.decoder(z)
+    torch.cuda.synchronize()
+    enc, dec = [], []
+    for _ in range(args.steps):
+        e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+        e0.record()
+        rt.encoder(x)
+        e1.record()
+        rt.decoder(z)
+        e2.record()
+        torch.cuda.synchronize()
+        enc.append(e0.elapsed_time(e1))
+        dec.append(e1.elapsed_time(e2))
+    print(json.dumps({"workload": "tile", "encoder_tile_ms": statistics.mean(enc),
+                      "decoder_tile_ms": statistics.mean(dec), "steps": args.steps, "warmup": args.warmup}))
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         run_reference(args)
+        return
+    if args.workload == "tile":
+        run_tile(args)
         return
     from h3vae_b200 import kernels as K
     from h3vae_b200.runtime import H3VAEPyOptRuntime

@@ -36,6 +36,9 @@ _SIGNATURES = {
                                    c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "h3b_norm_pad_f16": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                  c_void_p, c_float, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "h3b_upsample_norm_pad_f16": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,
+                                          c_void_p, c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_size_t,
+                                          c_void_p]),
     "h3b_residual_pack": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64,
                                   c_void_p, c_void_p]),
     "h3b_gemm_i8": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,

@@ -260,6 +260,30 @@ __device__ __forceinline__ int8_t quant_half_away(float x, float scale) {
   return static_cast<int8_t>(static_cast<int>(r));
 }
 
+// quant_half_away with the quotient formed by the precomputed reciprocal.  The
+// reciprocal product differs from the correctly rounded quotient by < 2^-22
+// relative (|q| <= 127.5 here), so only quotients within 2^-13 of a rounding
+// boundary k + 0.5 are recomputed with the exact division: the result is
+// identical to quant_half_away for every input (NaN and inf included).
+__device__ __forceinline__ int8_t quant_half_away_fast(float x, float scale, float inv_scale) {
+  float s = __fmul_rn(x, inv_scale);
+  const float a = fabsf(s);
+  if (fabsf(__fsub_rn(__fsub_rn(a, floorf(a)), 0.5f)) < (1.0f / 8192.0f)) s = __fdiv_rn(x, scale);
+  float r = (s >= 0.0f) ? floorf(__fadd_rn(s, 0.5f)) : -floorf(__fadd_rn(-s, 0.5f));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return static_cast<int8_t>(static_cast<int>(r));
+}
+
+// Order-preserving map of fp32 to uint32 (for atomicMin/atomicMax of signed
+// floats): non-negative values set the top bit, negative values are inverted.
+__device__ __forceinline__ unsigned int float_to_ordered(float f) {
+  const unsigned int u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float ordered_to_float(unsigned int u) {
+  return __uint_as_float((u & 0x80000000u) ? (u & 0x7fffffffu) : ~u);
+}
+
 // Row quantization rule of the decoder's INT8 linears: divide in fp32 by the
 // fp16-rounded scale, round the quotient to fp16, then to nearest-even,
 // NaN -> -128, clamp to [-128, 127].
@@ -296,30 +320,60 @@ __device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
 // QK RMSNorm (fp32 statistics, no affine) + fp16 round + rotate-half rotary
 // embedding on the first R dims of one 64-wide head vector held in registers.
 // Products are rounded to fp16 individually before the fp32 sum, and the sum
-// is rounded to fp16 on store.  dst must be 16-byte aligned.
-__device__ __forceinline__ void qk_norm_rope_store(float (&x)[64], float eps, int R, const __half* cs,
-                                                   const __half* sn, __half* dst) {
+// is rounded to fp16 on store.  R is a compile-time constant so the vector
+// stays in registers; cos/sin rows and dst must be 16-byte aligned.
+template <int R>
+__device__ __forceinline__ void qk_norm_rope_store_t(float (&x)[64], float eps, const __half* cs, const __half* sn,
+                                                     __half* dst) {
   float ss = 0.0f;
 #pragma unroll
   for (int d = 0; d < 64; ++d) ss = __fmaf_rn(x[d], x[d], ss);
   const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / 64.0f), eps));
 #pragma unroll
   for (int d = 0; d < 64; ++d) x[d] = round_fp16(__fmul_rn(x[d], inv));
-  const int half_r = R >> 1;
+  float c[R > 0 ? R : 1], sv[R > 0 ? R : 1];
+#pragma unroll
+  for (int q = 0; q < R / 8; ++q) {
+    const uint4 rc = reinterpret_cast<const uint4*>(cs)[q];
+    const uint4 rs = reinterpret_cast<const uint4*>(sn)[q];
+    const __half2* hc = reinterpret_cast<const __half2*>(&rc);
+    const __half2* hs = reinterpret_cast<const __half2*>(&rs);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 fc = __half22float2(hc[j]);
+      const float2 fs = __half22float2(hs[j]);
+      c[q * 8 + 2 * j] = fc.x;
+      c[q * 8 + 2 * j + 1] = fc.y;
+      sv[q * 8 + 2 * j] = fs.x;
+      sv[q * 8 + 2 * j + 1] = fs.y;
+    }
+  }
   __align__(16) __half outv[64];
 #pragma unroll
   for (int d = 0; d < 64; ++d) {
     float o = x[d];
     if (d < R) {
-      const float rot = (d < half_r) ? -x[d + half_r] : x[d - half_r];
-      const float a = round_fp16(__fmul_rn(x[d], __half2float(cs[d])));
-      const float b = round_fp16(__fmul_rn(rot, __half2float(sn[d])));
+      const float rot = (d < R / 2) ? -x[(d + R / 2) % 64] : x[(d + 64 - R / 2) % 64];
+      const float a = round_fp16(__fmul_rn(x[d], c[d % (R > 0 ? R : 1)]));
+      const float b = round_fp16(__fmul_rn(rot, sv[d % (R > 0 ? R : 1)]));
       o = __fadd_rn(a, b);
     }
     outv[d] = __float2half_rn(o);
   }
 #pragma unroll
   for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(dst)[q] = reinterpret_cast<const uint4*>(outv)[q];
+}
+
+// Runtime-R dispatch over the supported rotary widths {0, 16, 32, 48, 64}.
+__device__ __forceinline__ void qk_norm_rope_store(float (&x)[64], float eps, int R, const __half* cs,
+                                                   const __half* sn, __half* dst) {
+  switch (R) {
+    case 48: qk_norm_rope_store_t<48>(x, eps, cs, sn, dst); break;
+    case 64: qk_norm_rope_store_t<64>(x, eps, cs, sn, dst); break;
+    case 32: qk_norm_rope_store_t<32>(x, eps, cs, sn, dst); break;
+    case 16: qk_norm_rope_store_t<16>(x, eps, cs, sn, dst); break;
+    default: qk_norm_rope_store_t<0>(x, eps, cs, sn, dst); break;
+  }
 }
 
 }  // namespace h3b

@@ -431,7 +431,10 @@ int h3b_qk_rope(const void* qkv, const void* cos_t, const void* sin_t, int64_t b
   if (!qkv || !q_out || !k_out || (rot_dims > 0 && (!cos_t || !sin_t)))
     return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
   if (batch <= 0 || tokens <= 0 || heads <= 0) return h3b_host::set_error(H3B_EINVAL, "%s: empty input", name);
-  if (rot_dims < 0 || rot_dims > 64 || rot_dims % 2) return h3b_host::set_error(H3B_EINVAL, "%s: bad rotary dims", name);
+  if (rot_dims != 0 && rot_dims != 16 && rot_dims != 32 && rot_dims != 48 && rot_dims != 64)
+    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: rotary dims must be one of 0, 16, 32, 48, 64", name);
+  if (rot_dims > 0 && ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t)) & 15u))
+    return h3b_host::set_error(H3B_EINVAL, "%s: cos/sin tables must be 16-byte aligned", name);
   for (const void* p : std::initializer_list<const void*>{qkv, q_out, k_out})
     if (!al16(p)) return h3b_host::set_error(H3B_EINVAL, "%s: tensors must be 16-byte aligned", name);
   const int64_t rows = batch * tokens;

@@ -21,13 +21,18 @@ constexpr int kGroups = 32;
 constexpr int kVec = 8;            // fp16 channels per thread vector
 constexpr int kPackThreads = 256;
 constexpr int kStatThreads = 256;
-constexpr int kStatValuesPerThread = 64;  // 8 vectors of 8 channels
-constexpr int kStatElemsPerCta = kStatThreads * kStatValuesPerThread;
+constexpr int kStatVecsPerThread = 64;    // 16-byte vectors each thread streams per chunk
+constexpr int kStatElemsPerCta = kStatThreads * kStatVecsPerThread * kVec;
 
 struct NormShape {
-  int B, C, D, H, W;
+  int B, C, D, H, W;        // the stored (source) tensor
   int positions_per_chunk;  // P
   int nchunks;              // ceil(H*W / P)
+  // Optional nearest upsampling folded into the producer (fp16 mode only):
+  // the normalized tensor is up(x) with spatial factor us (1 or 2) and causal
+  // temporal doubling ut (0 or 1: frame 0 once, every later frame twice).
+  int us, ut;
+  int Du, Hu, Wu;           // logical (upsampled) frame / row / column counts
 };
 
 __device__ __forceinline__ void load_h8(const __half* src, float (&v)[8]) {
@@ -49,16 +54,77 @@ __device__ __forceinline__ void store_h8(__half* dst, const float (&v)[8]) {
 }
 
 // ---------------------------------------------------------------------------
-// GroupNorm statistics, pass 1: chunk partials.
+// GroupNorm statistics, pass 1: chunk partials (+ per-channel min / max).
 // grid = (nchunks, B*D), block = 256.  The chunk covers P = 16384 / C positions
 // of one (b, frame); thread tid owns channel vector v = tid % (C/8) and the
-// positions tid / (C/8) + k * (256 / (C/8)).
+// positions tid / (C/8) + k * (256 / (C/8)).  Per-channel values are combined
+// across the threads that share v with shuffles, then across warps in shared
+// memory.
 // ---------------------------------------------------------------------------
+// Combine a[8] (per-channel values of this thread's vector) over all threads
+// holding the same channel vector; result for channel c lands in chan[c].
+// kind 0 = sum, 1 = min, 2 = max.
+template <int KIND>
+__device__ __forceinline__ void channel_reduce(float (&a)[8], int vpp, int C, float* red, float* chan) {
+  auto op = [](float x, float y) { return KIND == 0 ? __fadd_rn(x, y) : (KIND == 1 ? fminf(x, y) : fmaxf(x, y)); };
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (vpp < 32) {
+    for (int o = 16; o >= vpp; o >>= 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) a[j] = op(a[j], __shfl_xor_sync(0xffffffffu, a[j], o));
+    }
+  }
+  __syncthreads();  // previous users of red / chan are done
+  if (lane < (vpp < 32 ? vpp : 32)) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) red[(warp * 32 + lane) * 8 + j] = a[j];
+  }
+  __syncthreads();
+  const int nwarps = kStatThreads / 32;
+  for (int c = threadIdx.x; c < C; c += kStatThreads) {
+    const int v = c >> 3, j = c & 7;
+    float acc;
+    if (vpp <= 32) {
+      acc = red[v * 8 + j];
+      for (int w = 1; w < nwarps; ++w) acc = op(acc, red[(w * 32 + v) * 8 + j]);
+    } else {
+      const int step = vpp / 32;
+      int w = v / 32;
+      acc = red[(w * 32 + (v & 31)) * 8 + j];
+      for (w += step; w < nwarps; w += step) acc = op(acc, red[(w * 32 + (v & 31)) * 8 + j]);
+    }
+    chan[c] = acc;
+  }
+  __syncthreads();
+}
+
+// (count, mean, M2) of a set of samples; Chan's pairwise merge.
+struct Moments {
+  float n, mean, m2;
+};
+
+__device__ __forceinline__ Moments merge_moments(Moments a, Moments b) {
+  if (b.n == 0.0f) return a;
+  if (a.n == 0.0f) return b;
+  const float n = a.n + b.n;
+  const float d = b.mean - a.mean;
+  const float f = __fdiv_rn(b.n, n);
+  return Moments{n, __fmaf_rn(d, f, a.mean), a.m2 + b.m2 + d * d * a.n * f};
+}
+
+// Streams one chunk of positions of one (b, frame): every thread keeps, per
+// channel of its vector, a shift (its first sample), the shifted sum and sum
+// of squares, and the running min / max.  The shifted sums become per-thread
+// (n, mean, M2) per group, merged per group in shared memory with Chan's
+// formula; the chunk's (mean, M2) per group goes to `partials`.
 __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* __restrict__ x,
                                                                   const __half* __restrict__ pre_bias,
-                                                                  NormShape s, float2* __restrict__ partials) {
+                                                                  NormShape s, float2* __restrict__ partials,
+                                                                  unsigned int* __restrict__ cmin,
+                                                                  unsigned int* __restrict__ cmax) {
   __shared__ float red[kStatThreads * kVec];
-  __shared__ float group_mean[kGroups];
+  __shared__ float chan[2048];
+  __shared__ Moments slots[kStatThreads][8];
   const int tid = threadIdx.x;
   const int chunk = blockIdx.x;
   const int bt = blockIdx.y;
@@ -75,70 +141,91 @@ __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* 
   if (pre_bias != nullptr) load_h8(pre_bias + c0, pb);
 
   const __half* base = x + (static_cast<int64_t>(bt) * HW + p0) * s.C + c0;
-  float vals[kStatValuesPerThread];
-  int nvec = 0;
-  float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  float shift[8], s1[8], s2[8], mn[8], mx[8];
+  int n = 0;
 #pragma unroll
-  for (int k = 0; k < kStatValuesPerThread / kVec; ++k) {
-    const int p = tid / vpp + k * pos_per_iter;
-    float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (p < valid_pos) {
-      load_h8(base + static_cast<int64_t>(p) * s.C, f);
-      if (pre_bias != nullptr) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
-      }
-      ++nvec;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sum[j] = __fadd_rn(sum[j], f[j]);
-    }
-#pragma unroll
-    for (int j = 0; j < 8; ++j) vals[k * 8 + j] = f[j];
+  for (int j = 0; j < 8; ++j) {
+    shift[j] = 0.0f; s1[j] = 0.0f; s2[j] = 0.0f;
+    mn[j] = INFINITY; mx[j] = -INFINITY;
   }
-  // Per-channel chunk sums -> per-group sums.
+#pragma unroll 4
+  for (int p = tid / vpp; p < valid_pos; p += pos_per_iter) {
+    float f[8];
+    load_h8(base + static_cast<int64_t>(p) * s.C, f);
+    if (pre_bias != nullptr) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) red[tid * 8 + j] = sum[j];
+      for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
+    }
+    if (n == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) shift[j] = f[j];
+    }
+    ++n;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float d = f[j] - shift[j];
+      s1[j] += d;
+      s2[j] = __fmaf_rn(d, d, s2[j]);
+      mn[j] = fminf(mn[j], f[j]);
+      mx[j] = fmaxf(mx[j], f[j]);
+    }
+  }
+  // Per-thread moments per group slot (a vector holds 8 / cg groups when cg < 8).
+  const int nslots = cg >= 8 ? 1 : 8 / cg;
+  const int per_slot = 8 / nslots;
+  const float fn = static_cast<float>(n);
+#pragma unroll
+  for (int sl = 0; sl < 8; ++sl) {
+    if (sl >= nslots) break;
+    Moments acc{0.0f, 0.0f, 0.0f};
+    for (int j = sl * per_slot; j < (sl + 1) * per_slot; ++j) {
+      Moments m{fn, 0.0f, 0.0f};
+      if (n > 0) {
+        const float mu = __fdiv_rn(s1[j], fn);
+        m.mean = shift[j] + mu;
+        m.m2 = fmaxf(s2[j] - s1[j] * mu, 0.0f);
+      }
+      acc = merge_moments(acc, m);
+    }
+    slots[tid][sl] = acc;
+  }
   __syncthreads();
   if (tid < kGroups) {
-    float acc = 0.0f;
-    for (int c = tid * cg; c < (tid + 1) * cg; ++c) {
-      const int vv = c / kVec, jj = c % kVec;
-      for (int t = vv; t < kStatThreads; t += vpp) acc += red[t * 8 + jj];
-    }
-    const float count = static_cast<float>(valid_pos) * cg;
-    group_mean[tid] = __fdiv_rn(acc, count);
+    // group tid: channels [tid*cg, (tid+1)*cg) -> vectors and slots
+    Moments acc{0.0f, 0.0f, 0.0f};
+    const int v0 = (tid * cg) / kVec, v1 = ((tid + 1) * cg - 1) / kVec;
+    const int sl = cg >= 8 ? 0 : (tid * cg % kVec) / cg;
+    for (int vv = v0; vv <= v1; ++vv)
+      for (int t = vv; t < kStatThreads; t += vpp) acc = merge_moments(acc, slots[t][sl]);
+    partials[(static_cast<int64_t>(bt) * s.nchunks + chunk) * kGroups + tid] = make_float2(acc.mean, acc.m2);
   }
-  __syncthreads();
-  // Centred second moment over the values held in registers.
-  float m2[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-#pragma unroll
-  for (int k = 0; k < kStatValuesPerThread / kVec; ++k) {
-    const int p = tid / vpp + k * pos_per_iter;
-    if (p < valid_pos) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float d = vals[k * 8 + j] - group_mean[(c0 + j) / cg];
-        m2[j] = __fmaf_rn(d, d, m2[j]);
-      }
-    }
-  }
-  (void)nvec;
-#pragma unroll
-  for (int j = 0; j < 8; ++j) red[tid * 8 + j] = m2[j];
-  __syncthreads();
-  if (tid < kGroups) {
-    float acc = 0.0f;
-    for (int c = tid * cg; c < (tid + 1) * cg; ++c) {
-      const int vv = c / kVec, jj = c % kVec;
-      for (int t = vv; t < kStatThreads; t += vpp) acc += red[t * 8 + jj];
-    }
-    partials[(static_cast<int64_t>(bt) * s.nchunks + chunk) * kGroups + tid] = make_float2(group_mean[tid], acc);
+  if (cmin != nullptr) {
+    channel_reduce<1>(mn, vpp, s.C, red, chan);
+    for (int c = tid; c < s.C; c += kStatThreads) atomicMin(&cmin[static_cast<int64_t>(bt) * s.C + c], float_to_ordered(chan[c]));
+    channel_reduce<2>(mx, vpp, s.C, red, chan);
+    for (int c = tid; c < s.C; c += kStatThreads) atomicMax(&cmax[static_cast<int64_t>(bt) * s.C + c], float_to_ordered(chan[c]));
   }
 }
 
-// GroupNorm statistics, pass 2: one warp per group of one (b, frame).
+// The producer's per-element value: GroupNorm affine -> fp16 -> SiLU -> fp16.
+// exp / divide are the fast SFU forms, the lowering of the reference kernels.
+__device__ __forceinline__ float norm_silu_value(float v, float mean, float rstd, float gamma, float beta) {
+  float y = __fmul_rn(__fsub_rn(v, mean), rstd);
+  y = round_fp16(__fadd_rn(__fmul_rn(y, gamma), beta));
+  return round_fp16(__fdividef(y, __fadd_rn(1.0f, __expf(-y))));
+}
+
+// GroupNorm statistics, pass 2: one warp per group of one (b, frame).  With
+// cmin/cmax it also folds the per-tensor absmax candidates: the normalized
+// value is monotone in x per channel and SiLU is increasing for z >= 0 while
+// |SiLU(z)| < 0.2786 for z < 0, so the extremes give the exact absmax whenever
+// it is >= kAmaxExact; below that the full interior scan decides.
+constexpr float kAmaxExact = 0.28f;
+
 __global__ void gn_merge_kernel(const float2* __restrict__ partials, NormShape s, float eps,
-                                float2* __restrict__ stats) {
+                                float2* __restrict__ stats, const unsigned int* __restrict__ cmin,
+                                const unsigned int* __restrict__ cmax, const __half* __restrict__ gamma,
+                                const __half* __restrict__ beta, float* amax) {
   const int bt = blockIdx.x;
   const int g = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -160,7 +247,19 @@ __global__ void gn_merge_kernel(const float2* __restrict__ partials, NormShape s
     m2 += pm.y + cnt * delta * delta;
   }
   const float var = __fdiv_rn(warp_sum(m2), total);
-  if (lane == 0) stats[static_cast<int64_t>(bt) * kGroups + g] = make_float2(mean, rsqrtf(fmaxf(var, 0.0f) + eps));
+  const float rstd = rsqrtf(fmaxf(var, 0.0f) + eps);
+  if (lane == 0) stats[static_cast<int64_t>(bt) * kGroups + g] = make_float2(mean, rstd);
+  if (cmin == nullptr) return;
+  float cand = 0.0f;
+  for (int c = g * cg + lane; c < (g + 1) * cg; c += 32) {
+    const float gm = __half2float(gamma[c]), bb = __half2float(beta[c]);
+    const float lo = ordered_to_float(cmin[static_cast<int64_t>(bt) * s.C + c]);
+    const float hi = ordered_to_float(cmax[static_cast<int64_t>(bt) * s.C + c]);
+    cand = fmaxf(cand, fabsf(norm_silu_value(lo, mean, rstd, gm, bb)));
+    cand = fmaxf(cand, fabsf(norm_silu_value(hi, mean, rstd, gm, bb)));
+  }
+  cand = warp_max(cand);
+  if (lane == 0) atomic_max_nonneg(amax, cand);
 }
 
 // ---------------------------------------------------------------------------
@@ -182,53 +281,61 @@ __global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* _
   const int cg = s.C / kGroups;
   // MODE 0 walks the interior rows only: the padded ring duplicates interior
   // values or is zero, so it cannot raise the maximum.
-  const int Hr = (MODE == 0) ? s.H : s.H + 2;
-  const int Wr = (MODE == 0) ? s.W : s.W + 2;
-  const int Dr = (MODE == 0) ? s.D : s.D + 2;
+  const int Hr = (MODE == 0) ? s.Hu : s.Hu + 2;
+  const int Wr = (MODE == 0) ? s.Wu : s.Wu + 2;
+  const int Dr = (MODE == 0) ? s.Du : s.Du + 2;
   int row = blockIdx.x;
   const int hr = row % Hr;
   row /= Hr;
   const int tr = row % Dr;
   const int b = row / Dr;
-  const int t = (MODE == 0) ? tr : tr - 2;
-  int h = (MODE == 0) ? hr : hr - 1;
-  h = h < 0 ? -h : (h >= s.H ? 2 * s.H - 2 - h : h);
-  const bool frame_ok = t >= 0;
+  const int tu = (MODE == 0) ? tr : tr - 2;                 // logical frame
+  int hu = (MODE == 0) ? hr : hr - 1;                        // logical row, reflected
+  hu = hu < 0 ? -hu : (hu >= s.Hu ? 2 * s.Hu - 2 - hu : hu);
+  const bool frame_ok = tu >= 0;
+  const int t = s.ut ? (tu + 1) >> 1 : tu;                   // source frame
+  const int h = s.us == 2 ? hu >> 1 : hu;                    // source row
+  if (MODE == 0 && *amax >= kAmaxExact) return;  // the extremes already gave the exact absmax
   float scale = 1.0f;
   if (MODE == 1) {
     scale = __fmul_rn(*amax, 1.0f / 127.0f);
     if (!(scale > 0.0f)) scale = 1.0f;
     if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
   }
+  const float inv_scale = __frcp_rn(scale);
   const int row_vecs = Wr * vpp;
   const __half* xrow = x + ((static_cast<int64_t>(b) * s.D + (frame_ok ? t : 0)) * s.H + h) * s.W * s.C;
   const float2* st = stats + (static_cast<int64_t>(b) * s.D + (frame_ok ? t : 0)) * kGroups;
   const int64_t out_row = static_cast<int64_t>(blockIdx.x) * row_vecs;
+  // The block stride (256 vectors) is a multiple of C/8, so every thread keeps
+  // one channel vector: its affine constants and group statistics are loaded once.
+  const int v = threadIdx.x & (vpp - 1);
+  const int c0 = v * kVec;
+  float gm[8], bt[8], pb[8], mean[8], rstd[8];
+  load_h8(gamma + c0, gm);
+  load_h8(beta + c0, bt);
+  if (pre_bias != nullptr) load_h8(pre_bias + c0, pb);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 mr = st[(c0 + j) / cg];
+    mean[j] = mr.x;
+    rstd[j] = mr.y;
+  }
   float local_max = 0.0f;
   for (int i = threadIdx.x; i < row_vecs; i += kPackThreads) {
-    const int v = i & (vpp - 1);
     int w = (i >> vshift) - ((MODE == 0) ? 0 : 1);
-    w = w < 0 ? -w : (w >= s.W ? 2 * s.W - 2 - w : w);
-    const int c0 = v * kVec;
+    w = w < 0 ? -w : (w >= s.Wu ? 2 * s.Wu - 2 - w : w);
+    if (s.us == 2) w >>= 1;
     float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (frame_ok) {
-      float f[8], gm[8], bt[8];
+      float f[8];
       load_h8(xrow + static_cast<int64_t>(w) * s.C + c0, f);
-      load_h8(gamma + c0, gm);
-      load_h8(beta + c0, bt);
       if (pre_bias != nullptr) {
-        float pb[8];
-        load_h8(pre_bias + c0, pb);
 #pragma unroll
         for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
       }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float2 mr = st[(c0 + j) / cg];
-        float y = __fmul_rn(__fsub_rn(f[j], mr.x), mr.y);
-        y = round_fp16(__fadd_rn(__fmul_rn(y, gm[j]), bt[j]));
-        z[j] = round_fp16(__fdiv_rn(y, __fadd_rn(1.0f, expf(-y))));
-      }
+      for (int j = 0; j < 8; ++j) z[j] = norm_silu_value(f[j], mean[j], rstd[j], gm[j], bt[j]);
     }
     if (MODE == 0) {
 #pragma unroll
@@ -236,7 +343,7 @@ __global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* _
     } else if (MODE == 1) {
       __align__(8) int8_t q[8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = quant_half_away(z[j], scale);
+      for (int j = 0; j < 8; ++j) q[j] = quant_half_away_fast(z[j], scale, inv_scale);
       reinterpret_cast<uint2*>(out)[out_row + i] = *reinterpret_cast<const uint2*>(q);
     } else {
       store_h8(reinterpret_cast<__half*>(out) + (out_row + i) * kVec, z);
@@ -390,6 +497,8 @@ bool norm_shape(int64_t B, int64_t C, int64_t D, int64_t H, int64_t W, NormShape
   s->B = (int)B; s->C = (int)C; s->D = (int)D; s->H = (int)H; s->W = (int)W;
   s->positions_per_chunk = kStatElemsPerCta / (int)C;
   s->nchunks = (int)((H * W + s->positions_per_chunk - 1) / s->positions_per_chunk);
+  s->us = 1; s->ut = 0;
+  s->Du = (int)D; s->Hu = (int)H; s->Wu = (int)W;
   return true;
 }
 
@@ -398,7 +507,10 @@ size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
 struct NormWorkspace {
   float2* partials;
   float2* stats;
+  unsigned int* cmin;
+  unsigned int* cmax;
   float* amax;
+  size_t minmax_bytes;
   size_t bytes;
 };
 
@@ -406,24 +518,39 @@ NormWorkspace norm_workspace_layout(const NormShape& s, void* base) {
   NormWorkspace w{};
   const size_t part = align256(sizeof(float2) * (size_t)s.B * s.D * s.nchunks * kGroups);
   const size_t st = align256(sizeof(float2) * (size_t)s.B * s.D * kGroups);
+  const size_t mm = align256(sizeof(unsigned int) * (size_t)s.B * s.D * s.C);
   uint8_t* p = static_cast<uint8_t*>(base);
   w.partials = reinterpret_cast<float2*>(p);
   w.stats = reinterpret_cast<float2*>(p + part);
-  w.amax = reinterpret_cast<float*>(p + part + st);
-  w.bytes = part + st + 256;
+  w.cmin = reinterpret_cast<unsigned int*>(p + part + st);
+  w.cmax = reinterpret_cast<unsigned int*>(p + part + st + mm);
+  w.amax = reinterpret_cast<float*>(p + part + st + 2 * mm);
+  w.minmax_bytes = mm;
+  w.bytes = part + st + 2 * mm + 256;
   return w;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int run_norm_stats(const void* x, const void* pre_bias, float eps, const NormShape& s, const NormWorkspace& w,
-                   cudaStream_t st, const char* name) {
+// Statistics (+ absmax candidates when want_amax): memsets of the min/max/amax
+// words, the chunk-partial kernel and the merge kernel.
+int run_norm_stats(const void* x, const void* pre_bias, const void* gamma, const void* beta, float eps,
+                   const NormShape& s, const NormWorkspace& w, bool want_amax, cudaStream_t st, const char* name) {
+  if (want_amax) {
+    if (cudaMemsetAsync(w.cmin, 0xFF, w.minmax_bytes, st) != cudaSuccess ||
+        cudaMemsetAsync(w.cmax, 0x00, w.minmax_bytes, st) != cudaSuccess ||
+        cudaMemsetAsync(w.amax, 0, sizeof(float), st) != cudaSuccess)
+      return h3b_host::set_error(H3B_ECUDA, "%s: memset failed", name);
+  }
   dim3 grid(s.nchunks, s.B * s.D);
   gn_partial_kernel<<<grid, kStatThreads, 0, st>>>(static_cast<const __half*>(x),
-                                                   static_cast<const __half*>(pre_bias), s, w.partials);
+                                                   static_cast<const __half*>(pre_bias), s, w.partials,
+                                                   want_amax ? w.cmin : nullptr, want_amax ? w.cmax : nullptr);
   int rc = h3b_host::check_launch(name);
   if (rc) return rc;
-  gn_merge_kernel<<<s.B * s.D, 32 * kGroups, 0, st>>>(w.partials, s, eps, w.stats);
+  gn_merge_kernel<<<s.B * s.D, 32 * kGroups, 0, st>>>(w.partials, s, eps, w.stats, want_amax ? w.cmin : nullptr,
+                                                       want_amax ? w.cmax : nullptr, static_cast<const __half*>(gamma),
+                                                       static_cast<const __half*>(beta), w.amax);
   return h3b_host::check_launch(name);
 }
 
@@ -465,19 +592,17 @@ int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H
   if (rc) return rc;
   if (!scale) return h3b_host::set_error(H3B_EINVAL, "%s: NULL scale", name);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  rc = run_norm_stats(x, pre_bias, eps, s, w, st, name);
+  rc = run_norm_stats(x, pre_bias, gamma, beta, eps, s, w, true, st, name);
   if (rc) return rc;
-  if (cudaMemsetAsync(w.amax, 0, sizeof(float), st) != cudaSuccess)
-    return h3b_host::set_error(H3B_ECUDA, "%s: memset failed", name);
   const __half* xh = static_cast<const __half*>(x);
   const __half* pb = static_cast<const __half*>(pre_bias);
   const __half* gh = static_cast<const __half*>(gamma);
   const __half* bh = static_cast<const __half*>(beta);
-  norm_pack_kernel<0><<<(unsigned)(B * D * H), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax, nullptr,
+  norm_pack_kernel<0><<<(unsigned)(B * s.Du * s.Hu), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax, nullptr,
                                                                       nullptr);
   rc = h3b_host::check_launch(name);
   if (rc) return rc;
-  norm_pack_kernel<1><<<(unsigned)(B * (D + 2) * (H + 2)), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax,
+  norm_pack_kernel<1><<<(unsigned)(B * (s.Du + 2) * (s.Hu + 2)), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax,
                                                                                   scale, q);
   return h3b_host::check_launch(name);
 }
@@ -491,9 +616,33 @@ int h3b_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, 
   int rc = check_norm_args(x, pre_bias, gamma, beta, y, workspace, workspace_bytes, B, C, D, H, W, &s, &w, name);
   if (rc) return rc;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  rc = run_norm_stats(x, pre_bias, eps, s, w, st, name);
+  rc = run_norm_stats(x, pre_bias, gamma, beta, eps, s, w, false, st, name);
   if (rc) return rc;
-  norm_pack_kernel<2><<<(unsigned)(B * (D + 2) * (H + 2)), kPackThreads, 0, st>>>(
+  norm_pack_kernel<2><<<(unsigned)(B * (s.Du + 2) * (s.Hu + 2)), kPackThreads, 0, st>>>(
+      static_cast<const __half*>(x), static_cast<const __half*>(pre_bias), static_cast<const __half*>(gamma),
+      static_cast<const __half*>(beta), w.stats, s, nullptr, nullptr, y);
+  return h3b_host::check_launch(name);
+}
+
+int h3b_upsample_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W, int up_spatial,
+                              int up_temporal, const void* pre_bias, const void* gamma, const void* beta, float eps,
+                              void* y, void* workspace, size_t workspace_bytes, h3b_stream_t stream) {
+  const char* name = "h3b_upsample_norm_pad_f16";
+  if ((up_spatial != 1 && up_spatial != 2) || (up_temporal != 0 && up_temporal != 1))
+    return h3b_host::set_error(H3B_EINVAL, "%s: up_spatial must be 1 or 2 and up_temporal 0 or 1", name);
+  NormShape s;
+  NormWorkspace w;
+  int rc = check_norm_args(x, pre_bias, gamma, beta, y, workspace, workspace_bytes, B, C, D, H, W, &s, &w, name);
+  if (rc) return rc;
+  s.us = up_spatial;
+  s.ut = up_temporal;
+  s.Du = up_temporal ? (int)(2 * D - 1) : (int)D;
+  s.Hu = (int)(H * up_spatial);
+  s.Wu = (int)(W * up_spatial);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = run_norm_stats(x, pre_bias, gamma, beta, eps, s, w, false, st, name);
+  if (rc) return rc;
+  norm_pack_kernel<2><<<(unsigned)(B * (s.Du + 2) * (s.Hu + 2)), kPackThreads, 0, st>>>(
       static_cast<const __half*>(x), static_cast<const __half*>(pre_bias), static_cast<const __half*>(gamma),
       static_cast<const __half*>(beta), w.stats, s, nullptr, nullptr, y);
   return h3b_host::check_launch(name);

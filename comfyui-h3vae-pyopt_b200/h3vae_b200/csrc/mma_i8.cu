@@ -1,14 +1,16 @@
 // tcgen05 kind::i8 mainloop shared by the implicit-GEMM causal conv3d and the
 // decoder INT8 linears.
 //
-// Structure (one persistent CTA per SM, 6 warps):
+// Structure (one persistent CTA per SM, 10 warps):
 //   warp 0      TMA producer: A tile (128 rows x 128 int8 of K) and B tile
 //               (BN rows x 128 int8 of K) per k-block into a STAGES-deep ring
 //               of 128-byte-swizzled shared-memory buffers.
 //   warp 1      TMEM owner + MMA issuer: 4 x tcgen05.mma (K=32 each) per
 //               k-block into one of two TMEM accumulators (2 x BN int32 columns).
-//   warps 2..5  epilogue: tcgen05.ld of the finished accumulator (one TMEM
-//               lane = one output row per thread), dequantize, fused op, store.
+//   warps 2..9  epilogue: tcgen05.ld of the finished accumulator (one TMEM
+//               lane = one output row per thread; the two warps of a lane
+//               quadrant take alternate 32-column chunks), dequantize, fused
+//               op, store.
 // The double-buffered accumulator lets the epilogue of tile i overlap the
 // mainloop of tile i+1.
 //
@@ -57,7 +59,8 @@ struct MmaParams {
 
 constexpr int kBM = 128;
 constexpr int kBK = 128;  // bytes of K per stage = 4 MMAs of K=32
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 8;   // two warps per TMEM lane quadrant, splitting the columns
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kATileBytes = kBM * kBK;
 
 // Column stride between the two TMEM accumulators (kept a power of two) and
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 128);
+      mbar_init(&tempty_bar[a], 32 * kEpiWarps);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -264,6 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // -------------------------------- epilogue --------------------------------
     const int quad = warp & 3;          // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;   // tile row == TMEM lane
+    const int half = (warp - 2) >> 2;   // 0 / 1: which alternate column chunks this warp owns
     uint32_t local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int m_tile = tile / p.n_tiles;
@@ -280,7 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sx = valid ? p.a_scale[m] : 0.0f;
         const bool vec_ok = (p.ldo % 8) == 0;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           uint32_t r[32];
           tmem_ld32(t_row + c * 32, r);
           tmem_ld_wait();
@@ -312,7 +316,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0) && (p.osW % 8 == 0) &&
                             (p.osH % 8 == 0) && (p.osD % 8 == 0) && (p.osB % 8 == 0);
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = half; c < BN / 32; c += 2) {
           uint32_t r[32];
           tmem_ld32(t_row + c * 32, r);
           tmem_ld_wait();
@@ -336,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float sx = valid ? p.a_scale[m] : 0.0f;
         const bool vec_ok = (p.F % 8) == 0;
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = half; c < BN / 64; c += 2) {
           uint32_t rg[32], ru[32];
           tmem_ld32(t_row + c * 32, rg);
           tmem_ld32(t_row + BN / 2 + c * 32, ru);
@@ -350,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int jj = min(j0 + j, p.F - 1);
               const float g = round_fp16(dequant(rg[j], sx, p.w_scale[jj], p.bias, jj));
               const float u = round_fp16(dequant(ru[j], sx, p.w_scale[p.F + jj], p.bias, p.F + jj));
-              const float sg = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+              const float sg = __fdividef(g, __fadd_rn(1.0f, expf(-g)));
               v[j] = __fmul_rn(sg, u);
             }
             store_row_chunk(p.out + m * p.F + j0, v, valid_cols, vec_ok);
@@ -366,7 +370,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t tt = valid ? m - bb * p.tokens : 0;
         const int64_t dst_off = ((bb * p.heads + h) * p.tokens + tt) * 64;
 #pragma unroll 1
-        for (int part = 0; part < 3; ++part) {
+        for (int part = half; part < 3; part += 2) {
           float x[64];
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
@@ -651,8 +655,10 @@ int h3b_gemm_i8_qkv_rope(const int8_t* qa, const float* a_scale, const int8_t* q
   if (rc) return rc;
   if (!q_out || !k_out || !v_out || (rot_dims > 0 && (!cos_t || !sin_t)))
     return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
-  if (rot_dims < 0 || rot_dims > 64 || rot_dims % 2)
-    return h3b_host::set_error(H3B_EINVAL, "%s: rotary dims must be even and <= 64", name);
+  if (rot_dims != 0 && rot_dims != 16 && rot_dims != 32 && rot_dims != 48 && rot_dims != 64)
+    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: rotary dims must be one of 0, 16, 32, 48, 64", name);
+  if (rot_dims > 0 && ((reinterpret_cast<uintptr_t>(cos_t) | reinterpret_cast<uintptr_t>(sin_t)) & 15u))
+    return h3b_host::set_error(H3B_EINVAL, "%s: cos/sin tables must be 16-byte aligned", name);
   for (const void* ptr : std::initializer_list<const void*>{q_out, k_out, v_out})
     if (reinterpret_cast<uintptr_t>(ptr) & 15u) return h3b_host::set_error(H3B_EINVAL, "%s: q/k/v must be 16-byte aligned", name);
   MmaParams p{};

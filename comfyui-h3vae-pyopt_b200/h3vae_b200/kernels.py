@@ -199,6 +199,23 @@ def norm_pad_f16(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: 
     return y
 
 
+def upsample_norm_pad_f16(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float, *,
+                          spatial: bool, temporal: bool, pre_bias: torch.Tensor | None = None) -> torch.Tensor:
+    """pad(silu(GN(up(x) [+ pre_bias]))) with nearest x2 spatial / causal x2 temporal upsampling folded
+    into the producer; fp16 NDHWC [B, C, D'+2, H'+2, W'+2] with D' = 2D-1 (temporal) and H' = 2H."""
+    dev, x, lib, ws, ws_bytes = _norm_common(x, pre_bias, gamma, beta)
+    b, c, d, h, w = x.shape
+    us, ut = (2 if spatial else 1), (1 if temporal and d > 1 else 0)
+    du = 2 * d - 1 if ut else d
+    y = torch.empty((b, c, du + 2, h * us + 2, w * us + 2), device=dev, dtype=F16,
+                    memory_format=torch.channels_last_3d)
+    _lib.check(lib.h3b_upsample_norm_pad_f16(x.data_ptr(), b, c, d, h, w, us, ut, _ptr(pre_bias), gamma.data_ptr(),
+                                             beta.data_ptr(), float(eps), y.data_ptr(), ws.data_ptr(), ws_bytes,
+                                             _stream(dev)))
+    _count(3)
+    return y
+
+
 def residual_pack(x: torch.Tensor, residual: torch.Tensor, bias: torch.Tensor) -> torch.Tensor:
     """fp16(r + (x + bias)), right/bottom reflect +1, two causal zero frames; NDHWC [B,C,D+2,H+1,W+1]."""
     dev = _require_cuda(x, residual, bias)

@@ -402,18 +402,17 @@ class H3Decoder:
         tokens = feat.permute(0, 2, 3, 4, 1).reshape(b, t * h * w, cfg.hidden)        # a view of NDHWC storage
         y = self.transformer(tokens, (t, h, w))
         x = y.view(b, t, h, w, cfg.hidden).permute(0, 4, 1, 2, 3)                      # NDHWC logical [B,d,t,h,w]
-        for (gw, gb, wt, bs), sp, tp in zip(self.up, cfg.up_spatial, cfg.up_temporal):
-            x = conv_f16(K.norm_pad_f16(x, gw, gb, cfg.gn_eps), wt, bs)
-            x = upsample(x, temporal=tp, spatial=sp)
-        x = conv_f16(K.norm_pad_f16(x, self.out_gn_w, self.out_gn_b, cfg.gn_eps), self.conv_out_w, self.conv_out_b)
-        return x
-
-
-def upsample(x: torch.Tensor, *, temporal: bool, spatial: bool) -> torch.Tensor:
-    """Nearest x2 spatial upsampling and causal x2 temporal upsampling (frame 0 kept once, every
-    later frame repeated: t -> 1 + 2 (t - 1)), NDHWC in and out."""
-    if temporal and x.shape[2] > 1:
-        x = torch.cat([x[:, :, :1], x[:, :, 1:].repeat_interleave(2, dim=2)], dim=2)
-    if spatial:
-        x = x.repeat_interleave(2, dim=3).repeat_interleave(2, dim=4)
-    return x.contiguous(memory_format=CL3)
+        # Each stage: GN + SiLU + pad -> conv (its bias is carried as the next producer's pre_bias,
+        # the same fp16(conv + bias) rounding), then the x2 upsampling, which the next producer
+        # reads through its index map instead of materializing it.
+        gns = [(gw, gb) for gw, gb, _, _ in self.up] + [(self.out_gn_w, self.out_gn_b)]
+        pending_bias, up_s, up_t = None, False, False
+        for k, (wt, bs, sp, tp) in enumerate(zip([u[2] for u in self.up], [u[3] for u in self.up], cfg.up_spatial,
+                                                 cfg.up_temporal)):
+            gw, gb = gns[k]
+            y = K.upsample_norm_pad_f16(x, gw, gb, cfg.gn_eps, spatial=up_s, temporal=up_t, pre_bias=pending_bias)
+            x = conv_f16(y, wt, None)
+            pending_bias, up_s, up_t = bs, sp, tp
+        y = K.upsample_norm_pad_f16(x, self.out_gn_w, self.out_gn_b, cfg.gn_eps, spatial=up_s, temporal=up_t,
+                                    pre_bias=pending_bias)
+        return conv_f16(y, self.conv_out_w, self.conv_out_b)

@@ -105,6 +105,20 @@ int h3b_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, 
                      const void* pre_bias, const void* gamma, const void* beta, float eps, void* y,
                      void* workspace, size_t workspace_bytes, h3b_stream_t stream);
 
+/* Nearest upsampling folded into the fp16 producer: x [B,C,D,H,W] (NDHWC) is
+ * read as up(x) -- spatial factor up_spatial (1 or 2), causal temporal
+ * doubling when up_temporal = 1 (frame 0 once, later frames twice: D -> 2D-1)
+ * -- and y = pad(silu(GN(up(x) [+ pre_bias]))) is written as fp16 NDHWC
+ * [B, D'+2, H'+2, W'+2, C] without materializing up(x).  Replication leaves
+ * each frame's statistics unchanged, so they come from the source frame.
+ * Workspace: h3b_norm_workspace_size(B, C, D, H, W).
+ * ref: the causal conv3d upsampling stages of the klvae decoder
+ * (h3vae_runtime.py:542, external) fed through
+ *      opt/encoder_fused_temporal_norm.py:54-80 (norm/pack arithmetic) */
+int h3b_upsample_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W, int up_spatial,
+                              int up_temporal, const void* pre_bias, const void* gamma, const void* beta, float eps,
+                              void* y, void* workspace, size_t workspace_bytes, h3b_stream_t stream);
+
 /* ---- (a6) residual + bias + downsample pad pack ------------------------- */
 
 /* y = fp16(r + (x + bias)) computed in fp32; right/bottom reflect pad +1,
@@ -139,7 +153,7 @@ int h3b_gemm_i8_swiglu(const int8_t* qa, const float* a_scale, const int8_t* qw,
  * token m = b*tokens + t and head h:
  *   qkv = fp16(fma(acc*s, ws, bias));  q' = fp16(q * rsqrt(mean(q^2) + eps))
  *   q_out[d] = fp16(q'[d]*cos[d]) + fp16(rot(q')[d]*sin[d]) for d < R, q'[d] after
- * (same for k), v passes through.  cos/sin: fp16 [M, R].  q/k/v outputs are
+ * (same for k), v passes through.  cos/sin: fp16 [M, R], R in {0,16,32,48,64}.  q/k/v outputs are
  * fp16 [batch, heads, tokens, 64].
  * ref: opt/decoder_fused_qk_rope.py:13-54 (_qk_rope / qk_rope) fused behind
  *      opt/int8_qkv.py:33-41 (INT8 to_qkv) */
