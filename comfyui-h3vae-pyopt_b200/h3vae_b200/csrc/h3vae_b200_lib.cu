@@ -4,4 +4,4 @@
 #include "mma_i8.cu"
 #include "encoder_producers.cu"
 #include "decoder_producers.cu"
-#include "attention.cu"
+#include "attention_tc.cu"

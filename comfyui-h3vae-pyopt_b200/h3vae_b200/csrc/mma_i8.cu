@@ -90,12 +90,16 @@ __device__ __forceinline__ void store_row_chunk(__half* dst, const float (&v)[32
       *reinterpret_cast<uint4*>(dst + q * 8) = *reinterpret_cast<uint4*>(h);
     }
   } else {
-    for (int j = 0; j < 32 && j < valid_cols; ++j) dst[j] = __float2half_rn(v[j]);
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid_cols) dst[j] = __float2half_rn(v[j]);
   }
 }
 
 __device__ __forceinline__ void store_acc_chunk(int32_t* dst, const uint32_t (&r)[32], int valid_cols) {
-  for (int j = 0; j < 32 && j < valid_cols; ++j) dst[j] = static_cast<int32_t>(r[j]);
+#pragma unroll
+  for (int j = 0; j < 32; ++j)
+    if (j < valid_cols) dst[j] = static_cast<int32_t>(r[j]);
 }
 
 // v = fp16(fp16(v) + residual): the residual block's `x + h` on fp16 tensors.
@@ -113,7 +117,9 @@ __device__ __forceinline__ void add_residual_chunk(float (&v)[32], const __half*
       }
     }
   } else {
-    for (int j = 0; j < 32 && j < valid_cols; ++j) v[j] = __fadd_rn(round_fp16(v[j]), __half2float(res[j]));
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < valid_cols) v[j] = __fadd_rn(round_fp16(v[j]), __half2float(res[j]));
   }
 }
 
