@@ -227,7 +227,7 @@ def norm_pad_f16(x, gamma, beta, eps, pre_bias=None) -> np.ndarray:
 
 def norm_pad_quant(x, gamma, beta, eps, pre_bias=None):
     """INT8 producer: per-tensor scale of the padded fp16 values, half-away quantization.
-    ref: opt/encoder_int8_norm.py:198-231, opt/encoder_int8_norm_recompute.py:40-49."""
+    ref: opt/encoder_int8_norm.py:77-110, opt/encoder_int8_norm_recompute.py:40-49."""
     y = pad_reflect_causal(norm_silu(x, gamma, beta, eps, pre_bias))
     scale = tensor_scale(np.abs(y).max())
     return quant_half_away(y, scale), scale
@@ -387,7 +387,7 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, scale: float) -> np.n
 # (a15) pixel finalization, (a8) tile planner and blend
 # ---------------------------------------------------------------------------
 def finalize_pixels(x: np.ndarray, std, mean) -> np.ndarray:
-    """clamp(x*std + mean, 0, 1) in fp32 without FMA, NaN preserved.  ref: opt/fp16_finalize.py:249-265."""
+    """clamp(x*std + mean, 0, 1) in fp32 without FMA, NaN preserved.  ref: opt/fp16_finalize.py:24-41."""
     xf = np.asarray(x).astype(F32)
     v = xf * np.asarray(std, F32).reshape(1, 3, 1, 1, 1) + np.asarray(mean, F32).reshape(1, 3, 1, 1, 1)
     v = np.where(v < 0, F32(0), np.where(v > 1, F32(1), v))
