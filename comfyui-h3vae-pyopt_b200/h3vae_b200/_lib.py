@@ -34,6 +34,8 @@ _SIGNATURES = {
     "h3b_norm_workspace_size": (c_size_t, [c_int64] * 5),
     "h3b_norm_pad_quant": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                    c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
+    "h3b_norm_pad_quant_noalloc": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p,
+                                           c_void_p, c_void_p, c_float, c_void_p, c_void_p, c_void_p]),
     "h3b_norm_pad_f16": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
                                  c_void_p, c_float, c_void_p, c_void_p, c_size_t, c_void_p]),
     "h3b_upsample_norm_pad_f16": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_int, c_int,

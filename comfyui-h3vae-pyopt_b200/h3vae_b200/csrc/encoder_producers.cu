@@ -13,6 +13,8 @@
 //                       in H/W and two zero frames in front; modes: absmax of the
 //                       interior, INT8 with the per-tensor scale, or fp16 output.
 //   residual_pack_kernel, quantize kernels, finalize_pixels_kernel.
+#include <mutex>
+
 #include "common.cuh"
 
 namespace h3b {
@@ -605,6 +607,62 @@ int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H
   norm_pack_kernel<1><<<(unsigned)(B * (s.Du + 2) * (s.Hu + 2)), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax,
                                                                                   scale, q);
   return h3b_host::check_launch(name);
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of h3b_norm_pad_quant.  Its scratch (the statistics
+// partials, per-frame statistics, per-channel min/max words and the absmax
+// word) lives in one file-scope device array instead of a caller workspace.
+// The host never passes the array's name to a kernel (in host code that name
+// is only a stand-in): the device address is resolved once per device with
+// cudaGetSymbolAddress while that device is current, and cached.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr size_t kNormStaticScratchBytes = size_t(4) << 20;  // 4 MiB, held by every device that loads the library
+__device__ __align__(256) unsigned char g_norm_static_scratch[kNormStaticScratchBytes];
+std::mutex g_norm_static_mutex;
+constexpr int kMaxDevices = 128;
+void* g_norm_static_ptr[kMaxDevices] = {};
+}  // namespace
+
+int h3b_norm_pad_quant_noalloc(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
+                               const void* pre_bias, const void* gamma, const void* beta, float eps, int8_t* q,
+                               float* scale, h3b_stream_t stream) {
+  const char* name = "h3b_norm_pad_quant_noalloc";
+  NormShape s;
+  if (!norm_shape(B, C, D, H, W, &s))
+    return h3b_host::set_error(H3B_EUNSUPPORTED,
+                               "%s: unsupported shape B=%lld C=%lld D=%lld H=%lld W=%lld (need H,W>=2, C a power of "
+                               "two in [32, 2048])",
+                               name, (long long)B, (long long)C, (long long)D, (long long)H, (long long)W);
+  const size_t need = norm_workspace_layout(s, nullptr).bytes;
+  if (need > kNormStaticScratchBytes)
+    return h3b_host::set_error(H3B_EUNSUPPORTED,
+                               "%s: this shape needs %zu bytes of scratch, above the %zu-byte static buffer; use "
+                               "h3b_norm_pad_quant with a caller workspace",
+                               name, need, kNormStaticScratchBytes);
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return h3b_host::set_error(H3B_ECUDA, "%s: no usable current device (%s)", name, cudaGetErrorString(e));
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_norm_static_mutex);
+    if (g_norm_static_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_norm_static_scratch);
+      if (e != cudaSuccess || ptr == nullptr)
+        return h3b_host::set_error(H3B_ECUDA, "%s: cudaGetSymbolAddress of the static scratch failed: %s", name,
+                                   cudaGetErrorString(e));
+      g_norm_static_ptr[dev] = ptr;
+    }
+    scratch = g_norm_static_ptr[dev];
+  }
+  // h3b_norm_pad_quant clears the min / max / absmax words on the stream before
+  // use and fully rewrites the partials and statistics, so stale contents from
+  // an earlier call never leak into this one.
+  return h3b_norm_pad_quant(x, B, C, D, H, W, pre_bias, gamma, beta, eps, q, scale, scratch,
+                            kNormStaticScratchBytes, stream);
 }
 
 int h3b_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W, const void* pre_bias,

@@ -96,6 +96,25 @@ int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H
                        const void* pre_bias, const void* gamma, const void* beta, float eps, int8_t* q,
                        float* scale, void* workspace, size_t workspace_bytes, h3b_stream_t stream);
 
+/* Allocation-free INT8 producer: the same computation and output as
+ * h3b_norm_pad_quant, for callers that cannot allocate device memory at the
+ * call site -- e.g. a host that hands the library only the input and output
+ * buffers carved from its own pre-sized pool and has no allocator (and no
+ * spare workspace) to offer.  The scratch is a 4 MiB static device array that
+ * every GPU loading the library holds until exit; shapes whose
+ * h3b_norm_workspace_size() exceeds 4 MiB are rejected with H3B_EUNSUPPORTED
+ * (e.g. B=4, C=128, D=17, 256x256 needs about 1.2 MiB and fits).
+ * The first call on a device resolves the array's address for that device
+ * (cudaGetSymbolAddress with the device current); make that first call before
+ * any stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (other streams, other host threads) race on it, so serialize them.
+ * No cudaMalloc / cudaFree or allocating library routine is called.
+ * No counterpart in the reference: its producer always allocates its scratch
+ * through PyTorch (opt/encoder_int8_norm.py:77-110 is the computation). */
+int h3b_norm_pad_quant_noalloc(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
+                               const void* pre_bias, const void* gamma, const void* beta, float eps, int8_t* q,
+                               float* scale, h3b_stream_t stream);
+
 /* FP16 producer with the same arithmetic, writing y: fp16 NDHWC
  * [B, D+2, H+2, W+2, C] (padded) for the fp16 convolutions.
  * ref: opt/encoder_fused_temporal_norm.py:54-80 (temporal_norm_pack),
