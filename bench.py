@@ -38,6 +38,11 @@ VIDEO_SHAPE = (1, 3, 124, 768, 1344)
 TILE = 256
 OVERLAP = 32
 METRIC = "768x1344x124 tile256 encode+decode round-trip seconds"
+# DRAM bytes (read + write) per INT8 conv launch at encoder batch 4: ncu dram__bytes_read.sum +
+# dram__bytes_write.sum summed over the 16 conv launches of one tile-batch-1 encoder call
+# (2.78 GB: 14 launches measured, the two stage-4 launches estimated from their twins), times 4 for
+# batch 4 (activation traffic scales with the batch), divided by the 16 launches.
+CONV_DRAM_BYTES_PER_LAUNCH = 2.78e9 * 4 / 16
 UNIT = "s"
 
 
@@ -52,6 +57,8 @@ def parse_args():
     ap.add_argument("--workload", choices=("video", "tile"), default="video",
                     help="video: the config-5 round trip (the bench line); tile: one config-3 encoder call and "
                          "one config-4 decoder call per step (small enough for ncu captures)")
+    ap.add_argument("--tile-batch", type=int, default=4,
+                    help="tile workload: clips per encoder call and tiles per decoder call (4 = configs 3/4)")
     return ap.parse_args()
 
 
@@ -272,8 +279,9 @@ def run_tile(args):
     rt = H3VAEPyOptRuntime(int8_encode=True, int8_decode=True, decode_fusions=True, log_calls=False,
                            compile_decoder=False, compile_encoder=False)
     g = torch.Generator(device="cuda").manual_seed(0)
-    x = (torch.rand((4, 3, 17, 256, 256), generator=g, device="cuda") * 2 - 1).half()
-    z = torch.randn((4, 16, 5, 32, 32), generator=g, device="cuda").half()
+    tb = args.tile_batch
+    x = (torch.rand((tb, 3, 17, 256, 256), generator=g, device="cuda") * 2 - 1).half()
+    z = torch.randn((tb, 16, 5, 32, 32), generator=g, device="cuda").half()
     for _ in range(args.warmup):
         rt.encoder(x)
         rt.decoder(z)
@@ -289,7 +297,7 @@ def run_tile(args):
         torch.cuda.synchronize()
         enc.append(e0.elapsed_time(e1))
         dec.append(e1.elapsed_time(e2))
-    print(json.dumps({"workload": "tile", "encoder_tile_ms": statistics.mean(enc),
+    print(json.dumps({"workload": "tile", "tile_batch": tb, "encoder_tile_ms": statistics.mean(enc),
                       "decoder_tile_ms": statistics.mean(dec), "steps": args.steps, "warmup": args.warmup}))
 
 
@@ -423,7 +431,10 @@ def main():
                          "achieved": conv_tops, "peak": int8_peak, "unit": "TFLOP/s",
                          "peak_source": "INT8 ops/s of torch._int_mm 8192^3 measured live on this GPU "
                                         "(MEASURED_PEAKS.json has no INT8 entry)",
-                         "frac": conv_tops / int8_peak if int8_peak else None, "traffic": None,
+                         "frac": conv_tops / int8_peak if int8_peak else None,
+                         "traffic": CONV_DRAM_BYTES_PER_LAUNCH,
+                         "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, conv launches of a "
+                                           "tile-batch-1 encoder call scaled x4 (bytes per launch)",
                          "launches": conv_launches, "ms_total": conv_ms},
             "e2e": e2e, "cpu_baseline": cpu, "clocks": cl, "gpu_launches": launches,
         }
