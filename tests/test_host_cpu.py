@@ -1,0 +1,177 @@
+"""Host-side checks that need no GPU: the C-ABI library exports, the option validation policy of
+the runtime, the ComfyUI node surface, and the argument checks of the reference-facing op mirrors.
+"""
+from __future__ import annotations
+
+import re
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import ROOT
+
+
+def _header_symbols():
+    text = (ROOT / "include" / "h3vae_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    text = re.sub(r"//[^\n]*", "", text)
+    return sorted(set(re.findall(r"\b(h3b_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_header_symbol():
+    from h3vae_b200 import _lib, build_lib
+    build_lib.build()
+    lib = _lib.load()
+    symbols = _header_symbols()
+    assert len(symbols) == 24
+    missing = [s for s in symbols if not hasattr(lib, s)]
+    assert not missing, f"declared in the header but not exported: {missing}"
+    assert set(symbols) == set(_lib._SIGNATURES), "ctypes signature table out of sync with the header"
+    assert lib.h3b_abi_version() == 100
+
+
+def test_workspace_sizes_scale_with_shape():
+    from h3vae_b200 import _lib
+    lib = _lib.load()
+    small = lib.h3b_norm_workspace_size(1, 128, 19, 64, 64)
+    big = lib.h3b_norm_workspace_size(4, 128, 19, 258, 258)
+    assert 0 < small < big
+    assert lib.h3b_quantize_tensor_workspace_size() > 0
+
+
+def test_product_modules_do_not_import_the_oracle():
+    pkg = ROOT / "comfyui-h3vae-pyopt_b200"
+    for path in list(pkg.rglob("*.py")) + list(pkg.rglob("*.cu")) + list(pkg.rglob("*.cuh")):
+        assert "oracle" not in path.read_text().replace("oracle-free", ""), f"{path} references the oracle"
+
+
+# ---------------------------------------------------------------------------
+# Option validation (ref: h3vae_runtime.py:50-181): fail before any weight is built, no fallback
+# ---------------------------------------------------------------------------
+GOOD = dict(cuda_available=True, capability=(10, 0), hip=None)
+
+
+def test_int8_decode_validation_policy():
+    from h3vae_b200.runtime import _validate_int8_decode_options as v
+    v(enabled=False, fast_linear=True, device="cpu", dtype=torch.float32)       # disabled: nothing checked
+    v(enabled=True, fast_linear=False, device="cuda", dtype=torch.float16, library_available=True, **GOOD)
+    with pytest.raises(ValueError, match="mutually exclusive"):
+        v(enabled=True, fast_linear=True, device="cuda", dtype=torch.float16, **GOOD)
+    with pytest.raises(RuntimeError, match="CUDA device"):
+        v(enabled=True, fast_linear=False, device="cpu", dtype=torch.float16, **GOOD)
+    with pytest.raises(RuntimeError, match="fp16"):
+        v(enabled=True, fast_linear=False, device="cuda", dtype=torch.float32, **GOOD)
+    with pytest.raises(RuntimeError, match="ROCm"):
+        v(enabled=True, fast_linear=False, device="cuda", dtype=torch.float16,
+          **{**GOOD, "hip": "6.2"})
+    with pytest.raises(RuntimeError, match="available CUDA GPU"):
+        v(enabled=True, fast_linear=False, device="cuda", dtype=torch.float16,
+          **{**GOOD, "cuda_available": False})
+    with pytest.raises(RuntimeError, match="sm_100"):
+        v(enabled=True, fast_linear=False, device="cuda", dtype=torch.float16,
+          **{**GOOD, "capability": (12, 0)})
+    with pytest.raises(RuntimeError, match="no fallback"):
+        v(enabled=True, fast_linear=False, device="cuda", dtype=torch.float16, library_available=False, **GOOD)
+
+
+def test_int8_encode_and_fusion_validation_policy():
+    from h3vae_b200.runtime import _validate_decode_fusions_options, _validate_int8_encode_options
+    _validate_int8_encode_options(enabled=True, device="cuda", dtype=torch.float16, library_available=True, **GOOD)
+    with pytest.raises(RuntimeError, match="int8_encode requires dtype=fp16"):
+        _validate_int8_encode_options(enabled=True, device="cuda", dtype=torch.float32, **GOOD)
+    with pytest.raises(RuntimeError, match="int8_encode requires a CUDA device"):
+        _validate_int8_encode_options(enabled=True, device="cpu", dtype=torch.float16, **GOOD)
+    with pytest.raises(RuntimeError, match="sm_100"):
+        _validate_int8_encode_options(enabled=True, device="cuda", dtype=torch.float16,
+                                      **{**GOOD, "capability": (9, 0)})
+    with pytest.raises(ValueError, match="mutually exclusive"):
+        _validate_decode_fusions_options(enabled=True, device="cuda", dtype=torch.float16, fast_linear=True)
+    with pytest.raises(RuntimeError, match="fp16"):
+        _validate_decode_fusions_options(enabled=True, device="cuda", dtype=torch.float32, fast_linear=False)
+    _validate_decode_fusions_options(enabled=True, device="cuda", dtype=torch.float16, fast_linear=False, **GOOD)
+
+
+@pytest.mark.parametrize("kwargs, exc, match", [
+    (dict(fast_linear=True), ValueError, "fast_linear"),
+    (dict(encoder_tile_size=24), ValueError, "multiple of 16"),
+    (dict(encoder_tile_size=32), ValueError, "exceed"),
+    (dict(encoder_staged_batch=3), ValueError, "1, 2 or 4"),
+    (dict(tile_batch=-1), ValueError, "non-negative"),
+    (dict(model_code_dir="/nonexistent"), NotImplementedError, "synthetic"),
+    (dict(dtype=torch.float32), RuntimeError, "fp16"),
+    (dict(int8_decode=True, device="cpu"), RuntimeError, "CUDA device"),
+])
+def test_runtime_rejects_bad_options_before_building(kwargs, exc, match):
+    from h3vae_b200.runtime import H3VAEPyOptRuntime
+    with pytest.raises(exc, match=match):
+        H3VAEPyOptRuntime(**{"device": "cpu", **kwargs})
+
+
+# ---------------------------------------------------------------------------
+# ComfyUI node surface (ref: h3vae_nodes.py:35-197)
+# ---------------------------------------------------------------------------
+def test_node_inputs_and_mappings():
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("h3b_custom_nodes", ROOT / "comfyui-h3vae-pyopt_b200" / "__init__.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    node = mod.NODE_CLASS_MAPPINGS["H3VAEPyOptLoader"]
+    assert "H3VAEPyOptLoader" in mod.NODE_DISPLAY_NAME_MAPPINGS
+    types = node.INPUT_TYPES()
+    required = {k: v[1].get("default") for k, v in types["required"].items()}
+    assert required == {"vae_name": "use default", "dtype": "fp16", "decoder_tile_size": 256, "tile_batch": 2,
+                        "compile_decoder": True, "compile_encoder": True, "encoder_staged_batch": 4,
+                        "cudnn_benchmark": True, "warmup": "none", "warmup_frames": 124, "warmup_width": 1344,
+                        "warmup_height": 768, "log_calls": True}
+    optional = {k: v[1].get("default") for k, v in types["optional"].items()}
+    assert optional.keys() == {"encoder_tile_size", "fast_linear", "decode_fusions", "int8_decode", "int8_encode",
+                               "model_code_dir", "weights_path"}
+    assert node.RETURN_TYPES == ("VAE",) and node.FUNCTION == "load"
+    with pytest.raises(ValueError, match="mutually exclusive"):
+        node().load("use default", "fp16", 256, 2, True, True, 4, True, "none", 124, 1344, 768, True,
+                    fast_linear=True, int8_decode=True)
+
+
+# ---------------------------------------------------------------------------
+# opt/* mirrors: argument checks that run before any kernel, and static weight quantization
+# ---------------------------------------------------------------------------
+def test_opt_mirror_argument_checks():
+    from h3vae_b200.opt import fp16_finalize, int8_ffn_up_fused, int8_swiglu_fused
+    with pytest.raises(ValueError, match="even width"):
+        int8_swiglu_fused.validate_input(torch.zeros(4, 7, dtype=torch.float16))
+    with pytest.raises(ValueError, match="FP16"):
+        int8_swiglu_fused.validate_input(torch.zeros(4, 8))
+    q = torch.zeros(4, 64, dtype=torch.int8)
+    with pytest.raises(ValueError, match="dimensions"):
+        int8_swiglu_fused.prequantized_linear(q, torch.ones(4, 1), torch.zeros(8, 32, dtype=torch.int8), torch.ones(8))
+    with pytest.raises(ValueError, match="one scale"):
+        int8_swiglu_fused.prequantized_linear(q, torch.ones(3, 1), torch.zeros(8, 64, dtype=torch.int8), torch.ones(8))
+    with pytest.raises(ValueError, match=r"\[2F, K\]"):
+        int8_ffn_up_fused.validate_prequantized(q, torch.ones(4, 1), torch.zeros(7, 64, dtype=torch.int8),
+                                                torch.ones(7), None)
+    x = torch.zeros(1, 3, 2, 4, 4)
+    with pytest.raises(ValueError, match="channel constants"):
+        fp16_finalize.validate(x, torch.ones(3, dtype=torch.float16), torch.zeros(3))
+    with pytest.raises(ValueError, match="B,3,T,H,W"):
+        fp16_finalize.validate(torch.zeros(1, 4, 2, 4, 4), torch.ones(3), torch.zeros(3))
+
+
+def test_kitchen_static_weight_matches_oracle():
+    from oracle import h3vae_oracle as O
+    from h3vae_b200.opt.kitchen_int8 import KitchenInt8Linear
+    lin = torch.nn.Linear(256, 96).half()
+    with torch.no_grad():
+        lin.weight[5].zero_()
+    mod = KitchenInt8Linear(lin).eval()
+    q_ref, s_ref = O.quantize_rowwise_weight(lin.weight.detach())
+    np.testing.assert_array_equal(mod.qweight.numpy(), q_ref.numpy())
+    np.testing.assert_array_equal(mod.weight_scale.numpy(), s_ref.reshape(-1).numpy())
+    assert mod.weight_scale[5] == 1.0 and not mod.qweight[5].any()
+    with pytest.raises(RuntimeError, match="no_grad"):
+        mod(torch.zeros(2, 256, dtype=torch.float16))
+    with torch.no_grad(), pytest.raises(ValueError, match="K=128"):
+        mod(torch.zeros(2, 128, dtype=torch.float16))
+    lin.weight.data[0, 0] = float("inf")
+    with pytest.raises(ValueError, match="non-finite"):
+        KitchenInt8Linear(lin)
