@@ -29,6 +29,8 @@ _SIGNATURES = {
     "h3b_device_error": (c_int, [POINTER(c_uint), c_int]),
     "h3b_conv3d_i8": (c_int, [c_void_p, _i64p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
                               c_void_p, c_void_p, c_void_p, c_void_p, _i64p, c_void_p, c_void_p, c_int, c_void_p]),
+    "h3b_conv3d_f16": (c_int, [c_void_p, _i64p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
+                               c_void_p, c_void_p, _i64p, c_void_p, c_int, c_void_p]),
     "h3b_quantize_tensor_workspace_size": (c_size_t, []),
     "h3b_quantize_tensor_i8": (c_int, [c_void_p, _i64p, _i64p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "h3b_norm_workspace_size": (c_size_t, [c_int64] * 5),

@@ -1,8 +1,8 @@
 // Shared device/host helpers for the sm_100a kernels of the H3 VAE INT8 path.
 //
 // Everything here is hand-written inline PTX for the Blackwell data-centre
-// tensor-core path: mbarriers, TMA (cp.async.bulk.tensor, no cluster
-// multicast anywhere), and the tcgen05 family (TMEM alloc, MMA, commit, ld).
+// tensor-core path: mbarriers, per-CTA TMA tiled loads (cp.async.bulk.tensor),
+// and the tcgen05 family (TMEM alloc, MMA, commit, ld).
 // Every spin-wait is bounded: after kSpinLimit polls it records an error code
 // in the caller-visible device error word and reports failure so the kernel
 // can unwind instead of hanging the GPU.
@@ -112,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tiled, no multicast)
+// TMA (tiled loads into this CTA's shared memory)
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");

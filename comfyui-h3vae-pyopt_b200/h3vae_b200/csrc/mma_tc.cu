@@ -1,12 +1,15 @@
-// tcgen05 kind::i8 mainloop shared by the implicit-GEMM causal conv3d and the
-// decoder INT8 linears.
+// tcgen05 mainloop shared by the implicit-GEMM causal conv3d (INT8 and fp16
+// operands) and the decoder INT8 linears.
 //
 // Structure (one persistent CTA per SM, 10 warps):
-//   warp 0      TMA producer: A tile (128 rows x 128 int8 of K) and B tile
-//               (BN rows x 128 int8 of K) per k-block into a STAGES-deep ring
-//               of 128-byte-swizzled shared-memory buffers.
-//   warp 1      TMEM owner + MMA issuer: 4 x tcgen05.mma (K=32 each) per
-//               k-block into one of two TMEM accumulators (2 x BN int32 columns).
+//   warp 0      TMA producer: MT A tiles (128 rows x 128 bytes of K each) and
+//               one B tile (BN rows x 128 bytes of K) per k-block into a
+//               STAGES-deep ring of 128-byte-swizzled shared-memory buffers.
+//   warp 1      TMEM owner + MMA issuer: 4 x tcgen05.mma per k-block and A
+//               tile (kind::i8 K=32 or kind::f16 K=16: 32 bytes of K each)
+//               into one of two TMEM accumulators (MT x BN 32-bit columns).
+//               MT = 2 lets two 128-row M tiles share each B tile, which
+//               halves the B traffic per MMA for narrow (BN = 128) outputs.
 //   warps 2..9  epilogue: tcgen05.ld of the finished accumulator (one TMEM
 //               lane = one output row per thread; the two warps of a lane
 //               quadrant take alternate 32-column chunks), dequantize, fused
@@ -16,10 +19,12 @@
 //
 // Conv mode: the A operand of output tile (b, od, rows oh0.., cols ow0..) for
 // tap (kd, kh, kw) and channel chunk c0 is one 5-D TMA box
-// {128 channels, bw, bh, 1, 1} at (c0, ow0+kw, oh0+kh, od+kd, b) of the padded
-// NDHWC int8 input -- the im2col tile is never materialized.  Output frames
-// od < 2 start at tap kd = 2 - od when the producer guarantees two zero causal
-// frames (integer zero products are skipped, the sum is unchanged).
+// {128 bytes of channels, bw*sw, bh*sh, 1, 1} at
+// (c0, ow0*sw+kw, oh0*sh+kh, od*sd+kd, b) of the padded NDHWC input, with TMA
+// element strides {1, sw, sh, 1, 1} so a stride-2 conv reads every other
+// pixel -- the im2col tile is never materialized.  Taps that only read the
+// two zero causal frames (od*sd + kd < 2) are skipped when the producer
+// guarantees those frames (zero products, the sum is unchanged).
 #include "common.cuh"
 
 namespace h3b {
@@ -31,9 +36,11 @@ struct MmaParams {
   int M, N, K;          // GEMM view (conv: N = out channels)
   int m_tiles, n_tiles;
   int k_blocks;         // GEMM: ceil(K / 128); conv: taps * c_chunks
+  int m_groups;         // ceil(m_tiles / MT): CTA tiles along M
   // conv geometry
   int B, Do, Ho, Wo;
   int kd, kh, kw, taps, c_chunks, C;
+  int sd, sh, sw;
   int bw, bh, w_tiles, h_tiles;
   int causal;
   // epilogue operands
@@ -64,12 +71,19 @@ constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr uint32_t kATileBytes = kBM * kBK;
 
 // Column stride between the two TMEM accumulators (kept a power of two) and
-// the power-of-two allocation that holds both.
-template <int BN>
+// the power-of-two allocation that holds both; W = MT * BN columns each.
+template <int W>
 struct TmemLayout {
-  static constexpr uint32_t acc_stride = (BN <= 32) ? 32 : (BN <= 64) ? 64 : (BN <= 128) ? 128 : 256;
+  static_assert(W <= 256, "two accumulators must fit the 512 TMEM columns");
+  static constexpr uint32_t acc_stride = (W <= 32) ? 32 : (W <= 64) ? 64 : (W <= 128) ? 128 : 256;
   static constexpr uint32_t cols = 2 * acc_stride;
 };
+
+// Output value of one accumulator column: INT8 dequantization, or the fp32
+// accumulator of an fp16 conv plus its bias.
+template <bool F16>
+__device__ __forceinline__ float epi_value(uint32_t acc_bits, float sx, const float* w_scale, const __half* bias,
+                                           int n);
 
 // ---------------------------------------------------------------------------
 // Epilogue helpers
@@ -78,6 +92,18 @@ __device__ __forceinline__ float dequant(uint32_t acc_bits, float sx, float ws, 
   float v = __fmul_rn(static_cast<float>(static_cast<int32_t>(acc_bits)), sx);
   if (bias != nullptr) return __fmaf_rn(v, ws, __half2float(bias[n]));
   return __fmul_rn(v, ws);
+}
+
+template <>
+__device__ __forceinline__ float epi_value<false>(uint32_t acc_bits, float sx, const float* w_scale,
+                                                  const __half* bias, int n) {
+  return dequant(acc_bits, sx, w_scale[n], bias, n);
+}
+
+template <>
+__device__ __forceinline__ float epi_value<true>(uint32_t acc_bits, float, const float*, const __half* bias, int n) {
+  const float v = __uint_as_float(acc_bits);
+  return bias != nullptr ? __fadd_rn(v, __half2float(bias[n])) : v;
 }
 
 __device__ __forceinline__ void store_row_chunk(__half* dst, const float (&v)[32], int valid_cols, bool vec_ok) {
@@ -126,20 +152,25 @@ __device__ __forceinline__ void add_residual_chunk(float (&v)[32], const __half*
 // ---------------------------------------------------------------------------
 // The kernel
 // ---------------------------------------------------------------------------
-template <int BN, int STAGES, AMode AM, Epi EP>
+template <int BN, int STAGES, AMode AM, Epi EP, int MT, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
-    mma_i8_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+    mma_tc_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                   const MmaParams p) {
+  static_assert(MT == 1 || MT == 2, "one or two M tiles per CTA tile");
+  static_assert(MT == 1 || EP == Epi::kConv || EP == Epi::kLinear, "paired M tiles: conv / linear epilogues only");
+  static_assert(!F16 || EP == Epi::kConv, "fp16 operands: conv epilogue only");
+  constexpr int kKE = F16 ? 64 : 128;   // K elements per 128-byte k-block
   constexpr uint32_t kBTileBytes = BN * kBK;
-  constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes;
-  constexpr uint32_t kTmemCols = TmemLayout<BN>::cols;
-  constexpr uint32_t kAccStride = TmemLayout<BN>::acc_stride;
-  constexpr uint32_t kIdesc = make_idesc_i8(kBM, BN);
+  constexpr uint32_t kAStageBytes = MT * kATileBytes;
+  constexpr uint32_t kStageBytes = kAStageBytes + kBTileBytes;
+  constexpr uint32_t kTmemCols = TmemLayout<MT * BN>::cols;
+  constexpr uint32_t kAccStride = TmemLayout<MT * BN>::acc_stride;
+  constexpr uint32_t kIdesc = F16 ? make_idesc_f16(kBM, BN) : make_idesc_i8(kBM, BN);
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
-  uint8_t* smem_b = smem + STAGES * kATileBytes;
+  uint8_t* smem_b = smem + STAGES * kAStageBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + STAGES;
@@ -150,7 +181,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_tiles = p.m_tiles * p.n_tiles;
+  const int num_tiles = p.m_groups * p.n_tiles;
+
+  // Conv: output tile m_tile -> (b, od, oh0, ow0); first k-block that does not
+  // only read the two zero causal frames.
+  auto conv_tile = [&](int m_tile, int& b, int& od, int& oh0, int& ow0) {
+    int t = m_tile;
+    const int tw = t % p.w_tiles; t /= p.w_tiles;
+    const int th = t % p.h_tiles; t /= p.h_tiles;
+    od = t % p.Do;
+    b = t / p.Do;
+    oh0 = th * p.bh;
+    ow0 = tw * p.bw;
+  };
+  auto first_kblock = [&](int m_group) {
+    int kb = 0;
+    if constexpr (AM == AMode::kConv5D) {
+      if (p.causal) {
+        kb = p.k_blocks;
+#pragma unroll
+        for (int i = 0; i < MT; ++i) {
+          const int mt = m_group * MT + i;
+          if (mt >= p.m_tiles) break;
+          const int od = (mt / (p.w_tiles * p.h_tiles)) % p.Do;
+          const int kd0 = max(0, 2 - od * p.sd);
+          kb = min(kb, kd0 * p.kh * p.kw * p.c_chunks);
+        }
+      }
+    }
+    return kb;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -183,26 +243,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int m_tile = tile / p.n_tiles;
-        const int n_tile = tile - m_tile * p.n_tiles;
-        int kb_begin = 0, kb_end = p.k_blocks;
-        int b = 0, od = 0, oh0 = 0, ow0 = 0;
+        const int m_group = tile / p.n_tiles;
+        const int n_tile = tile - m_group * p.n_tiles;
+        const int kb_begin = first_kblock(m_group);
+        int cb[MT], cd[MT], chh[MT], cw[MT];
         if constexpr (AM == AMode::kConv5D) {
-          int t = m_tile;
-          const int tw = t % p.w_tiles; t /= p.w_tiles;
-          const int th = t % p.h_tiles; t /= p.h_tiles;
-          od = t % p.Do;
-          b = t / p.Do;
-          oh0 = th * p.bh;
-          ow0 = tw * p.bw;
-          if (p.causal && od < 2) kb_begin = (2 - od) * p.kh * p.kw * p.c_chunks;
+#pragma unroll
+          for (int i = 0; i < MT; ++i) {
+            // A tile past the last M tile decodes to b >= B: the TMA box is
+            // entirely out of range and loads zeros.
+            conv_tile(m_group * MT + i, cb[i], cd[i], chh[i], cw[i]);
+            cd[i] *= p.sd;
+            chh[i] *= p.sh;
+            cw[i] *= p.sw;
+          }
         }
-        for (int kb = kb_begin; kb < kb_end; ++kb, ++it) {
+        for (int kb = kb_begin; kb < p.k_blocks; ++kb, ++it) {
           const uint32_t s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&empty_bar[s], ph ^ 1u, abort_flag)) { ok = false; break; }
           mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
-          uint8_t* sa = smem_a + s * kATileBytes;
+          uint8_t* sa = smem_a + s * kAStageBytes;
           uint8_t* sb = smem_b + s * kBTileBytes;
           if constexpr (AM == AMode::kConv5D) {
             const int tap = kb / p.c_chunks;
@@ -210,16 +271,21 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tkw = tap % p.kw;
             const int tkh = (tap / p.kw) % p.kh;
             const int tkd = tap / (p.kw * p.kh);
-            tma_load_5d(sa, &map_a, &full_bar[s], cc * kBK, ow0 + tkw, oh0 + tkh, od + tkd, b);
-            tma_load_2d(sb, &map_b, &full_bar[s], kb * kBK, n_tile * BN);
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+              tma_load_5d(sa + i * kATileBytes, &map_a, &full_bar[s], cc * kKE, cw[i] + tkw, chh[i] + tkh,
+                          cd[i] + tkd, cb[i]);
+            tma_load_2d(sb, &map_b, &full_bar[s], kb * kKE, n_tile * BN);
           } else {
-            tma_load_2d(sa, &map_a, &full_bar[s], kb * kBK, m_tile * kBM);
+#pragma unroll
+            for (int i = 0; i < MT; ++i)
+              tma_load_2d(sa + i * kATileBytes, &map_a, &full_bar[s], kb * kKE, (m_group * MT + i) * kBM);
             if constexpr (EP == Epi::kSwiGLU) {
               const int j0 = n_tile * (BN / 2);
-              tma_load_2d(sb, &map_b, &full_bar[s], kb * kBK, j0);
-              tma_load_2d(sb + (BN / 2) * kBK, &map_b, &full_bar[s], kb * kBK, p.F + j0);
+              tma_load_2d(sb, &map_b, &full_bar[s], kb * kKE, j0);
+              tma_load_2d(sb + (BN / 2) * kBK, &map_b, &full_bar[s], kb * kKE, p.F + j0);
             } else {
-              tma_load_2d(sb, &map_b, &full_bar[s], kb * kBK, n_tile * BN);
+              tma_load_2d(sb, &map_b, &full_bar[s], kb * kKE, n_tile * BN);
             }
           }
         }
@@ -238,14 +304,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
-        int kb_begin = 0;
-        if constexpr (AM == AMode::kConv5D) {
-          if (p.causal) {
-            const int m_tile = tile / p.n_tiles;
-            const int od = (m_tile / (p.w_tiles * p.h_tiles)) % p.Do;
-            if (od < 2) kb_begin = (2 - od) * p.kh * p.kw * p.c_chunks;
-          }
-        }
+        const int kb_begin = first_kblock(tile / p.n_tiles);
         const uint32_t acc = local & 1u;
         const uint32_t aph = (local >> 1) & 1u;
         if (!mbar_wait(&tempty_bar[acc], aph ^ 1u, abort_flag)) { ok = false; break; }
@@ -256,12 +315,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(&full_bar[s], ph, abort_flag)) { ok = false; break; }
           tc_fence_after();
-          const uint64_t adesc = make_sw128_desc(smem_u32(smem_a + s * kATileBytes));
           const uint64_t bdesc = make_sw128_desc(smem_u32(smem_b + s * kBTileBytes));
 #pragma unroll
-          for (int k = 0; k < kBK / 32; ++k) {
-            // Advance the start address by 32 bytes (2 x 16 B) per K=32 step.
-            mma_i8(d_tmem, adesc + 2 * k, bdesc + 2 * k, kIdesc, (kb > kb_begin || k > 0) ? 1u : 0u);
+          for (int i = 0; i < MT; ++i) {
+            const uint64_t adesc = make_sw128_desc(smem_u32(smem_a + s * kAStageBytes + i * kATileBytes));
+#pragma unroll
+            for (int k = 0; k < kBK / 32; ++k) {
+              // Advance the start address by 32 bytes (2 x 16 B) per MMA K step.
+              const uint32_t accumulate = (kb > kb_begin || k > 0) ? 1u : 0u;
+              if constexpr (F16)
+                mma_f16(d_tmem + i * BN, adesc + 2 * k, bdesc + 2 * k, kIdesc, accumulate);
+              else
+                mma_i8(d_tmem + i * BN, adesc + 2 * k, bdesc + 2 * k, kIdesc, accumulate);
+            }
           }
           tc_commit(&empty_bar[s]);
         }
@@ -276,72 +342,77 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int half = (warp - 2) >> 2;   // 0 / 1: which alternate column chunks this warp owns
     uint32_t local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int m_tile = tile / p.n_tiles;
-      const int n_tile = tile - m_tile * p.n_tiles;
+      const int m_group = tile / p.n_tiles;
+      const int n_tile = tile - m_group * p.n_tiles;
       const uint32_t acc = local & 1u;
       const uint32_t aph = (local >> 1) & 1u;
       if (!mbar_wait(&tfull_bar[acc], aph, abort_flag)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem_base + acc * kAccStride + (static_cast<uint32_t>(quad * 32) << 16);
+      const uint32_t t_acc = tmem_base + acc * kAccStride + (static_cast<uint32_t>(quad * 32) << 16);
 
       if constexpr (EP == Epi::kLinear) {
-        const int64_t m = static_cast<int64_t>(m_tile) * kBM + row;
-        const bool valid = m < p.M;
-        const float sx = valid ? p.a_scale[m] : 0.0f;
-        const bool vec_ok = (p.ldo % 8) == 0;
 #pragma unroll 1
-        for (int c = half; c < BN / 32; c += 2) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * 32, r);
-          tmem_ld_wait();
-          const int n0 = n_tile * BN + c * 32;
-          const int valid_cols = p.N - n0;
-          if (valid && valid_cols > 0) {
-            float v[32];
+        for (int i = 0; i < MT; ++i) {
+          const uint32_t t_row = t_acc + i * BN;
+          const int64_t m = static_cast<int64_t>(m_group * MT + i) * kBM + row;
+          const bool valid = m < p.M;
+          const float sx = valid ? p.a_scale[m] : 0.0f;
+          const bool vec_ok = (p.ldo % 8) == 0;
+#pragma unroll 1
+          for (int c = half; c < BN / 32; c += 2) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c * 32, r);
+            tmem_ld_wait();
+            const int n0 = n_tile * BN + c * 32;
+            const int valid_cols = p.N - n0;
+            if (valid && valid_cols > 0) {
+              float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = min(n0 + j, p.N - 1);
-              v[j] = dequant(r[j], sx, p.w_scale[n], p.bias, n);
+              for (int j = 0; j < 32; ++j) {
+                const int n = min(n0 + j, p.N - 1);
+                v[j] = dequant(r[j], sx, p.w_scale[n], p.bias, n);
+              }
+              store_row_chunk(p.out + m * p.ldo + n0, v, valid_cols, vec_ok);
+              if (p.acc_out != nullptr) store_acc_chunk(p.acc_out + m * p.N + n0, r, valid_cols);
             }
-            store_row_chunk(p.out + m * p.ldo + n0, v, valid_cols, vec_ok);
-            if (p.acc_out != nullptr) store_acc_chunk(p.acc_out + m * p.N + n0, r, valid_cols);
           }
         }
       } else if constexpr (EP == Epi::kConv) {
-        int t = m_tile;
-        const int tw = t % p.w_tiles; t /= p.w_tiles;
-        const int th = t % p.h_tiles; t /= p.h_tiles;
-        const int od = t % p.Do;
-        const int b = t / p.Do;
-        const int oh = th * p.bh + row / p.bw;
-        const int ow = tw * p.bw + row % p.bw;
-        const bool valid = (oh < p.Ho) && (ow < p.Wo);
-        const float sx = *p.a_scale;
-        const int64_t obase = b * p.osB + od * p.osD + static_cast<int64_t>(oh) * p.osH + static_cast<int64_t>(ow) * p.osW;
-        const int64_t pos = ((static_cast<int64_t>(b) * p.Do + od) * p.Ho + oh) * p.Wo + ow;
+        const float sx = F16 ? 0.0f : *p.a_scale;
         const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0) && (p.osW % 8 == 0) &&
                             (p.osH % 8 == 0) && (p.osD % 8 == 0) && (p.osB % 8 == 0);
 #pragma unroll 1
-        for (int c = half; c < BN / 32; c += 2) {
-          uint32_t r[32];
-          tmem_ld32(t_row + c * 32, r);
-          tmem_ld_wait();
-          const int n0 = n_tile * BN + c * 32;
-          const int valid_cols = p.N - n0;
-          if (valid && valid_cols > 0) {
-            float v[32];
+        for (int i = 0; i < MT; ++i) {
+          const uint32_t t_row = t_acc + i * BN;
+          const int mt = m_group * MT + i;
+          int b, od, oh0, ow0;
+          conv_tile(mt, b, od, oh0, ow0);
+          const int oh = oh0 + row / p.bw;
+          const int ow = ow0 + row % p.bw;
+          const bool valid = (mt < p.m_tiles) && (oh < p.Ho) && (ow < p.Wo);
+          const int64_t obase =
+              b * p.osB + od * p.osD + static_cast<int64_t>(oh) * p.osH + static_cast<int64_t>(ow) * p.osW;
+          const int64_t pos = ((static_cast<int64_t>(b) * p.Do + od) * p.Ho + oh) * p.Wo + ow;
+#pragma unroll 1
+          for (int c = half; c < BN / 32; c += 2) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c * 32, r);
+            tmem_ld_wait();
+            const int n0 = n_tile * BN + c * 32;
+            const int valid_cols = p.N - n0;
+            if (valid && valid_cols > 0) {
+              float v[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = min(n0 + j, p.N - 1);
-              v[j] = dequant(r[j], sx, p.w_scale[n], p.bias, n);
+              for (int j = 0; j < 32; ++j) v[j] = epi_value<F16>(r[j], sx, p.w_scale, p.bias, min(n0 + j, p.N - 1));
+              if (p.residual != nullptr) add_residual_chunk(v, p.residual + obase + n0, valid_cols, vec_ok);
+              store_row_chunk(p.out + obase + n0, v, valid_cols, vec_ok);
+              if (!F16 && p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
             }
-            if (p.residual != nullptr) add_residual_chunk(v, p.residual + obase + n0, valid_cols, vec_ok);
-            store_row_chunk(p.out + obase + n0, v, valid_cols, vec_ok);
-            if (p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
           }
         }
       } else if constexpr (EP == Epi::kSwiGLU) {
-        const int64_t m = static_cast<int64_t>(m_tile) * kBM + row;
+        const uint32_t t_row = t_acc;
+        const int64_t m = static_cast<int64_t>(m_group) * kBM + row;
         const bool valid = m < p.M;
         const float sx = valid ? p.a_scale[m] : 0.0f;
         const bool vec_ok = (p.F % 8) == 0;
@@ -368,7 +439,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else if constexpr (EP == Epi::kQkvRope) {
         // BN == 192: this tile is one head's [q | k | v] for 128 tokens.
-        const int64_t m = static_cast<int64_t>(m_tile) * kBM + row;
+        const uint32_t t_row = t_acc;
+        const int64_t m = static_cast<int64_t>(m_group) * kBM + row;
         const bool valid = m < p.M;
         const float sx = valid ? p.a_scale[m] : 0.0f;
         const int h = n_tile;
@@ -466,15 +538,15 @@ namespace {
 
 using namespace h3b;
 
-template <int BN, int STAGES, AMode AM, Epi EP>
+template <int BN, int STAGES, AMode AM, Epi EP, int MT = 1, bool F16 = false>
 int launch_mma(const CUtensorMap& ma, const CUtensorMap& mb, const MmaParams& p, cudaStream_t stream,
                const char* name) {
-  constexpr size_t smem = STAGES * (kATileBytes + BN * kBK) + 1024 + 256;
+  constexpr size_t smem = STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256;
   static_assert(smem <= 232448, "shared memory budget");
-  auto kern = mma_i8_kernel<BN, STAGES, AM, EP>;
+  auto kern = mma_tc_kernel<BN, STAGES, AM, EP, MT, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return h3b_host::set_error(H3B_ECUDA, "%s: smem attribute: %s", name, cudaGetErrorString(e));
-  const int tiles = p.m_tiles * p.n_tiles;
+  const int tiles = p.m_groups * p.n_tiles;
   if (tiles <= 0) return H3B_OK;
   const int grid = tiles < h3b_host::num_sms() ? tiles : h3b_host::num_sms();
   kern<<<grid, kThreads, smem, stream>>>(ma, mb, p);
@@ -510,6 +582,118 @@ int check_gemm_common(const int8_t* qa, const float* a_scale, const int8_t* qw, 
   return H3B_OK;
 }
 
+// Shared host side of the INT8 and fp16 implicit-GEMM convs: geometry checks,
+// tile shape, tensor maps (5-D im2col boxes with element strides for the
+// conv stride), kernel choice.  elt = operand bytes (1 or 2).
+struct ConvArgs {
+  const void* x;
+  const int64_t* x_dims;
+  const void* w;
+  int64_t O;
+  int kd, kh, kw, sd, sh, sw;
+  const float* x_scale;
+  const float* w_scale;
+  const void* bias;
+  void* out;
+  const int64_t* out_strides;
+  const void* residual;
+  int32_t* acc_out;
+  int causal_zero_frames;
+  cudaStream_t stream;
+};
+
+int check_conv_geometry(const ConvArgs& a, const char* name, int64_t* dims6) {
+  if (!a.x || !a.x_dims || !a.w || !a.out || !a.out_strides)
+    return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  const int64_t B = a.x_dims[0], D = a.x_dims[1], H = a.x_dims[2], W = a.x_dims[3], C = a.x_dims[4];
+  if (B <= 0 || D <= 0 || H <= 0 || W <= 0 || C <= 0 || a.O <= 0)
+    return h3b_host::set_error(H3B_EINVAL, "%s: empty tensor", name);
+  for (int k : {a.kd, a.kh, a.kw})
+    if (k != 1 && k != 3) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: kernel dims must be 1 or 3", name);
+  for (int s : {a.sd, a.sh, a.sw})
+    if (s != 1 && s != 2) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: strides must be 1 or 2", name);
+  if (a.causal_zero_frames != 0 && a.causal_zero_frames != 2)
+    return h3b_host::set_error(H3B_EINVAL, "%s: causal_zero_frames must be 0 or 2", name);
+  if (D < a.kd || H < a.kh || W < a.kw) return h3b_host::set_error(H3B_EINVAL, "%s: input too small for valid conv", name);
+  const int64_t Do = (D - a.kd) / a.sd + 1, Ho = (H - a.kh) / a.sh + 1, Wo = (W - a.kw) / a.sw + 1;
+  if (B * D * H * W * C >= (int64_t(1) << 40) || B * Do * Ho * Wo * a.O >= (int64_t(1) << 40))
+    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: tensor too large", name);
+  if (a.residual != nullptr &&
+      (reinterpret_cast<uintptr_t>(a.residual) & 15u) != (reinterpret_cast<uintptr_t>(a.out) & 15u))
+    return h3b_host::set_error(H3B_EINVAL, "%s: residual and out must share 16-byte alignment", name);
+  dims6[0] = Do; dims6[1] = Ho; dims6[2] = Wo;
+  return H3B_OK;
+}
+
+template <bool F16>
+int conv3d_tc(const ConvArgs& a, int64_t Do, int64_t Ho, int64_t Wo, const char* name) {
+  constexpr int kElt = F16 ? 2 : 1;
+  constexpr int kKE = kBK / kElt;
+  const int64_t B = a.x_dims[0], D = a.x_dims[1], H = a.x_dims[2], W = a.x_dims[3], C = a.x_dims[4];
+  const int64_t taps = static_cast<int64_t>(a.kd) * a.kh * a.kw;
+  MmaParams p{};
+  int bw = 1;
+  while (bw < Wo && bw < kBM) bw <<= 1;
+  const int bh = kBM / bw;
+  p.B = (int)B; p.Do = (int)Do; p.Ho = (int)Ho; p.Wo = (int)Wo;
+  p.kd = a.kd; p.kh = a.kh; p.kw = a.kw; p.sd = a.sd; p.sh = a.sh; p.sw = a.sw;
+  p.taps = (int)taps; p.C = (int)C; p.c_chunks = (int)(C / kKE);
+  p.bw = bw; p.bh = bh;
+  p.w_tiles = (int)((Wo + bw - 1) / bw);
+  p.h_tiles = (int)((Ho + bh - 1) / bh);
+  p.causal = (a.causal_zero_frames == 2 && a.kd == 3) ? 1 : 0;
+  p.N = (int)a.O;
+  p.K = (int)(taps * C);
+  p.k_blocks = p.taps * p.c_chunks;
+  p.m_tiles = (int)(B * Do) * p.h_tiles * p.w_tiles;
+  p.a_scale = a.x_scale; p.w_scale = a.w_scale; p.bias = static_cast<const __half*>(a.bias);
+  p.out = static_cast<__half*>(a.out);
+  p.osB = a.out_strides[0]; p.osD = a.out_strides[1]; p.osH = a.out_strides[2]; p.osW = a.out_strides[3];
+  p.acc_out = a.acc_out;
+  p.residual = static_cast<const __half*>(a.residual);
+
+  const CUtensorMapDataType dt = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUtensorMap ma, mb;
+  uint64_t adims[5] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)D, (uint64_t)B};
+  uint64_t astr[4] = {(uint64_t)(C * kElt), (uint64_t)(C * W * kElt), (uint64_t)(C * W * H * kElt),
+                      (uint64_t)(C * W * H * D * kElt)};
+  // With element strides {1, sw, sh} the box spans bw*sw x bh*sh pixels and
+  // loads every sw-th / sh-th one: bw x bh rows of 128 bytes.
+  uint32_t abox[5] = {(uint32_t)kKE, (uint32_t)(bw * a.sw), (uint32_t)(bh * a.sh), 1, 1};
+  uint32_t aes[5] = {1, (uint32_t)a.sw, (uint32_t)a.sh, 1, 1};
+  int rc = h3b_host::encode_tiled(&ma, dt, 5, a.x, adims, astr, abox, aes, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  uint32_t es[2] = {1, 1};
+  uint64_t bdims[2] = {(uint64_t)(taps * C), (uint64_t)a.O};
+  uint64_t bstr[1] = {(uint64_t)(taps * C * kElt)};
+  auto b_map = [&](uint32_t rows) {
+    uint32_t bbox[2] = {(uint32_t)kKE, rows};
+    return h3b_host::encode_tiled(&mb, dt, 2, a.w, bdims, bstr, bbox, es, CU_TENSOR_MAP_SWIZZLE_128B);
+  };
+  const int sms = h3b_host::num_sms();
+  if (a.O <= 64) {
+    p.n_tiles = 1;
+    p.m_groups = (p.m_tiles + 1) / 2;
+    if ((rc = b_map(64))) return rc;
+    return launch_mma<64, 5, AMode::kConv5D, Epi::kConv, 2, F16>(ma, mb, p, a.stream, name);
+  }
+  if (a.O <= 128) {
+    p.n_tiles = 1;
+    if ((rc = b_map(128))) return rc;
+    // Two M tiles per CTA share the B tile when there is enough work to fill the SMs.
+    if ((p.m_tiles + 1) / 2 >= sms) {
+      p.m_groups = (p.m_tiles + 1) / 2;
+      return launch_mma<128, 4, AMode::kConv5D, Epi::kConv, 2, F16>(ma, mb, p, a.stream, name);
+    }
+    p.m_groups = p.m_tiles;
+    return launch_mma<128, 6, AMode::kConv5D, Epi::kConv, 1, F16>(ma, mb, p, a.stream, name);
+  }
+  p.n_tiles = (int)((a.O + 255) / 256);
+  p.m_groups = p.m_tiles;
+  if ((rc = b_map(256))) return rc;
+  return launch_mma<256, 4, AMode::kConv5D, Epi::kConv, 1, F16>(ma, mb, p, a.stream, name);
+}
+
 }  // namespace
 
 extern "C" {
@@ -519,89 +703,46 @@ int h3b_conv3d_i8(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int
                   void* out, const int64_t* out_strides, const void* residual, int32_t* acc_out,
                   int causal_zero_frames, h3b_stream_t stream) {
   const char* name = "h3b_conv3d_i8";
-  if (!qx || !x_dims || !qw || !x_scale || !w_scale || !out || !out_strides)
-    return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  ConvArgs a{qx, x_dims, qw, out_channels, kd, kh, kw, sd, sh, sw, x_scale, w_scale, bias, out, out_strides,
+             residual, acc_out, causal_zero_frames, reinterpret_cast<cudaStream_t>(stream)};
+  if (!x_scale || !w_scale) return h3b_host::set_error(H3B_EINVAL, "%s: NULL scale", name);
+  int64_t o3[3];
+  int rc = check_conv_geometry(a, name, o3);
+  if (rc) return rc;
   const int64_t B = x_dims[0], D = x_dims[1], H = x_dims[2], W = x_dims[3], C = x_dims[4];
-  const int64_t O = out_channels;
-  if (B <= 0 || D <= 0 || H <= 0 || W <= 0 || C <= 0 || O <= 0)
-    return h3b_host::set_error(H3B_EINVAL, "%s: empty tensor", name);
-  for (int k : {kd, kh, kw})
-    if (k != 1 && k != 3) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: kernel dims must be 1 or 3", name);
-  for (int s : {sd, sh, sw})
-    if (s != 1 && s != 2) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: strides must be 1 or 2", name);
-  if (causal_zero_frames != 0 && causal_zero_frames != 2)
-    return h3b_host::set_error(H3B_EINVAL, "%s: causal_zero_frames must be 0 or 2", name);
-  const int64_t Do = (D - kd) / sd + 1, Ho = (H - kh) / sh + 1, Wo = (W - kw) / sw + 1;
-  if (D < kd || H < kh || W < kw) return h3b_host::set_error(H3B_EINVAL, "%s: input too small for valid conv", name);
+  const int64_t Do = o3[0], Ho = o3[1], Wo = o3[2], O = out_channels;
   const int64_t taps = static_cast<int64_t>(kd) * kh * kw;
   if (taps * C * 127 * 127 >= (int64_t(1) << 31))
     return h3b_host::set_error(H3B_EINVAL, "%s: INT32 accumulator bound exceeds signed INT32 range", name);
-  if (B * D * H * W * C >= (int64_t(1) << 40) || B * Do * Ho * Wo * O >= (int64_t(1) << 40))
-    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: tensor too large", name);
-
-  const __half* bias_h = static_cast<const __half*>(bias);
-  __half* out_h = static_cast<__half*>(out);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-
-  const bool tma_path = (C % kBK == 0) && sd == 1 && sh == 1 && sw == 1 && B * Do <= (int64_t(1) << 30);
+  const bool tma_path = (C % kBK == 0) && B * Do <= (int64_t(1) << 30);
   if (!tma_path) {
     const int64_t total = B * Do * Ho * Wo * O;
     const int threads = 256;
     int64_t blocks = (total + threads - 1) / threads;
     if (blocks > 65535LL * 16) blocks = 65535LL * 16;
-    conv3d_i8_simt_kernel<<<static_cast<unsigned>(blocks), threads, 0, st>>>(
+    conv3d_i8_simt_kernel<<<static_cast<unsigned>(blocks), threads, 0, a.stream>>>(
         qx, (int)B, (int)D, (int)H, (int)W, (int)C, qw, (int)O, kd, kh, kw, sd, sh, sw, (int)Do, (int)Ho, (int)Wo,
-        x_scale, w_scale, bias_h, out_h, out_strides[0], out_strides[1], out_strides[2], out_strides[3], acc_out,
-        static_cast<const __half*>(residual));
+        x_scale, w_scale, static_cast<const __half*>(bias), static_cast<__half*>(out), out_strides[0],
+        out_strides[1], out_strides[2], out_strides[3], acc_out, static_cast<const __half*>(residual));
     return h3b_host::check_launch(name);
   }
+  return conv3d_tc<false>(a, Do, Ho, Wo, name);
+}
 
-  MmaParams p{};
-  int bw = 1;
-  while (bw < Wo && bw < kBM) bw <<= 1;
-  const int bh = kBM / bw;
-  p.B = (int)B; p.Do = (int)Do; p.Ho = (int)Ho; p.Wo = (int)Wo;
-  p.kd = kd; p.kh = kh; p.kw = kw; p.taps = (int)taps; p.C = (int)C; p.c_chunks = (int)(C / kBK);
-  p.bw = bw; p.bh = bh;
-  p.w_tiles = (int)((Wo + bw - 1) / bw);
-  p.h_tiles = (int)((Ho + bh - 1) / bh);
-  p.causal = (causal_zero_frames == 2 && kd == 3) ? 1 : 0;
-  p.N = (int)O;
-  p.K = (int)(taps * C);
-  p.k_blocks = p.taps * p.c_chunks;
-  p.m_tiles = (int)(B * Do) * p.h_tiles * p.w_tiles;
-  p.a_scale = x_scale; p.w_scale = w_scale; p.bias = bias_h;
-  p.out = out_h;
-  p.osB = out_strides[0]; p.osD = out_strides[1]; p.osH = out_strides[2]; p.osW = out_strides[3];
-  p.acc_out = acc_out;
-  p.residual = static_cast<const __half*>(residual);
-  if (residual != nullptr && (reinterpret_cast<uintptr_t>(residual) & 15u) != (reinterpret_cast<uintptr_t>(out) & 15u))
-    return h3b_host::set_error(H3B_EINVAL, "%s: residual and out must share 16-byte alignment", name);
-
-  CUtensorMap ma, mb;
-  uint64_t adims[5] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)D, (uint64_t)B};
-  uint64_t astr[4] = {(uint64_t)C, (uint64_t)(C * W), (uint64_t)(C * W * H), (uint64_t)(C * W * H * D)};
-  uint32_t abox[5] = {kBK, (uint32_t)bw, (uint32_t)bh, 1, 1};
-  uint32_t es[5] = {1, 1, 1, 1, 1};
-  int rc = h3b_host::encode_tiled(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, qx, adims, astr, abox, es,
-                                  CU_TENSOR_MAP_SWIZZLE_128B);
+int h3b_conv3d_f16(const void* x, const int64_t* x_dims, const void* w, int64_t out_channels, int kd, int kh, int kw,
+                   int sd, int sh, int sw, const void* bias, void* out, const int64_t* out_strides,
+                   const void* residual, int causal_zero_frames, h3b_stream_t stream) {
+  const char* name = "h3b_conv3d_f16";
+  ConvArgs a{x, x_dims, w, out_channels, kd, kh, kw, sd, sh, sw, nullptr, nullptr, bias, out, out_strides,
+             residual, nullptr, causal_zero_frames, reinterpret_cast<cudaStream_t>(stream)};
+  int64_t o3[3];
+  int rc = check_conv_geometry(a, name, o3);
   if (rc) return rc;
-  if (O <= 128) {
-    p.n_tiles = 1;
-    uint64_t bdims[2] = {(uint64_t)(taps * C), (uint64_t)O};
-    uint64_t bstr[1] = {(uint64_t)(taps * C)};
-    uint32_t bbox[2] = {kBK, 128};
-    rc = h3b_host::encode_tiled(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qw, bdims, bstr, bbox, es, CU_TENSOR_MAP_SWIZZLE_128B);
-    if (rc) return rc;
-    return launch_mma<128, 6, AMode::kConv5D, Epi::kConv>(ma, mb, p, st, name);
-  }
-  p.n_tiles = (int)((O + 255) / 256);
-  uint64_t bdims[2] = {(uint64_t)(taps * C), (uint64_t)O};
-  uint64_t bstr[1] = {(uint64_t)(taps * C)};
-  uint32_t bbox[2] = {kBK, 256};
-  rc = h3b_host::encode_tiled(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qw, bdims, bstr, bbox, es, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  return launch_mma<256, 4, AMode::kConv5D, Epi::kConv>(ma, mb, p, st, name);
+  const int64_t C = x_dims[4];
+  if (C % 64 != 0)
+    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: C=%lld must be a multiple of 64", name, (long long)C);
+  if (x_dims[0] * o3[0] > (int64_t(1) << 30)) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: too many frames", name);
+  return conv3d_tc<true>(a, o3[0], o3[1], o3[2], name);
 }
 
 int h3b_gemm_i8(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale, const void* bias,
@@ -614,6 +755,7 @@ int h3b_gemm_i8(const int8_t* qa, const float* a_scale, const int8_t* qw, const 
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.k_blocks = (int)((K + kBK - 1) / kBK);
   p.m_tiles = (int)((M + kBM - 1) / kBM);
+  p.m_groups = p.m_tiles;
   p.a_scale = a_scale; p.w_scale = w_scale; p.bias = static_cast<const __half*>(bias);
   p.out = static_cast<__half*>(out); p.ldo = ldo; p.acc_out = acc_out;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
@@ -642,6 +784,7 @@ int h3b_gemm_i8_swiglu(const int8_t* qa, const float* a_scale, const int8_t* qw,
   p.M = (int)M; p.N = (int)(2 * F); p.K = (int)K; p.F = (int)F;
   p.k_blocks = (int)((K + kBK - 1) / kBK);
   p.m_tiles = (int)((M + kBM - 1) / kBM);
+  p.m_groups = p.m_tiles;
   p.n_tiles = (int)((F + 127) / 128);
   p.a_scale = a_scale; p.w_scale = w_scale; p.bias = static_cast<const __half*>(bias);
   p.out = static_cast<__half*>(act);
@@ -671,6 +814,7 @@ int h3b_gemm_i8_qkv_rope(const int8_t* qa, const float* a_scale, const int8_t* q
   p.M = (int)M; p.N = (int)N; p.K = (int)K;
   p.k_blocks = (int)((K + kBK - 1) / kBK);
   p.m_tiles = (int)((M + kBM - 1) / kBM);
+  p.m_groups = p.m_tiles;
   p.n_tiles = (int)heads;
   p.heads = (int)heads; p.tokens = (int)tokens; p.R = (int)rot_dims; p.eps = eps;
   p.cos_t = static_cast<const __half*>(cos_t); p.sin_t = static_cast<const __half*>(sin_t);

@@ -135,6 +135,48 @@ def conv3d_i8(qx: torch.Tensor, x_scale: torch.Tensor, qweight: torch.Tensor, we
     return out
 
 
+def pack_conv_weight_f16(weight: torch.Tensor) -> torch.Tensor:
+    """[O, C, kd, kh, kw] -> fp16 [O, kd*kh*kw*C] (tap-major, channel-minor), the B operand layout."""
+    o = weight.shape[0]
+    return weight.detach().permute(0, 2, 3, 4, 1).reshape(o, -1).to(F16).contiguous()
+
+
+def conv3d_f16(x: torch.Tensor, wpacked: torch.Tensor, bias: torch.Tensor | None, kernel: tuple[int, int, int],
+               stride: tuple[int, int, int] = (1, 1, 1), *, causal_zero_frames: int = 0,
+               residual: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Valid fp16 conv3d (fp32 accumulate) of a padded NDHWC fp16 activation (logical [B,C,D,H,W])
+    on the tcgen05 tensor cores; bias and the optional residual add are fused in the epilogue."""
+    dev = _require_cuda(x, wpacked, bias, residual, out)
+    if x.ndim != 5 or x.dtype != F16 or not is_ndhwc(x):
+        raise ValueError("x must be a channels_last_3d fp16 [B,C,D,H,W] tensor")
+    _require(wpacked, F16, "weight")
+    _require(bias, F16, "bias")
+    b, c, d, h, w = x.shape
+    kd, kh, kw = (int(k) for k in kernel)
+    sd, sh, sw = (int(s) for s in stride)
+    o = wpacked.shape[0]
+    if wpacked.ndim != 2 or wpacked.shape[1] != kd * kh * kw * c:
+        raise ValueError(f"weight shape {tuple(wpacked.shape)} != packed {(o, kd * kh * kw * c)}")
+    if bias is not None and bias.shape != (o,):
+        raise ValueError("bias must be [out_channels]")
+    do, ho, wo = (d - kd) // sd + 1, (h - kh) // sh + 1, (w - kw) // sw + 1
+    if min(do, ho, wo) <= 0:
+        raise ValueError(f"input shape {tuple(x.shape)} is too small for valid conv")
+    if out is None:
+        out = torch.empty((b, o, do, ho, wo), device=dev, dtype=F16, memory_format=torch.channels_last_3d)
+    elif out.shape != (b, o, do, ho, wo) or out.dtype != F16 or out.stride(1) != 1:
+        raise ValueError("out must be fp16 [B,O,Do,Ho,Wo] with unit channel stride")
+    if residual is not None and (residual.dtype != F16 or residual.shape != out.shape
+                                 or residual.stride() != out.stride()):
+        raise ValueError("residual must be fp16 with the output's shape and strides")
+    _lib.check(_lib.load().h3b_conv3d_f16(
+        x.data_ptr(), _lib.i64_array((b, d, h, w, c)), wpacked.data_ptr(), o, kd, kh, kw, sd, sh, sw, _ptr(bias),
+        out.data_ptr(), _lib.i64_array((out.stride(0), out.stride(2), out.stride(3), out.stride(4))),
+        _ptr(residual), int(causal_zero_frames), _stream(dev)))
+    _count(1)
+    return out
+
+
 def quantize_tensor_i8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-tensor half-away INT8 quantization of fp16 [B,C,D,H,W] (any strides) to NDHWC int8."""
     dev = _require_cuda(x)

@@ -80,6 +80,27 @@ def conv_f16(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, stride=(1
     return F.conv3d(x, w, b, stride=stride).contiguous(memory_format=CL3)
 
 
+class Conv3dF16:
+    """One fp16 valid conv of the model.  Channel counts that are a multiple of 64 run on the
+    tcgen05 fp16 implicit-GEMM kernel (bias and an optional residual add fused, stride-2 through
+    TMA element strides); the three narrow-input convs (3-channel pixels, 16-channel latents,
+    the 32-channel quant conv) stay on cuDNN."""
+
+    def __init__(self, w: torch.Tensor, b: torch.Tensor | None, stride=(1, 1, 1)):
+        self.w, self.b, self.stride = w, b, tuple(stride)
+        self.kernel = tuple(int(k) for k in w.shape[2:])
+        self.packed = K.pack_conv_weight_f16(w) if w.shape[1] % 64 == 0 else None
+
+    def __call__(self, x: torch.Tensor, *, residual: torch.Tensor | None = None, causal: bool = False,
+                 bias: bool = True) -> torch.Tensor:
+        b = self.b if bias else None
+        if self.packed is not None:
+            return K.conv3d_f16(K.ndhwc(x), self.packed, b, self.kernel, self.stride,
+                                causal_zero_frames=2 if causal else 0, residual=residual)
+        y = conv_f16(x, self.w, b, self.stride)
+        return y if residual is None else (y + residual).contiguous(memory_format=CL3)
+
+
 def _randn(gen, shape, std, device, dtype=torch.float16):
     return (torch.randn(*shape, generator=gen) * std).to(device=device, dtype=dtype)
 
@@ -131,11 +152,14 @@ class _ResBlock:
         if int8:
             self.q1, self.s1 = prepare_int8_weight(self.w1)
             self.q2, self.s2 = prepare_int8_weight(self.w2)
+        self.conv1 = Conv3dF16(self.w1, self.b1)
+        self.conv2 = Conv3dF16(self.w2, self.b2)
+        self.nin = Conv3dF16(self.nin_w, self.nin_b) if self.nin_w is not None else None
 
     def shortcut(self, x):
-        if self.nin_w is None:
+        if self.nin is None:
             return x
-        return conv_f16(x, self.nin_w, self.nin_b)
+        return self.nin(x)
 
     def __call__(self, x: torch.Tensor, *, pack_for_downsample: bool) -> torch.Tensor:
         """Returns the block output, or when pack_for_downsample the residual-packed (padded) tensor
@@ -150,11 +174,11 @@ class _ResBlock:
                 return K.residual_pack(h2, skip, self.b2)
             return K.conv3d_i8(q2, s2, self.q2, self.s2, self.b2, (3, 3, 3), causal_zero_frames=2, residual=skip)
         y1 = K.norm_pad_f16(x, self.gn1_w, self.gn1_b, self.eps)
-        h = conv_f16(y1, self.w1, None)
+        h = self.conv1(y1, bias=False, causal=True)
         y2 = K.norm_pad_f16(h, self.gn2_w, self.gn2_b, self.eps, pre_bias=self.b1)
         if pack_for_downsample:
-            return K.residual_pack(conv_f16(y2, self.w2, None), skip, self.b2)
-        return (conv_f16(y2, self.w2, self.b2) + skip).contiguous(memory_format=CL3)
+            return K.residual_pack(self.conv2(y2, bias=False, causal=True), skip, self.b2)
+        return self.conv2(y2, causal=True, residual=skip)
 
 
 class H3Encoder:
@@ -180,7 +204,7 @@ class H3Encoder:
                 stride = (2 if cfg.temporal_down[s] else 1, 2 if cfg.spatial_down[s] else 1,
                           2 if cfg.spatial_down[s] else 1)
                 w = _randn(gen, (cout, cout, 3, 3, 3), 1.0 / math.sqrt(cout * 27), device).contiguous(memory_format=CL3)
-                self.down.append((w, _randn(gen, (cout,), 0.02, device), stride))
+                self.down.append(Conv3dF16(w, _randn(gen, (cout,), 0.02, device), stride))
             else:
                 self.down.append(None)
         cl = cfg.channels[-1]
@@ -192,6 +216,7 @@ class H3Encoder:
         lc = 2 * cfg.latent_channels
         self.quant_w = _randn(gen, (lc, lc, 1, 1, 1), 1.0 / math.sqrt(lc), device).contiguous(memory_format=CL3)
         self.quant_b = _randn(gen, (lc,), 0.02, device)
+        self.conv_out = Conv3dF16(self.conv_out_w, self.conv_out_b)
 
     @property
     def int8_conv_count(self) -> int:
@@ -209,11 +234,11 @@ class H3Encoder:
                 last = j == len(blocks) - 1
                 h = blk(h, pack_for_downsample=last and down is not None)
             if down is not None:
-                # h is the residual-packed [B,C,D+2,H+1,W+1] tensor: valid strided conv
-                w, b, stride = down
-                h = conv_f16(h, w, b, stride)
+                # h is the residual-packed [B,C,D+2,H+1,W+1] tensor (two zero frames in front):
+                # valid strided conv
+                h = down(h, causal=True)
         y = K.norm_pad_f16(h, self.norm_out_w, self.norm_out_b, self.cfg.eps)
-        moments = conv_f16(y, self.conv_out_w, self.conv_out_b)
+        moments = self.conv_out(y, causal=True)
         return conv_f16(moments, self.quant_w, self.quant_b)
 
 
@@ -296,6 +321,7 @@ class H3Decoder:
         self.ln_w = (1.0 + 0.1 * torch.randn(d, generator=gen)).half().to(device)
         self.ln_b = (0.1 * torch.randn(d, generator=gen)).half().to(device)
         self.up = []
+        self.up_convs: list[Conv3dF16] = []
         cin = d
         for cout in cfg.up_channels:
             gw = (1.0 + 0.1 * torch.randn(cin, generator=gen)).half().to(device)
@@ -303,12 +329,14 @@ class H3Decoder:
             w = _randn(gen, (cout, cin, 3, 3, 3), 1.0 / math.sqrt(cin * 27), device).contiguous(memory_format=CL3)
             b = _randn(gen, (cout,), 0.02, device)
             self.up.append((gw, gb, w, b))
+            self.up_convs.append(Conv3dF16(w, b))
             cin = cout
         self.out_gn_w = (1.0 + 0.1 * torch.randn(cin, generator=gen)).half().to(device)
         self.out_gn_b = (0.1 * torch.randn(cin, generator=gen)).half().to(device)
         self.conv_out_w = _randn(gen, (cfg.out_channels, cin, 3, 3, 3), 1.0 / math.sqrt(cin * 27),
                                  device).contiguous(memory_format=CL3)
         self.conv_out_b = _randn(gen, (cfg.out_channels,), 0.02, device)
+        self.conv_out = Conv3dF16(self.conv_out_w, self.conv_out_b)
         self._rope_cache: dict = {}
 
     @property
@@ -411,8 +439,8 @@ class H3Decoder:
                                                  cfg.up_temporal)):
             gw, gb = gns[k]
             y = K.upsample_norm_pad_f16(x, gw, gb, cfg.gn_eps, spatial=up_s, temporal=up_t, pre_bias=pending_bias)
-            x = conv_f16(y, wt, None)
+            x = self.up_convs[k](y, bias=False, causal=True)
             pending_bias, up_s, up_t = bs, sp, tp
         y = K.upsample_norm_pad_f16(x, self.out_gn_w, self.out_gn_b, cfg.gn_eps, spatial=up_s, temporal=up_t,
                                     pre_bias=pending_bias)
-        return conv_f16(y, self.conv_out_w, self.conv_out_b)
+        return self.conv_out(y, causal=True)

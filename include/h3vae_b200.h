@@ -70,6 +70,28 @@ int h3b_conv3d_i8(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int
                   const float* w_scale, const void* bias, void* out, const int64_t* out_strides,
                   const void* residual, int32_t* acc_out, int causal_zero_frames, h3b_stream_t stream);
 
+/* fp16 valid conv3d on the tensor cores (tcgen05 kind::f16, fp32 accumulate):
+ * the encoder/decoder convolutions outside the INT8 scope -- stride-2
+ * downsample convs, 1x1x1 shortcuts, conv_out, the decoder's upsampling convs.
+ *   x         fp16 NDHWC contiguous [B, D, H, W, C] (already padded), C % 64 == 0
+ *   x_dims    {B, D, H, W, C}
+ *   w         fp16 [O, kd*kh*kw*C] tap-major, channel-minor
+ *   strides   1 or 2 per axis (a stride-2 conv reads every other pixel through
+ *             TMA element strides)
+ *   bias      fp16 [O] or NULL: out = fp16(acc + bias) with an fp32 accumulator
+ *   out       fp16 [B, Do, Ho, Wo, O] at out_strides {sB, sD, sH, sW} (elements)
+ *   residual  optional fp16 tensor with out's strides: out = fp16(fp16(conv) + residual)
+ *   causal_zero_frames: 2 when input frames 0 and 1 are the causal zero pad;
+ *             taps that only read them are skipped
+ * Replaces the cuDNN F.conv3d calls of the fp16 encoder/decoder path,
+ * ref: opt/encoder_fused_residual_pack.py:85 (stride-2 downsample after the
+ *      residual pack), opt/encoder_fused_batched_norm.py:83,94,96 (suffix
+ *      convs), opt/encoder_internal_padding.py:34 (padded causal conv) */
+int h3b_conv3d_f16(const void* x, const int64_t* x_dims, const void* w, int64_t out_channels,
+                   int kd, int kh, int kw, int sd, int sh, int sw, const void* bias, void* out,
+                   const int64_t* out_strides, const void* residual, int causal_zero_frames,
+                   h3b_stream_t stream);
+
 /* ---- (a2) per-tensor activation quantization ---------------------------- */
 
 /* scale = max|x| * fp32(1/127) (0 -> 1);  q = clamp(half_away(x / scale), +-127)

@@ -1,0 +1,89 @@
+"""fp16 implicit-GEMM conv3d (tcgen05 kind::f16, fp32 accumulate) on the B200 vs a plain PyTorch
+fp32 reference of the same op (CPU F.conv3d on the fp16 inputs, rounded to fp16).  Tolerance:
+max-abs 1e-2 / rel 1e-3 on the fp16 outputs.  Covers the convolutions of the fp16 encoder/decoder
+path: stride-2 downsample convs after the residual pack, 1x1x1 shortcuts, narrow conv_out (O=32),
+the decoder's upsampling convs, fused bias and residual, the causal-zero tap skip."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def _ref(x, w, b, stride, residual=None):
+    y = F.conv3d(x.float(), w.float(), None if b is None else b.float(), stride=stride)
+    if residual is not None:
+        y = y.half().float() + residual.float()
+    return y.half().float()
+
+
+def _close(got, ref, atol=1e-2, rtol=1e-3):
+    diff = (got.float() - ref).abs()
+    bad = diff > atol + rtol * ref.abs()
+    assert not bool(bad.any()), (float(diff.max()), int(bad.sum()))
+
+
+CASES = [
+    # (shape [B,C,D,H,W] of the padded input, O, kernel, stride)
+    ((1, 128, 5, 19, 23), 128, (3, 3, 3), (1, 1, 1)),
+    ((2, 64, 4, 10, 18), 128, (3, 3, 3), (1, 1, 1)),
+    ((1, 128, 19, 65, 65), 128, (3, 3, 3), (1, 2, 2)),       # stage-0 downsample after the residual pack
+    ((1, 256, 11, 33, 33), 256, (3, 3, 3), (2, 2, 2)),       # stage-1 downsample
+    ((1, 512, 7, 17, 17), 512, (3, 3, 3), (2, 2, 2)),        # stage-2 downsample
+    ((2, 128, 9, 16, 16), 256, (1, 1, 1), (1, 1, 1)),        # 1x1x1 shortcut
+    ((1, 512, 7, 10, 12), 32, (3, 3, 3), (1, 1, 1)),         # encoder conv_out (BN=64 tile)
+    ((1, 1024, 7, 10, 10), 512, (3, 3, 3), (1, 1, 1)),       # decoder upsampling conv
+    ((1, 256, 5, 131, 130), 128, (3, 3, 3), (1, 1, 1)),      # two M tiles per CTA, odd tile count
+    ((1, 128, 5, 9, 200), 192, (3, 3, 3), (1, 1, 1)),        # O not a multiple of the tile, W > 128
+]
+
+
+@pytest.mark.parametrize("shape,o,kernel,stride", CASES)
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_conv3d_f16_matches_fp32_reference(cuda_lib, shape, o, kernel, stride, with_bias):
+    from h3vae_b200 import kernels as K
+    g = torch.Generator().manual_seed(sum(shape) * 7 + o)
+    c = shape[1]
+    x = torch.randn(shape, generator=g).half()
+    w = (torch.randn((o, c, *kernel), generator=g) / (c * kernel[0] * kernel[1] * kernel[2]) ** 0.5).half()
+    b = (torch.randn(o, generator=g) * 0.1).half() if with_bias else None
+    y = K.conv3d_f16(x.cuda().contiguous(memory_format=torch.channels_last_3d), K.pack_conv_weight_f16(w).cuda(),
+                     None if b is None else b.cuda(), kernel, stride)
+    assert y.is_contiguous(memory_format=torch.channels_last_3d)
+    _close(y.cpu(), _ref(x, w, b, stride))
+
+
+def test_conv3d_f16_residual_and_causal_skip(cuda_lib):
+    from h3vae_b200 import kernels as K
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn((2, 128, 7, 12, 20), generator=g).half()
+    x[:, :, :2] = 0                                   # the causal zero pad
+    w = (torch.randn((128, 128, 3, 3, 3), generator=g) / 3456 ** 0.5).half()
+    b = (torch.randn(128, generator=g) * 0.1).half()
+    ref = _ref(x, w, b, (1, 1, 1))
+    r = torch.randn(ref.shape, generator=g).half()
+    xc = x.cuda().contiguous(memory_format=torch.channels_last_3d)
+    wp = K.pack_conv_weight_f16(w).cuda()
+    rc = r.cuda().contiguous(memory_format=torch.channels_last_3d)
+    full = K.conv3d_f16(xc, wp, b.cuda(), (3, 3, 3), residual=rc)
+    skip = K.conv3d_f16(xc, wp, b.cuda(), (3, 3, 3), causal_zero_frames=2, residual=rc)
+    assert torch.equal(full, skip)
+    _close(full.cpu(), _ref(x, w, b, (1, 1, 1), residual=r))
+    # stride-2 temporal with the causal skip: od*2 + kd < 2 only for od = 0
+    x2 = torch.randn((1, 256, 9, 17, 17), generator=g).half()
+    x2[:, :, :2] = 0
+    w2 = (torch.randn((256, 256, 3, 3, 3), generator=g) / 6912 ** 0.5).half()
+    x2c = x2.cuda().contiguous(memory_format=torch.channels_last_3d)
+    a = K.conv3d_f16(x2c, K.pack_conv_weight_f16(w2).cuda(), None, (3, 3, 3), (2, 2, 2))
+    s = K.conv3d_f16(x2c, K.pack_conv_weight_f16(w2).cuda(), None, (3, 3, 3), (2, 2, 2), causal_zero_frames=2)
+    assert torch.equal(a, s)
+    _close(a.cpu(), _ref(x2, w2, None, (2, 2, 2)))
+
+
+def test_conv3d_f16_rejects_unsupported(cuda_lib):
+    from h3vae_b200 import kernels as K
+    x = torch.zeros((1, 48, 3, 8, 8), dtype=torch.float16, device="cuda").contiguous(
+        memory_format=torch.channels_last_3d)
+    w = torch.zeros((16, 27 * 48), dtype=torch.float16, device="cuda")
+    with pytest.raises(ValueError, match="multiple of 64"):
+        K.conv3d_f16(x, w, None, (3, 3, 3))

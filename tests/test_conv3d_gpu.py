@@ -51,6 +51,9 @@ CASES = [
     (128, 64, (1, 128, 5, 34, 130), (3, 3, 3), (1, 1, 1)),
     (7, 19, (2, 7, 5, 9, 11), (3, 3, 3), (1, 2, 2)),
     (128, 128, (1, 128, 5, 17, 33), (3, 3, 3), (1, 2, 2)),
+    (256, 256, (1, 256, 11, 33, 35), (3, 3, 3), (2, 2, 2)),
+    # two M tiles per CTA (O <= 128 with enough tiles to fill the SMs), an odd tile count
+    (128, 128, (1, 128, 5, 131, 130), (3, 3, 3), (1, 1, 1)),
 ]
 
 
@@ -74,6 +77,8 @@ def test_conv_matches_oracle(cuda_lib, ci, co, shape, kernel, stride, with_bias)
     (7, 19, (1, 7, 5, 10, 18), (3, 3, 3), (1, 1, 1)),
     (128, 128, (1, 128, 5, 17, 33), (3, 3, 3), (1, 2, 2)),
     (128, 128, (1, 128, 3, 10, 18), (1, 3, 3), (1, 1, 1)),
+    (128, 128, (1, 128, 5, 130, 130), (3, 3, 3), (1, 1, 1)),
+    (256, 256, (1, 256, 11, 17, 17), (3, 3, 3), (2, 2, 2)),
 ])
 def test_causal_zero_skip_is_exact(cuda_lib, ci, co, shape, kernel, stride):
     # ref: tests/test_encoder_int8_gpu.py:119-151 -- a known-zero prefix skipped or not gives equal results
