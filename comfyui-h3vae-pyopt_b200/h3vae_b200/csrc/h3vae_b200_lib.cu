@@ -5,3 +5,4 @@
 #include "encoder_producers.cu"
 #include "decoder_producers.cu"
 #include "attention_tc.cu"
+#include "conv_in.cu"

@@ -177,6 +177,36 @@ def conv3d_f16(x: torch.Tensor, wpacked: torch.Tensor, bias: torch.Tensor | None
     return out
 
 
+def conv_in_f16(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                norm: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+    """Encoder input conv: optional pixel normalization fp16(((x+1)*0.5 - mean)/std), causal +
+    reflect pad and the 3x3x3 conv (+bias) to 128 channels, fp32 accumulate on the tensor cores.
+    x fp16 [B, Cin<=4, T, H, W] (any strides); weight fp16 [128, Cin, 3, 3, 3] -> NDHWC fp16."""
+    dev = _require_cuda(x, weight, bias, *(norm or ()))
+    if x.ndim != 5 or x.dtype != F16:
+        raise ValueError("x must be fp16 [B,C,T,H,W]")
+    b, cin, t, h, w = x.shape
+    if weight.shape != (weight.shape[0], cin, 3, 3, 3) or weight.dtype != F16:
+        raise ValueError("weight must be fp16 [O, Cin, 3, 3, 3]")
+    o = weight.shape[0]
+    _require(bias, F16, "bias")
+    wp = weight.detach().permute(0, 2, 3, 4, 1).reshape(o, -1).contiguous()
+    mean = std = None
+    if norm is not None:
+        mean, std = (v.reshape(-1).to(F32).contiguous() for v in norm)
+        if mean.numel() != cin or std.numel() != cin:
+            raise ValueError("normalization vectors must have one value per input channel")
+    lib = _lib.load()
+    ws_bytes = lib.h3b_conv_in_workspace_size(b, t, h, w)
+    ws = torch.empty(ws_bytes, device=dev, dtype=torch.uint8)
+    out = torch.empty((b, o, t, h, w), device=dev, dtype=F16, memory_format=torch.channels_last_3d)
+    _lib.check(lib.h3b_conv_in_f16(x.data_ptr(), _lib.i64_array(x.shape), _lib.i64_array(x.stride()), _ptr(mean),
+                                   _ptr(std), wp.data_ptr(), o, _ptr(bias), out.data_ptr(), ws.data_ptr(), ws_bytes,
+                                   _stream(dev)))
+    _count(2)
+    return out
+
+
 def quantize_tensor_i8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-tensor half-away INT8 quantization of fp16 [B,C,D,H,W] (any strides) to NDHWC int8."""
     dev = _require_cuda(x)

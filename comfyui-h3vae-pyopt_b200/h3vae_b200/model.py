@@ -223,12 +223,19 @@ class H3Encoder:
         return sum(2 for blocks in self.stages for b in blocks if b.int8)
 
     @torch.no_grad()
-    def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        """x: fp16 [B,3,T,H,W] ImageNet-normalized pixels of one causal clip -> moments
-        [B, 2*latent, T', H/ratio, W/ratio] (fp16)."""
+    def __call__(self, x: torch.Tensor, norm: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+        """x: fp16 [B,3,T,H,W] pixels of one causal clip -> moments [B, 2*latent, T', H/ratio, W/ratio]
+        (fp16).  With norm=(mean, std), x is in [-1, 1] and the input conv applies the ImageNet
+        normalization fp16(((x + 1) / 2 - mean) / std) itself; otherwise x is already normalized."""
         if x.device.type != "cuda":
             raise RuntimeError("H3Encoder requires CUDA input (no CPU fallback)")
-        h = conv_f16(causal_reflect_pad(x.half()), self.conv_in_w, self.conv_in_b)
+        if self.conv_in_w.shape[0] == 128 and x.shape[1] <= 4:
+            h = K.conv_in_f16(x.half(), self.conv_in_w, self.conv_in_b, norm)
+        else:
+            if norm is not None:
+                mean, std = (v.float().view(1, -1, 1, 1, 1) for v in norm)
+                x = (((x.float() + 1.0) * 0.5 - mean) / std).half()
+            h = conv_f16(causal_reflect_pad(x.half()), self.conv_in_w, self.conv_in_b)
         for blocks, down in zip(self.stages, self.down):
             for j, blk in enumerate(blocks):
                 last = j == len(blocks) - 1

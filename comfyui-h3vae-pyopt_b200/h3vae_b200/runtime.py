@@ -333,7 +333,12 @@ class H3VAEPyOptRuntime(torch.nn.Module):
                         rep = clip[:, :, -1:].expand(-1, -1, CLIP_LENGTH - clip.shape[2], -1, -1)
                         clip = torch.cat([clip, rep], dim=2)
                     batch.append(clip)
-            moments = self.encoder(self._normalize_pixels(torch.cat(batch, 0)))
+            clips = torch.cat(batch, 0)
+            if clips.dtype == torch.float16:
+                # normalization fused into the encoder's input conv
+                moments = self.encoder(clips, norm=(self._img_mean, self._img_std))
+            else:
+                moments = self.encoder(self._normalize_pixels(clips))
             mean = moments[:, : self.latent_channels]
             wmap = self._weights(lplan, i, j)
             for n, (bi, c) in enumerate((bi, c) for bi in range(b) for c in cs):

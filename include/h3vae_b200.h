@@ -92,6 +92,23 @@ int h3b_conv3d_f16(const void* x, const int64_t* x_dims, const void* w, int64_t 
                    const int64_t* out_strides, const void* residual, int causal_zero_frames,
                    h3b_stream_t stream);
 
+/* Encoder input conv with the pixel normalization and the causal/reflect pad
+ * fused in: x fp16 logical [B, Cin, T, H, W] (element strides5, Cin <= 4) ->
+ *   n = fp16(((x + 1) * 0.5 - mean[c]) / std[c])   (fp32; skipped when both
+ *       normalization pointers are NULL)
+ *   padded: reflect 1 in H/W (zero when H or W is 1), 2 zero frames in front
+ *   out = fp16(conv3x3x3(padded, w) + bias), fp32 accumulate, NDHWC [B,T,H,W,O]
+ * w: fp16 [O, 27*Cin] tap-major, channel-minor; O = 128.
+ * workspace >= h3b_conv_in_workspace_size(B, T, H, W) bytes (8-byte aligned;
+ * it holds the padded normalized pixels).
+ * ref: h3vae_runtime.py:566-570 (_normalize_pixels) and the encoder's first
+ *      causal conv, opt/encoder_staged_batch.py:16-17 (EncoderPrefix.conv_in),
+ *      opt/encoder_internal_padding.py:27-36 (causal padding of the conv) */
+size_t h3b_conv_in_workspace_size(int64_t B, int64_t T, int64_t H, int64_t W);
+int h3b_conv_in_f16(const void* x, const int64_t* dims5, const int64_t* strides5, const float* norm_mean,
+                    const float* norm_std, const void* w, int64_t out_channels, const void* bias,
+                    void* out, void* workspace, size_t workspace_bytes, h3b_stream_t stream);
+
 /* ---- (a2) per-tensor activation quantization ---------------------------- */
 
 /* scale = max|x| * fp32(1/127) (0 -> 1);  q = clamp(half_away(x / scale), +-127)

@@ -87,3 +87,26 @@ def test_conv3d_f16_rejects_unsupported(cuda_lib):
     w = torch.zeros((16, 27 * 48), dtype=torch.float16, device="cuda")
     with pytest.raises(ValueError, match="multiple of 64"):
         K.conv3d_f16(x, w, None, (3, 3, 3))
+
+
+@pytest.mark.parametrize("shape", [(2, 3, 5, 20, 140), (1, 3, 17, 33, 17), (1, 3, 3, 1, 5), (1, 1, 2, 6, 9)])
+@pytest.mark.parametrize("normalize", [False, True])
+def test_conv_in_matches_fp32_reference(cuda_lib, shape, normalize):
+    """Fused pixel normalization + causal/reflect pad + 3x3x3 input conv (ref: h3vae_runtime.py:566-570
+    and the encoder's first causal conv) vs the same steps in PyTorch fp32 on the CPU."""
+    from h3vae_b200 import kernels as K
+    from h3vae_b200.model import causal_reflect_pad
+    g = torch.Generator().manual_seed(sum(shape))
+    cin = shape[1]
+    x = (torch.rand(shape, generator=g) * 2 - 1).half()
+    w = (torch.randn((128, cin, 3, 3, 3), generator=g) / (27 * cin) ** 0.5).half()
+    b = (torch.randn(128, generator=g) * 0.1).half()
+    mean = torch.rand(cin, generator=g) * 0.5
+    std = 0.2 + torch.rand(cin, generator=g) * 0.1
+    n = x
+    if normalize:
+        n = (((x.float() + 1.0) * 0.5 - mean.view(1, -1, 1, 1, 1)) / std.view(1, -1, 1, 1, 1)).half()
+    ref = F.conv3d(causal_reflect_pad(n.float()), w.float(), b.float()).half().float()
+    y = K.conv_in_f16(x.cuda(), w.cuda(), b.cuda(), (mean.cuda(), std.cuda()) if normalize else None)
+    assert y.is_contiguous(memory_format=torch.channels_last_3d)
+    _close(y.cpu(), ref)

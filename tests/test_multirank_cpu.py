@@ -34,7 +34,10 @@ class _FakeEncoder:
         self.int8_conv_count = 0
         self.mix = torch.randn(32, 3, generator=torch.Generator().manual_seed(3)).double()
 
-    def __call__(self, x):
+    def __call__(self, x, norm=None):
+        if norm is not None:
+            mean, std = (v.float().view(1, -1, 1, 1, 1) for v in norm)
+            x = (((x.float() + 1.0) * 0.5 - mean) / std).half()
         p = torch.nn.functional.avg_pool3d(x.double()[:, :, ::4], (1, 8, 8))
         return torch.einsum("oc,ncthw->nothw", self.mix, p).half()
 
