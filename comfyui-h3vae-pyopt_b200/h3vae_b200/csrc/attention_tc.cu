@@ -1,30 +1,77 @@
 // Non-causal fp16 attention (head dim 64) on the tcgen05 tensor cores.
 //
-// One CTA = one (batch, head, 128-query tile); 6 warps:
-//   warp 0      TMA: Q once, then K and V tiles of 128 keys through a 3-stage ring
-//   warp 1      TMEM owner + MMA issuer:  S_j = Q K_j^T  (M128 N128 K64, fp32 in
-//               TMEM, double buffered), then O_j = P_j V_j (M128 N64 K128, P from
-//               shared memory, V as the MN-major B operand straight from its TMA tile)
-//   warps 2..5  softmax, one query row per thread (TMEM lane): running max, P_j =
-//               exp2(S_j * scale*log2e - m_j) rounded to fp16 into 128-byte-swizzled
-//               shared memory, running sum, and the O accumulator in registers:
-//               o = o * exp2(m_{j-1} - m_j) + O_j.
-// While the softmax warps work on S_j the tensor cores compute S_{j+1} and
-// O_{j-1}.  Every wait is bounded (see common.cuh).
+// One CTA = one (batch, head) and two 128-query tiles; 10 warps:
+//   warp 0      TMA: both Q tiles once, then K and V tiles of 128 keys through
+//               a 3-stage ring
+//   warp 1      TMEM owner + MMA issuer.  Per key block j and query tile t:
+//               S_j(t) = Q_t K_j^T (M128 N128 K64, fp32 in TMEM), then, once the
+//               softmax of tile t has written P_j(t) to shared memory,
+//               O(t) += P_j(t) V_j (M128 N64 K128, V as the MN-major B operand
+//               straight from its TMA tile).  S_{j+1}(t) is issued as soon as
+//               the softmax has copied S_j(t) out of TMEM.
+//   warps 2..9  softmax, four warps per query tile, one query row per thread
+//               (its TMEM lane).  The row's 128 scores come out of TMEM in one
+//               round trip, after which the S columns are released so the MMA
+//               warp computes S_{j+1} while this block is exponentiated.
+//               P_j = exp2(S_j * scale*log2e - m) is rounded to
+//               fp16 into 128-byte-swizzled shared memory and the running row
+//               sum stays in a register.  O accumulates in TMEM across key
+//               blocks.  The reference max m only moves when a block's max
+//               exceeds it by more than 8 (log2 units; P stays <= 256, well
+//               inside fp16); then the rows' O in TMEM is rescaled by
+//               exp2(m_old - m_new) before the next P V accumulates.  One
+//               division by the row sum at the end.
+// The base-2 exponentials (16K per tile and key block, one SFU op each) are
+// the bound; the two tiles take turns on the SFU (named-barrier ping-pong) so
+// one tile's exponentials overlap the other's TMEM reads and waits.  Every mbarrier wait is bounded (see common.cuh); its outcome is
+// made warp-uniform before any warp-collective TMEM access.
 #include "common.cuh"
 
 namespace h3b {
 
-constexpr int kFaM = 128;       // queries per CTA
-constexpr int kFaN = 128;       // keys per tile
+// Packed fp32 pairs (Blackwell f32x2 arithmetic) and the single-instruction
+// base-2 exponential of the softmax.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+constexpr int kFaM = 128;       // queries per tile
+constexpr int kFaTiles = 2;     // query tiles per CTA
+constexpr int kFaN = 128;       // keys per block
 constexpr int kFaD = 64;        // head dim
 constexpr int kFaStages = 3;
-constexpr int kFaThreads = 192;
-constexpr uint32_t kFaQBytes = kFaM * kFaD * 2;   // 16 KB
+constexpr int kFaSoftmaxWarps = 4;   // per query tile: one row per thread
+constexpr int kFaThreads = 64 + 32 * kFaSoftmaxWarps * kFaTiles;
+constexpr uint32_t kFaQBytes = kFaM * kFaD * 2;   // 16 KB per tile
 constexpr uint32_t kFaKVBytes = kFaN * kFaD * 2;  // 16 KB each for K and V
-constexpr uint32_t kFaPBytes = kFaM * kFaN * 2;   // 32 KB (two 16 KB swizzle columns of 64 keys)
-constexpr uint32_t kFaTmemCols = 512;             // S0 | S1 | O0 | O1
-constexpr uint32_t kFaS0 = 0, kFaO0 = 256;
+constexpr uint32_t kFaPBytes = kFaM * kFaN * 2;   // 32 KB per tile (two 16 KB swizzle columns of 64 keys)
+constexpr uint32_t kFaTmemCols = 512;             // per tile: S (128) | O (64), at tile * 256
+constexpr uint32_t kFaSmemBytes = kFaTiles * kFaQBytes + 2 * kFaStages * kFaKVBytes + kFaTiles * kFaPBytes + 1024 + 256;
 
 struct FaParams {
   int q_len, kv_len;
@@ -38,26 +85,25 @@ __global__ void __launch_bounds__(kFaThreads, 1)
                         const __grid_constant__ CUtensorMap mv, const FaParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sq = smem;
-  uint8_t* sk = sq + kFaQBytes;
-  uint8_t* sv = sk + kFaStages * kFaKVBytes;
-  uint8_t* sp = sv + kFaStages * kFaKVBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + 2 * kFaPBytes);
+  uint8_t* sq = smem;                                  // [tile]
+  uint8_t* sk = sq + kFaTiles * kFaQBytes;             // [stage]
+  uint8_t* sv = sk + kFaStages * kFaKVBytes;           // [stage]
+  uint8_t* sp = sv + kFaStages * kFaKVBytes;           // [tile]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + kFaTiles * kFaPBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + kFaStages;
-  uint64_t* s_full = kv_empty + kFaStages;
-  uint64_t* s_empty = s_full + 2;
-  uint64_t* p_full = s_empty + 2;
-  uint64_t* o_full = p_full + 2;
-  uint64_t* o_empty = o_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_empty + 2);
+  uint64_t* s_full = kv_empty + kFaStages;    // [tile]
+  uint64_t* s_empty = s_full + kFaTiles;      // [tile]
+  uint64_t* p_full = s_empty + kFaTiles;      // [tile]
+  uint64_t* o_full = p_full + kFaTiles;       // [tile]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_full + kFaTiles);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int qt = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int n_tiles = (p.kv_len + kFaN - 1) / kFaN;
+  const int qt0 = blockIdx.x * kFaTiles, h = blockIdx.y, b = blockIdx.z;
+  const int n_blocks = (p.kv_len + kFaN - 1) / kFaN;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -65,12 +111,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
-      mbar_init(&p_full[i], 128);
-      mbar_init(&o_full[i], 1);
-      mbar_init(&o_empty[i], 128);
+    for (int t = 0; t < kFaTiles; ++t) {
+      mbar_init(&s_full[t], 1);
+      mbar_init(&s_empty[t], 32 * kFaSoftmaxWarps);
+      mbar_init(&p_full[t], 32 * kFaSoftmaxWarps);
+      mbar_init(&o_full[t], 1);
     }
     *abort_flag = 0;
     fence_barrier_init();
@@ -90,11 +135,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------------------------- TMA ----------------------------------
     if (elect_one_sync()) {
-      mbar_arrive_expect_tx(q_full, kFaQBytes);
-      tma_load_4d(sq, &mq, q_full, 0, qt * kFaM, h, b);
+      mbar_arrive_expect_tx(q_full, kFaTiles * kFaQBytes);
+      for (int t = 0; t < kFaTiles; ++t) tma_load_4d(sq + t * kFaQBytes, &mq, q_full, 0, (qt0 + t) * kFaM, h, b);
       uint32_t issued = 0;
-      for (int j = 0; j < n_tiles; ++j, ++issued) {
+      for (int j = 0; j < n_blocks; ++j, ++issued) {
         const int s = j % kFaStages;
         if (!mbar_wait(&kv_empty[s], ((j / kFaStages) & 1) ^ 1, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[s], 2 * kFaKVBytes);
@@ -109,130 +155,187 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       }
     }
   } else if (warp == 1) {
+    // ------------------------------- MMA issuer -------------------------------
     if (elect_one_sync()) {
       constexpr uint32_t idesc_qk = make_idesc_f16(kFaM, kFaN);
       constexpr uint32_t idesc_pv = make_idesc_f16(kFaM, kFaD) | (1u << 16);  // B (V) is MN-major
       bool ok = mbar_wait(q_full, 0, abort_flag);
-      const uint64_t qdesc = make_sw128_desc(smem_u32(sq));
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % kFaStages, sb = j & 1;
+      // S_j(t) into tile t's S columns; requires K_j resident and S_{j-1}(t) read out.
+      auto issue_s = [&](int j, int t) -> bool {
+        const int s = j % kFaStages;
         if (!mbar_wait(&kv_full[s], (j / kFaStages) & 1, abort_flag)) return false;
-        if (!mbar_wait(&s_empty[sb], ((j >> 1) & 1) ^ 1, abort_flag)) return false;
+        if (!mbar_wait(&s_empty[t], (j & 1) ^ 1, abort_flag)) return false;
         tc_fence_after();
+        const uint64_t qdesc = make_sw128_desc(smem_u32(sq + t * kFaQBytes));
         const uint64_t kdesc = make_sw128_desc(smem_u32(sk + s * kFaKVBytes));
 #pragma unroll
         for (int k = 0; k < kFaD / 16; ++k)  // 16 fp16 = 32 bytes per MMA step
-          mma_f16(tmem + kFaS0 + sb * kFaN, qdesc + 2 * k, kdesc + 2 * k, idesc_qk, k > 0 ? 1u : 0u);
-        tc_commit(&s_full[sb]);
+          mma_f16(tmem + t * 256, qdesc + 2 * k, kdesc + 2 * k, idesc_qk, k > 0 ? 1u : 0u);
+        tc_commit(&s_full[t]);
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; j < n_tiles && ok; ++j) {
-        if (j + 1 < n_tiles && !issue_s(j + 1)) break;
-        const int s = j % kFaStages, ob = j & 1;
-        if (!mbar_wait(&p_full[ob], (j >> 1) & 1, abort_flag)) break;
-        if (!mbar_wait(&o_empty[ob], ((j >> 1) & 1) ^ 1, abort_flag)) break;
-        tc_fence_after();
-        const uint32_t pbase = smem_u32(sp + ob * kFaPBytes);
-        const uint32_t vbase = smem_u32(sv + s * kFaKVBytes);
+      for (int t = 0; t < kFaTiles && ok; ++t) ok = issue_s(0, t);
+      for (int j = 0; j < n_blocks && ok; ++j) {
+        const int s = j % kFaStages;
+        // S_{j+1}(t) as soon as the softmax of tile t has copied S_j(t) into its
+        // registers, so it overlaps that softmax's exponentials.
+        for (int t = 0; t < kFaTiles && ok && j + 1 < n_blocks; ++t) ok = issue_s(j + 1, t);
+        for (int t = 0; t < kFaTiles && ok; ++t) {
+          // P_j(t) written; O(t) holds the sum over the blocks before j,
+          // already rescaled if the reference max moved.
+          if (!mbar_wait(&p_full[t], j & 1, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t pbase = smem_u32(sp + t * kFaPBytes);
+          const uint32_t vbase = smem_u32(sv + s * kFaKVBytes);
 #pragma unroll
-        for (int t = 0; t < kFaN / 16; ++t) {
-          const uint64_t pdesc = make_sw128_desc(pbase + (t >> 2) * (kFaPBytes / 2)) + 2 * (t & 3);
-          const uint64_t vdesc = make_sw128_desc(vbase + t * 16 * 128);
-          mma_f16(tmem + kFaO0 + ob * kFaD, pdesc, vdesc, idesc_pv, t > 0 ? 1u : 0u);
+          for (int k = 0; k < kFaN / 16; ++k) {
+            const uint64_t pdesc = make_sw128_desc(pbase + (k >> 2) * (kFaPBytes / 2)) + 2 * (k & 3);
+            const uint64_t vdesc = make_sw128_desc(vbase + k * 16 * 128);
+            mma_f16(tmem + t * 256 + kFaN, pdesc, vdesc, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&o_full[t]);
         }
-        tc_commit(&o_full[ob]);
         tc_commit(&kv_empty[s]);
       }
     }
   } else {
     // ------------------------------ softmax warps ------------------------------
+    const int sw = warp - 2;
+    const int tile = sw / kFaSoftmaxWarps;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
-    const uint32_t lane_off = static_cast<uint32_t>(quad * 32) << 16;
-    float m = -INFINITY, l = 0.0f, alpha_prev = 0.0f;
-    float o[kFaD];
-#pragma unroll
-    for (int d = 0; d < kFaD; ++d) o[d] = 0.0f;
+    const uint32_t t_lane = tmem + tile * 256 + (static_cast<uint32_t>(quad * 32) << 16);
+    const uint32_t t_s = t_lane;
+    const uint32_t t_o = t_lane + kFaN;
+    float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    auto take_o = [&](int jj) -> bool {
-      const int ob = jj & 1;
-      if (!mbar_wait(&o_full[ob], (jj >> 1) & 1, abort_flag)) return false;
-      tc_fence_after();
-      uint32_t r0[32], r1[32];
-      tmem_ld32(tmem + lane_off + kFaO0 + ob * kFaD, r0);
-      tmem_ld32(tmem + lane_off + kFaO0 + ob * kFaD + 32, r1);
-      tmem_ld_wait();
-      tc_fence_before();
-      mbar_arrive(&o_empty[ob]);
-#pragma unroll
-      for (int d = 0; d < 32; ++d) {
-        o[d] = __fmaf_rn(o[d], alpha_prev, __uint_as_float(r0[d]));
-        o[32 + d] = __fmaf_rn(o[32 + d], alpha_prev, __uint_as_float(r1[d]));
-      }
-      return true;
+    uint8_t* prow = sp + tile * kFaPBytes + row * 128;
+    // Named barriers 1 and 2 (both tiles' 256 softmax threads) pass the SFU turn:
+    // tile 0 syncs on 1 and arrives on 2, tile 1 the reverse.  Tile 1 hands
+    // tile 0 the first turn and skips its hand-back after the last block, so
+    // every barrier completes as often as it is waited on.
+    constexpr int kSoftmaxThreads = 32 * kFaSoftmaxWarps * kFaTiles;
+    auto exp_turn_begin = [&]() {
+      asm volatile("bar.sync %0, %1;" ::"r"(tile == 0 ? 1 : 2), "r"(kSoftmaxThreads) : "memory");
     };
-    for (int j = 0; j < n_tiles && ok; ++j) {
-      const int sb = j & 1;
-      if (!mbar_wait(&s_full[sb], (j >> 1) & 1, abort_flag)) { ok = false; break; }
-      tc_fence_after();
-      float sv_[kFaN];
-#pragma unroll
-      for (int c = 0; c < kFaN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_off + kFaS0 + sb * kFaN + c * 32, r);
-        tmem_ld_wait();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) sv_[c * 32 + i] = __uint_as_float(r[i]);
-      }
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
+    auto exp_turn_end = [&](int jj) {
+      if (tile == 0 || jj + 1 < n_blocks)
+        asm volatile("bar.arrive %0, %1;" ::"r"(tile == 0 ? 2 : 1), "r"(kSoftmaxThreads) : "memory");
+    };
+    if (tile == 1) asm volatile("bar.arrive 1, %0;" ::"r"(kSoftmaxThreads) : "memory");
+    const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
+    for (int j = 0; j < n_blocks; ++j) {
+      ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[tile], j & 1, abort_flag));
       const int valid = p.kv_len - j * kFaN;
-      float tmax = -INFINITY;
+      // All 128 scores of the row into registers with one TMEM round trip; the
+      // S columns are released at once so S_{j+1} can be computed meanwhile.
+      uint32_t sv_[128];
+      if (ok) {
+        tc_fence_after();
 #pragma unroll
-      for (int i = 0; i < kFaN; ++i) {
-        if (i >= valid) sv_[i] = -INFINITY;
-        tmax = fmaxf(tmax, sv_[i]);
+        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv_[c * 32]));
+        tmem_ld_wait();
+        tc_fence_before();
+        mbar_arrive(&s_empty[tile]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 128; ++k) sv_[k] = 0xff800000u;   // -inf
       }
-      const float m_new = fmaxf(m, tmax * p.scale_log2);
-      const float alpha = exp2f(m - m_new);
-      float rowsum = 0.0f;
-      uint8_t* prow = sp + sb * kFaPBytes + row * 128;
+      if (valid < kFaN) {
 #pragma unroll
-      for (int blk = 0; blk < 2; ++blk) {
-#pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          __align__(16) __half2 hv[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const int k = blk * 64 + c * 8 + 2 * e;
-            const float p0 = exp2f(__fmaf_rn(sv_[k], p.scale_log2, -m_new));
-            const float p1 = exp2f(__fmaf_rn(sv_[k + 1], p.scale_log2, -m_new));
-            rowsum += p0 + p1;
-            hv[e] = __floats2half2_rn(p0, p1);
-          }
-          *reinterpret_cast<uint4*>(prow + blk * (kFaPBytes / 2) + ((c ^ (row & 7)) << 4)) =
-              *reinterpret_cast<const uint4*>(hv);
-        }
+        for (int k = 0; k < 128; ++k)
+          if (k >= valid) sv_[k] = 0xff800000u;
       }
-      fence_proxy_async_smem();
-      mbar_arrive(&p_full[sb]);
-      l = __fmaf_rn(l, alpha, rowsum);
-      if (j > 0 && !take_o(j - 1)) { ok = false; break; }
-      alpha_prev = alpha;
-      m = m_new;
-    }
-    if (ok && n_tiles > 0) ok = take_o(n_tiles - 1);
-    const int qrow = qt * kFaM + row;
-    if (ok && qrow < p.q_len) {
-      const float inv = l > 0.0f ? 1.0f / l : 0.0f;
-      __half* dst = p.out + b * p.os[0] + h * p.os[1] + static_cast<int64_t>(qrow) * p.os[2];
+      // row maximum: four independent chains of 3-input max
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-      for (int q = 0; q < kFaD / 8; ++q) {
+      for (int k = 0; k < 128; k += 2)
+        mx[(k >> 1) & 3] = fmax3(mx[(k >> 1) & 3], __uint_as_float(sv_[k]), __uint_as_float(sv_[k + 1]));
+      const float tmax = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+      // Lazy reference max: it moves only when a score exceeds it by more than 8
+      // (log2 units).  Every block has a valid key, so m is finite from the
+      // first block on; exp2(-inf - m) = 0 there.
+      const float m_blk = tmax * p.scale_log2;
+      const bool move = m_blk > m + 8.0f;
+      const float m_new = move ? m_blk : m;
+      const float alpha = move ? ex2_approx(m - m_new) : 1.0f;
+      // P V of block j-1 has finished: the P buffer is free and O(t) is stable.
+      if (j > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[tile], (j - 1) & 1, abort_flag));
+      // The two tiles take turns on the SFU: tile 0 exponentiates block j after
+      // tile 1 finished block j-1, tile 1 after tile 0 finished block j, so one
+      // tile's exponentials overlap the other's TMEM reads, maximum and waits.
+      exp_turn_begin();
+      // P_j = exp2(S * scale - m) over the 128 keys
+      const uint64_t negm2 = f2_pack(-m_new, -m_new);
+      uint64_t sum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
         __align__(16) __half2 hv[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) hv[e] = __floats2half2_rn(o[q * 8 + 2 * e] * inv, o[q * 8 + 2 * e + 1] * inv);
-        *reinterpret_cast<uint4*>(dst + q * 8) = *reinterpret_cast<const uint4*>(hv);
+        for (int e = 0; e < 4; ++e) {
+          const int k = q * 8 + 2 * e;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(sv_[k]), __uint_as_float(sv_[k + 1])), scale2, negm2), x0, x1);
+          const float p0 = ex2_approx(x0);
+          const float p1 = ex2_approx(x1);
+          sum2[e & 1] = f2_add(sum2[e & 1], f2_pack(p0, p1));
+          hv[e] = __floats2half2_rn(p0, p1);
+        }
+        // keys q*8..q*8+7: swizzle column q/8, 16-byte chunk q%8 of this row
+        if (ok)
+          *reinterpret_cast<uint4*>(prow + (q >> 3) * (kFaPBytes / 2) + (((q & 7) ^ (row & 7)) << 4)) =
+              *reinterpret_cast<const uint4*>(hv);
+      }
+      exp_turn_end(j);
+      // O(t) rescale when the reference max moved (before P V of block j reads
+      // it).  tcgen05.ld / st are warp-collective, so the whole warp runs it when
+      // any of its rows moved (alpha = 1 for the others).
+      if (ok && j > 0) {
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, move)) {
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld32(t_o + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int d = 0; d < 32; ++d) r[d] = __float_as_uint(__fmul_rn(__uint_as_float(r[d]), alpha));
+            tmem_st32(t_o + c * 32, r);
+          }
+          tmem_st_wait();
+        }
+      }
+      if (ok) {
+        tc_fence_before();
+        fence_proxy_async_smem();
+        mbar_arrive(&p_full[tile]);
+      }
+      float sa, sb_;
+      f2_unpack(f2_add(sum2[0], sum2[1]), sa, sb_);
+      l = __fmaf_rn(l, alpha, sa + sb_);
+      m = m_new;
+    }
+    if (n_blocks > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[tile], (n_blocks - 1) & 1, abort_flag));
+    const int qrow = (qt0 + tile) * kFaM + row;
+    const float inv = l > 0.0f ? 1.0f / l : 0.0f;
+    __half* dst = p.out + b * p.os[0] + h * p.os[1] + static_cast<int64_t>(qrow) * p.os[2];
+    if (ok) tc_fence_after();
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      uint32_t r[32];
+      if (ok) {
+        tmem_ld32(t_o + c * 32, r);
+        tmem_ld_wait();
+      }
+      if (ok && qrow < p.q_len) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          __align__(16) __half2 hv[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            hv[e] = __floats2half2_rn(__uint_as_float(r[q * 8 + 2 * e]) * inv, __uint_as_float(r[q * 8 + 2 * e + 1]) * inv);
+          *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = *reinterpret_cast<const uint4*>(hv);
+        }
       }
     }
   }
@@ -286,11 +389,11 @@ extern "C" int h3b_attention_f16(const void* q, const int64_t* q_strides, const 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.out = static_cast<__half*>(out);
   for (int i = 0; i < 3; ++i) p.os[i] = out_strides[i];
-  constexpr size_t smem = kFaQBytes + 2 * kFaStages * kFaKVBytes + 2 * kFaPBytes + 1024 + 256;
+  constexpr size_t smem = kFaSmemBytes;
   static_assert(smem <= 232448, "shared memory budget");
   cudaError_t e = cudaFuncSetAttribute(attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return h3b_host::set_error(H3B_ECUDA, "%s: smem attribute: %s", name, cudaGetErrorString(e));
-  dim3 grid((unsigned)((q_len + kFaM - 1) / kFaM), (unsigned)heads, (unsigned)batch);
+  dim3 grid((unsigned)((q_len + kFaTiles * kFaM - 1) / (kFaTiles * kFaM)), (unsigned)heads, (unsigned)batch);
   attention_tc_kernel<<<grid, kFaThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(mq, mk, mv, p);
   return h3b_host::check_launch(name);
 }

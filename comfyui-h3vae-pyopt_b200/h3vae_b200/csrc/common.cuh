@@ -223,6 +223,29 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "r"(taddr));
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]),
+      "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]),
+      "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor for a K-major operand tile stored in the
@@ -275,12 +298,28 @@ __device__ __forceinline__ int8_t quant_half_away(float x, float scale) {
 // boundary k + 0.5 are recomputed with the exact division: the result is
 // identical to quant_half_away for every input (NaN and inf included).
 __device__ __forceinline__ int8_t quant_half_away_fast(float x, float scale, float inv_scale) {
+  // s = x / scale through the reciprocal; only within 2^-13 of a .5 tie can
+  // that differ in rounding from the true quotient, so those recompute with
+  // the IEEE division.  Rounding uses the 1.5 * 2^23 magic constant (fp32 adds
+  // on the full-rate pipe) instead of floor / float->int conversions:
+  // a + M rounds a = |s| <= 255 to the nearest integer (ties to even), whose
+  // value sits in the low mantissa bits of a + M; exact ties then step away
+  // from zero.
+  constexpr float kMagic = 12582912.0f;
   float s = __fmul_rn(x, inv_scale);
-  const float a = fabsf(s);
-  if (fabsf(__fsub_rn(__fsub_rn(a, floorf(a)), 0.5f)) < (1.0f / 8192.0f)) s = __fdiv_rn(x, scale);
-  float r = (s >= 0.0f) ? floorf(__fadd_rn(s, 0.5f)) : -floorf(__fadd_rn(-s, 0.5f));
-  r = fminf(fmaxf(r, -127.0f), 127.0f);
-  return static_cast<int8_t>(static_cast<int>(r));
+  float a = fminf(fabsf(s), 255.0f);
+  float t = __fadd_rn(a, kMagic);
+  float d = __fsub_rn(a, __fsub_rn(t, kMagic));   // a - rne(a), in [-0.5, 0.5]
+  if (fabsf(d) > 0.5f - 1.0f / 8192.0f) {
+    s = __fdiv_rn(x, scale);
+    a = fminf(fabsf(s), 255.0f);
+    t = __fadd_rn(a, kMagic);
+    d = __fsub_rn(a, __fsub_rn(t, kMagic));
+  }
+  int k = __float_as_int(t) - __float_as_int(kMagic);
+  k += (d == 0.5f) ? 1 : 0;
+  k = min(k, 127);
+  return static_cast<int8_t>(s < 0.0f ? -k : k);
 }
 
 // Order-preserving map of fp32 to uint32 (for atomicMin/atomicMax of signed

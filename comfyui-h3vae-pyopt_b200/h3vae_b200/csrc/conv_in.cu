@@ -172,7 +172,8 @@ __global__ void __launch_bounds__(kCinThreads, 2)
     const int half = warp >> 2;         // chunks 0..6 / 7..13 while building; columns 0..63 / 64..127 after
     auto epilogue = [&](int tile, uint32_t i) -> bool {
       const uint32_t s = i & 1u;
-      if (!mbar_wait(&t_full[s], (i >> 1) & 1u, abort_flag)) return false;
+      // tcgen05.ld is warp-collective: leave together if any lane's wait gave up
+      if (!__all_sync(0xffffffffu, mbar_wait(&t_full[s], (i >> 1) & 1u, abort_flag))) return false;
       tc_fence_after();
       int t = tile;
       const int wt = t % w_tiles; t /= w_tiles;
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(kCinThreads, 2)
     bool ok = true;
     for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++i) {
       const uint32_t s = i & 1u;
-      if (!mbar_wait(&a_empty[s], ((i >> 1) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+      if (!__all_sync(0xffffffffu, mbar_wait(&a_empty[s], ((i >> 1) & 1u) ^ 1u, abort_flag))) { ok = false; break; }
       int t = tile;
       const int wt = t % w_tiles; t /= w_tiles;
       const int h = t % H; t /= H;

@@ -114,19 +114,23 @@ __device__ __forceinline__ Moments merge_moments(Moments a, Moments b) {
   return Moments{n, __fmaf_rn(d, f, a.mean), a.m2 + b.m2 + d * d * a.n * f};
 }
 
-// Streams one chunk of positions of one (b, frame): every thread keeps, per
-// channel of its vector, a shift (its first sample), the shifted sum and sum
-// of squares, and the running min / max.  The shifted sums become per-thread
-// (n, mean, M2) per group, merged per group in shared memory with Chan's
-// formula; the chunk's (mean, M2) per group goes to `partials`.
+// Streams one chunk of positions of one (b, frame).  GPV = GroupNorm groups
+// per 8-channel vector (8 / (C/32) when C/32 < 8, else 1), a compile-time
+// constant so every accumulator stays in registers.  Per group of its vector a
+// thread keeps a shift (its first sample of the group's first channel), the
+// shifted sum and sum of squares; with MINMAX also the per-channel min / max.
+// The shifted sums become per-thread (n, mean, M2) per group, merged per group
+// in shared memory with Chan's formula; the chunk's (mean, M2) per group goes
+// to `partials`.  The shift is taken before the loop so the loop body is
+// branch-free and its unrolled loads overlap.
+template <int GPV, bool MINMAX>
 __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* __restrict__ x,
                                                                   const __half* __restrict__ pre_bias,
                                                                   NormShape s, float2* __restrict__ partials,
                                                                   unsigned int* __restrict__ cmin,
                                                                   unsigned int* __restrict__ cmax) {
-  __shared__ float red[kStatThreads * kVec];
-  __shared__ float chan[2048];
-  __shared__ Moments slots[kStatThreads][8];
+  constexpr int kPerGroup = kVec / GPV;       // channels of one group inside a vector
+  __shared__ Moments slots[kStatThreads][GPV];
   const int tid = threadIdx.x;
   const int chunk = blockIdx.x;
   const int bt = blockIdx.y;
@@ -143,65 +147,77 @@ __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* 
   if (pre_bias != nullptr) load_h8(pre_bias + c0, pb);
 
   const __half* base = x + (static_cast<int64_t>(bt) * HW + p0) * s.C + c0;
-  float shift[8], s1[8], s2[8], mn[8], mx[8];
-  int n = 0;
+  float shift[GPV], s1[GPV], s2[GPV];
+  float mn[MINMAX ? 8 : 1], mx[MINMAX ? 8 : 1];
+  const int p_first = tid / vpp;
+  const int n = p_first < valid_pos ? (valid_pos - p_first + pos_per_iter - 1) / pos_per_iter : 0;
+  {
+    float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (n > 0) {
+      load_h8(base + static_cast<int64_t>(p_first) * s.C, f);
+      if (pre_bias != nullptr) {
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    shift[j] = 0.0f; s1[j] = 0.0f; s2[j] = 0.0f;
-    mn[j] = INFINITY; mx[j] = -INFINITY;
+        for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < GPV; ++g) {
+      shift[g] = f[g * kPerGroup];
+      s1[g] = 0.0f;
+      s2[g] = 0.0f;
+    }
+  }
+  if constexpr (MINMAX) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      mn[j] = INFINITY;
+      mx[j] = -INFINITY;
+    }
   }
 #pragma unroll 4
-  for (int p = tid / vpp; p < valid_pos; p += pos_per_iter) {
+  for (int p = p_first; p < valid_pos; p += pos_per_iter) {
     float f[8];
     load_h8(base + static_cast<int64_t>(p) * s.C, f);
     if (pre_bias != nullptr) {
 #pragma unroll
       for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
     }
-    if (n == 0) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) shift[j] = f[j];
-    }
-    ++n;
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float d = f[j] - shift[j];
-      s1[j] += d;
-      s2[j] = __fmaf_rn(d, d, s2[j]);
-      mn[j] = fminf(mn[j], f[j]);
-      mx[j] = fmaxf(mx[j], f[j]);
+      const int g = j / kPerGroup;
+      const float d = f[j] - shift[g];
+      s1[g] += d;
+      s2[g] = __fmaf_rn(d, d, s2[g]);
+      if constexpr (MINMAX) {
+        mn[j] = fminf(mn[j], f[j]);
+        mx[j] = fmaxf(mx[j], f[j]);
+      }
     }
   }
-  // Per-thread moments per group slot (a vector holds 8 / cg groups when cg < 8).
-  const int nslots = cg >= 8 ? 1 : 8 / cg;
-  const int per_slot = 8 / nslots;
-  const float fn = static_cast<float>(n);
+  const float fn = static_cast<float>(n * kPerGroup);
 #pragma unroll
-  for (int sl = 0; sl < 8; ++sl) {
-    if (sl >= nslots) break;
-    Moments acc{0.0f, 0.0f, 0.0f};
-    for (int j = sl * per_slot; j < (sl + 1) * per_slot; ++j) {
-      Moments m{fn, 0.0f, 0.0f};
-      if (n > 0) {
-        const float mu = __fdiv_rn(s1[j], fn);
-        m.mean = shift[j] + mu;
-        m.m2 = fmaxf(s2[j] - s1[j] * mu, 0.0f);
-      }
-      acc = merge_moments(acc, m);
+  for (int g = 0; g < GPV; ++g) {
+    Moments m{fn, 0.0f, 0.0f};
+    if (n > 0) {
+      const float mu = __fdiv_rn(s1[g], fn);
+      m.mean = shift[g] + mu;
+      m.m2 = fmaxf(s2[g] - s1[g] * mu, 0.0f);
     }
-    slots[tid][sl] = acc;
+    slots[tid][g] = m;
   }
   __syncthreads();
   if (tid < kGroups) {
-    // group tid: channels [tid*cg, (tid+1)*cg) -> vectors and slots
+    // group tid: channels [tid*cg, (tid+1)*cg) -> vectors v0..v1, slot within the vector
     Moments acc{0.0f, 0.0f, 0.0f};
     const int v0 = (tid * cg) / kVec, v1 = ((tid + 1) * cg - 1) / kVec;
-    const int sl = cg >= 8 ? 0 : (tid * cg % kVec) / cg;
+    const int sl = GPV == 1 ? 0 : (tid * cg % kVec) / cg;
     for (int vv = v0; vv <= v1; ++vv)
       for (int t = vv; t < kStatThreads; t += vpp) acc = merge_moments(acc, slots[t][sl]);
     partials[(static_cast<int64_t>(bt) * s.nchunks + chunk) * kGroups + tid] = make_float2(acc.mean, acc.m2);
   }
-  if (cmin != nullptr) {
+  if constexpr (MINMAX) {
+    __shared__ float red[kStatThreads * kVec];
+    __shared__ float chan[2048];
     channel_reduce<1>(mn, vpp, s.C, red, chan);
     for (int c = tid; c < s.C; c += kStatThreads) atomicMin(&cmin[static_cast<int64_t>(bt) * s.C + c], float_to_ordered(chan[c]));
     channel_reduce<2>(mx, vpp, s.C, red, chan);
@@ -271,13 +287,14 @@ __global__ void gn_merge_kernel(const float2* __restrict__ partials, NormShape s
 // walked with shifts only (C/8 is a power of two), so the kernel is bound by
 // HBM, not by index arithmetic.
 // ---------------------------------------------------------------------------
-template <int MODE>
-__global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* __restrict__ x,
-                                                                 const __half* __restrict__ pre_bias,
-                                                                 const __half* __restrict__ gamma,
-                                                                 const __half* __restrict__ beta,
-                                                                 const float2* __restrict__ stats, NormShape s,
-                                                                 float* amax, float* scale_out, void* out) {
+template <int MODE, int GPV>
+__global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kernel(const __half* __restrict__ x,
+                                                                    const __half* __restrict__ pre_bias,
+                                                                    const __half* __restrict__ gamma,
+                                                                    const __half* __restrict__ beta,
+                                                                    const float2* __restrict__ stats, NormShape s,
+                                                                    float* amax, float* scale_out, void* out) {
+  constexpr int kPerGroup = kVec / GPV;
   const int vpp = s.C / kVec;
   const int vshift = __ffs(vpp) - 1;
   const int cg = s.C / kGroups;
@@ -310,45 +327,72 @@ __global__ void __launch_bounds__(kPackThreads) norm_pack_kernel(const __half* _
   const float2* st = stats + (static_cast<int64_t>(b) * s.D + (frame_ok ? t : 0)) * kGroups;
   const int64_t out_row = static_cast<int64_t>(blockIdx.x) * row_vecs;
   // The block stride (256 vectors) is a multiple of C/8, so every thread keeps
-  // one channel vector: its affine constants and group statistics are loaded once.
+  // one channel vector: its affine constants (packed fp16) and the statistics
+  // of the GPV groups it touches are loaded once.
   const int v = threadIdx.x & (vpp - 1);
   const int c0 = v * kVec;
-  float gm[8], bt[8], pb[8], mean[8], rstd[8];
-  load_h8(gamma + c0, gm);
-  load_h8(beta + c0, bt);
-  if (pre_bias != nullptr) load_h8(pre_bias + c0, pb);
+  const uint4 gm = *reinterpret_cast<const uint4*>(gamma + c0);
+  const uint4 bt = *reinterpret_cast<const uint4*>(beta + c0);
+  const uint4 pbv = pre_bias != nullptr ? *reinterpret_cast<const uint4*>(pre_bias + c0) : make_uint4(0, 0, 0, 0);
+  float mean[GPV], rstd[GPV];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const float2 mr = st[(c0 + j) / cg];
-    mean[j] = mr.x;
-    rstd[j] = mr.y;
+  for (int g = 0; g < GPV; ++g) {
+    const float2 mr = st[(c0 + g * kPerGroup) / cg];
+    mean[g] = mr.x;
+    rstd[g] = mr.y;
   }
-  float local_max = 0.0f;
-  for (int i = threadIdx.x; i < row_vecs; i += kPackThreads) {
+  auto column = [&](int i) {
     int w = (i >> vshift) - ((MODE == 0) ? 0 : 1);
     w = w < 0 ? -w : (w >= s.Wu ? 2 * s.Wu - 2 - w : w);
-    if (s.us == 2) w >>= 1;
-    float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (frame_ok) {
-      float f[8];
-      load_h8(xrow + static_cast<int64_t>(w) * s.C + c0, f);
+    return s.us == 2 ? (w >> 1) : w;
+  };
+  auto values = [&](const uint4& raw, float (&z)[8]) {
+    const __half2* xv = reinterpret_cast<const __half2*>(&raw);
+    const __half2* g2 = reinterpret_cast<const __half2*>(&gm);
+    const __half2* b2 = reinterpret_cast<const __half2*>(&bt);
+    const __half2* p2 = reinterpret_cast<const __half2*>(&pbv);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float2 f = __half22float2(xv[e]);
       if (pre_bias != nullptr) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
+        const float2 pb = __half22float2(p2[e]);
+        f = __half22float2(__floats2half2_rn(__fadd_rn(f.x, pb.x), __fadd_rn(f.y, pb.y)));
       }
-#pragma unroll
-      for (int j = 0; j < 8; ++j) z[j] = norm_silu_value(f[j], mean[j], rstd[j], gm[j], bt[j]);
+      const float2 gf = __half22float2(g2[e]);
+      const float2 bf = __half22float2(b2[e]);
+      const int g0 = (2 * e) / kPerGroup, g1 = (2 * e + 1) / kPerGroup;
+      z[2 * e] = norm_silu_value(f.x, mean[g0], rstd[g0], gf.x, bf.x);
+      z[2 * e + 1] = norm_silu_value(f.y, mean[g1], rstd[g1], gf.y, bf.y);
     }
-    if (MODE == 0) {
+  };
+  float local_max = 0.0f;
+  // Two vectors per thread per step: both loads are issued before either is
+  // used, so each thread keeps two 16-byte reads in flight.
+  for (int i0 = threadIdx.x; i0 < row_vecs; i0 += 2 * kPackThreads) {
+    const int i1 = i0 + kPackThreads;
+    const bool has1 = i1 < row_vecs;
+    uint4 raw0 = make_uint4(0, 0, 0, 0), raw1 = make_uint4(0, 0, 0, 0);
+    if (frame_ok) {
+      raw0 = __ldg(reinterpret_cast<const uint4*>(xrow + static_cast<int64_t>(column(i0)) * s.C + c0));
+      if (has1) raw1 = __ldg(reinterpret_cast<const uint4*>(xrow + static_cast<int64_t>(column(i1)) * s.C + c0));
+    }
 #pragma unroll
-      for (int j = 0; j < 8; ++j) local_max = fmaxf(local_max, fabsf(z[j]));
-    } else if (MODE == 1) {
-      __align__(8) int8_t q[8];
+    for (int k = 0; k < 2; ++k) {
+      if (k == 1 && !has1) break;
+      const int i = k == 0 ? i0 : i1;
+      float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (frame_ok) values(k == 0 ? raw0 : raw1, z);
+      if (MODE == 0) {
 #pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = quant_half_away_fast(z[j], scale, inv_scale);
-      reinterpret_cast<uint2*>(out)[out_row + i] = *reinterpret_cast<const uint2*>(q);
-    } else {
-      store_h8(reinterpret_cast<__half*>(out) + (out_row + i) * kVec, z);
+        for (int j = 0; j < 8; ++j) local_max = fmaxf(local_max, fabsf(z[j]));
+      } else if (MODE == 1) {
+        __align__(8) int8_t q[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) q[j] = quant_half_away_fast(z[j], scale, inv_scale);
+        reinterpret_cast<uint2*>(out)[out_row + i] = *reinterpret_cast<const uint2*>(q);
+      } else {
+        store_h8(reinterpret_cast<__half*>(out) + (out_row + i) * kVec, z);
+      }
     }
   }
   if (MODE == 0) {
@@ -534,6 +578,24 @@ NormWorkspace norm_workspace_layout(const NormShape& s, void* base) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// GroupNorm groups inside one 8-channel vector (C / 32 channels per group).
+int groups_per_vector(int C) {
+  const int cg = C / kGroups;
+  return cg >= kVec ? 1 : kVec / cg;
+}
+
+// norm_pack_kernel<MODE, GPV> for the runtime group count.
+template <int MODE>
+void launch_norm_pack(unsigned grid, cudaStream_t st, const __half* x, const __half* pb, const __half* g,
+                      const __half* b, const float2* stats, const NormShape& s, float* amax, float* scale, void* out) {
+  switch (groups_per_vector(s.C)) {
+    case 1: norm_pack_kernel<MODE, 1><<<grid, kPackThreads, 0, st>>>(x, pb, g, b, stats, s, amax, scale, out); break;
+    case 2: norm_pack_kernel<MODE, 2><<<grid, kPackThreads, 0, st>>>(x, pb, g, b, stats, s, amax, scale, out); break;
+    case 4: norm_pack_kernel<MODE, 4><<<grid, kPackThreads, 0, st>>>(x, pb, g, b, stats, s, amax, scale, out); break;
+    default: norm_pack_kernel<MODE, 8><<<grid, kPackThreads, 0, st>>>(x, pb, g, b, stats, s, amax, scale, out); break;
+  }
+}
+
 // Statistics (+ absmax candidates when want_amax): memsets of the min/max/amax
 // words, the chunk-partial kernel and the merge kernel.
 int run_norm_stats(const void* x, const void* pre_bias, const void* gamma, const void* beta, float eps,
@@ -545,9 +607,20 @@ int run_norm_stats(const void* x, const void* pre_bias, const void* gamma, const
       return h3b_host::set_error(H3B_ECUDA, "%s: memset failed", name);
   }
   dim3 grid(s.nchunks, s.B * s.D);
-  gn_partial_kernel<<<grid, kStatThreads, 0, st>>>(static_cast<const __half*>(x),
-                                                   static_cast<const __half*>(pre_bias), s, w.partials,
-                                                   want_amax ? w.cmin : nullptr, want_amax ? w.cmax : nullptr);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* pb = static_cast<const __half*>(pre_bias);
+  unsigned int* cmin = want_amax ? w.cmin : nullptr;
+  unsigned int* cmax = want_amax ? w.cmax : nullptr;
+  switch (groups_per_vector(s.C) * 2 + (want_amax ? 1 : 0)) {
+    case 2: gn_partial_kernel<1, false><<<grid, kStatThreads, 0, st>>>(xh, pb, s, w.partials, cmin, cmax); break;
+    case 3: gn_partial_kernel<1, true><<<grid, kStatThreads, 0, st>>>(xh, pb, s, w.partials, cmin, cmax); break;
+    case 4: gn_partial_kernel<2, false><<<grid, kStatThreads, 0, st>>>(xh, pb, s, w.partials, cmin, cmax); break;
+    case 5: gn_partial_kernel<2, true><<<grid, kStatThreads, 0, st>>>(xh, pb, s, w.partials, cmin, cmax); break;
+    case 8: gn_partial_kernel<4, false><<<grid, kStatThreads, 0, st>>>(xh, pb, s, w.partials, cmin, cmax); break;
+    case 9: gn_partial_kernel<4, true><<<grid, kStatThreads, 0, st>>>(xh, pb, s, w.partials, cmin, cmax); break;
+    case 16: gn_partial_kernel<8, false><<<grid, kStatThreads, 0, st>>>(xh, pb, s, w.partials, cmin, cmax); break;
+    default: gn_partial_kernel<8, true><<<grid, kStatThreads, 0, st>>>(xh, pb, s, w.partials, cmin, cmax); break;
+  }
   int rc = h3b_host::check_launch(name);
   if (rc) return rc;
   gn_merge_kernel<<<s.B * s.D, 32 * kGroups, 0, st>>>(w.partials, s, eps, w.stats, want_amax ? w.cmin : nullptr,
@@ -600,12 +673,10 @@ int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H
   const __half* pb = static_cast<const __half*>(pre_bias);
   const __half* gh = static_cast<const __half*>(gamma);
   const __half* bh = static_cast<const __half*>(beta);
-  norm_pack_kernel<0><<<(unsigned)(B * s.Du * s.Hu), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax, nullptr,
-                                                                      nullptr);
+  launch_norm_pack<0>((unsigned)(B * s.Du * s.Hu), st, xh, pb, gh, bh, w.stats, s, w.amax, nullptr, nullptr);
   rc = h3b_host::check_launch(name);
   if (rc) return rc;
-  norm_pack_kernel<1><<<(unsigned)(B * (s.Du + 2) * (s.Hu + 2)), kPackThreads, 0, st>>>(xh, pb, gh, bh, w.stats, s, w.amax,
-                                                                                  scale, q);
+  launch_norm_pack<1>((unsigned)(B * (s.Du + 2) * (s.Hu + 2)), st, xh, pb, gh, bh, w.stats, s, w.amax, scale, q);
   return h3b_host::check_launch(name);
 }
 
@@ -676,9 +747,9 @@ int h3b_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, 
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   rc = run_norm_stats(x, pre_bias, gamma, beta, eps, s, w, false, st, name);
   if (rc) return rc;
-  norm_pack_kernel<2><<<(unsigned)(B * (s.Du + 2) * (s.Hu + 2)), kPackThreads, 0, st>>>(
-      static_cast<const __half*>(x), static_cast<const __half*>(pre_bias), static_cast<const __half*>(gamma),
-      static_cast<const __half*>(beta), w.stats, s, nullptr, nullptr, y);
+  launch_norm_pack<2>((unsigned)(B * (s.Du + 2) * (s.Hu + 2)), st, static_cast<const __half*>(x),
+                      static_cast<const __half*>(pre_bias), static_cast<const __half*>(gamma),
+                      static_cast<const __half*>(beta), w.stats, s, nullptr, nullptr, y);
   return h3b_host::check_launch(name);
 }
 
@@ -700,9 +771,9 @@ int h3b_upsample_norm_pad_f16(const void* x, int64_t B, int64_t C, int64_t D, in
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   rc = run_norm_stats(x, pre_bias, gamma, beta, eps, s, w, false, st, name);
   if (rc) return rc;
-  norm_pack_kernel<2><<<(unsigned)(B * (s.Du + 2) * (s.Hu + 2)), kPackThreads, 0, st>>>(
-      static_cast<const __half*>(x), static_cast<const __half*>(pre_bias), static_cast<const __half*>(gamma),
-      static_cast<const __half*>(beta), w.stats, s, nullptr, nullptr, y);
+  launch_norm_pack<2>((unsigned)(B * (s.Du + 2) * (s.Hu + 2)), st, static_cast<const __half*>(x),
+                      static_cast<const __half*>(pre_bias), static_cast<const __half*>(gamma),
+                      static_cast<const __half*>(beta), w.stats, s, nullptr, nullptr, y);
   return h3b_host::check_launch(name);
 }
 

@@ -346,7 +346,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n_tile = tile - m_group * p.n_tiles;
       const uint32_t acc = local & 1u;
       const uint32_t aph = (local >> 1) & 1u;
-      if (!mbar_wait(&tfull_bar[acc], aph, abort_flag)) break;
+      // tcgen05.ld is warp-collective: leave together if any lane's wait gave up
+      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[acc], aph, abort_flag))) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + acc * kAccStride + (static_cast<uint32_t>(quad * 32) << 16);
 

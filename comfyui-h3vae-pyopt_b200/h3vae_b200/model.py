@@ -81,15 +81,17 @@ def conv_f16(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, stride=(1
 
 
 class Conv3dF16:
-    """One fp16 valid conv of the model.  Channel counts that are a multiple of 64 run on the
-    tcgen05 fp16 implicit-GEMM kernel (bias and an optional residual add fused, stride-2 through
-    TMA element strides); the three narrow-input convs (3-channel pixels, 16-channel latents,
-    the 32-channel quant conv) stay on cuDNN."""
+    """One fp16 valid conv of the model.  Input channel counts that are a multiple of 64 with at
+    least 16 outputs run on the tcgen05 fp16 implicit-GEMM kernel (bias and an optional residual
+    add fused, stride-2 through TMA element strides).  The narrow ones stay on cuDNN: 16-channel
+    latents and the 32-channel quant conv (inputs narrower than one 128-byte K row) and the
+    3-channel RGB output conv, whose one 16-wide N tile would re-read the 27 shifted input taps
+    from L2 for very little MMA work."""
 
     def __init__(self, w: torch.Tensor, b: torch.Tensor | None, stride=(1, 1, 1)):
         self.w, self.b, self.stride = w, b, tuple(stride)
         self.kernel = tuple(int(k) for k in w.shape[2:])
-        self.packed = K.pack_conv_weight_f16(w) if w.shape[1] % 64 == 0 else None
+        self.packed = K.pack_conv_weight_f16(w) if (w.shape[1] % 64 == 0 and w.shape[0] >= 16) else None
 
     def __call__(self, x: torch.Tensor, *, residual: torch.Tensor | None = None, causal: bool = False,
                  bias: bool = True) -> torch.Tensor:

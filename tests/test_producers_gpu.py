@@ -214,6 +214,23 @@ def test_qk_rope_standalone(cuda_lib):
     _close(k.cpu().numpy(), rk)
 
 
+@pytest.mark.parametrize("mode", ["self", "rising"])
+def test_attention_running_max_moves(cuda_lib, mode):
+    """Rows whose running max jumps by a lot in a later key block (the diagonal of q = k = v, or keys
+    growing along the sequence) take the O rescale path while their warp neighbours may not."""
+    from h3vae_b200 import kernels as K
+    g = torch.Generator().manual_seed(11)
+    q = torch.randn(1, 2, 1024, 64, generator=g).half()
+    if mode == "self":
+        k = v = q
+    else:
+        k = (torch.randn(1, 2, 1024, 64, generator=g) * torch.linspace(0.2, 3.0, 1024).view(1, 1, -1, 1)).half()
+        v = torch.randn(1, 2, 1024, 64, generator=g).half()
+    out = K.attention_f16(q.cuda(), k.cuda(), v.cuda(), 0.125)
+    ref = O.attention(q.numpy(), k.numpy(), v.numpy(), 0.125)
+    _close(out.cpu().numpy(), ref, atol=4e-3, rtol=4e-3)
+
+
 @pytest.mark.parametrize("b,h,sq,skv", [(1, 2, 64, 64), (2, 3, 100, 77), (4, 16, 1024, 1024), (1, 2, 1797, 1797)])
 def test_attention(cuda_lib, b, h, sq, skv):
     from h3vae_b200 import kernels as K
