@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       uint32_t issued = 0;
       for (int j = 0; j < n_blocks; ++j, ++issued) {
         const int s = j % kFaStages;
-        if (!mbar_wait(&kv_empty[s], ((j / kFaStages) & 1) ^ 1, abort_flag)) break;
+        if (!mbar_poll(&kv_empty[s], ((j / kFaStages) & 1) ^ 1, abort_flag)) break;
         mbar_arrive_expect_tx(&kv_full[s], 2 * kFaKVBytes);
         tma_load_4d(sk + s * kFaKVBytes, &mk, &kv_full[s], 0, j * kFaN, h, b);
         tma_load_4d(sv + s * kFaKVBytes, &mv, &kv_full[s], 0, j * kFaN, h, b);
@@ -159,12 +159,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     if (elect_one_sync()) {
       constexpr uint32_t idesc_qk = make_idesc_f16(kFaM, kFaN);
       constexpr uint32_t idesc_pv = make_idesc_f16(kFaM, kFaD) | (1u << 16);  // B (V) is MN-major
-      bool ok = mbar_wait(q_full, 0, abort_flag);
+      bool ok = mbar_poll(q_full, 0, abort_flag);
       // S_j(t) into tile t's S columns; requires K_j resident and S_{j-1}(t) read out.
       auto issue_s = [&](int j, int t) -> bool {
         const int s = j % kFaStages;
-        if (!mbar_wait(&kv_full[s], (j / kFaStages) & 1, abort_flag)) return false;
-        if (!mbar_wait(&s_empty[t], (j & 1) ^ 1, abort_flag)) return false;
+        if (!mbar_poll(&kv_full[s], (j / kFaStages) & 1, abort_flag)) return false;
+        if (!mbar_poll(&s_empty[t], (j & 1) ^ 1, abort_flag)) return false;
         tc_fence_after();
         const uint64_t qdesc = make_sw128_desc(smem_u32(sq + t * kFaQBytes));
         const uint64_t kdesc = make_sw128_desc(smem_u32(sk + s * kFaKVBytes));
@@ -183,7 +183,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         for (int t = 0; t < kFaTiles && ok; ++t) {
           // P_j(t) written; O(t) holds the sum over the blocks before j,
           // already rescaled if the reference max moved.
-          if (!mbar_wait(&p_full[t], j & 1, abort_flag)) { ok = false; break; }
+          if (!mbar_poll(&p_full[t], j & 1, abort_flag)) { ok = false; break; }
           tc_fence_after();
           const uint32_t pbase = smem_u32(sp + t * kFaPBytes);
           const uint32_t vbase = smem_u32(sv + s * kFaKVBytes);
@@ -209,7 +209,9 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     const uint32_t t_o = t_lane + kFaN;
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
-    uint8_t* prow = sp + tile * kFaPBytes + row * 128;
+    const uint32_t prow = smem_u32(sp + tile * kFaPBytes + row * 128);
+    const uint32_t bar_s_full = smem_u32(&s_full[tile]), bar_s_empty = smem_u32(&s_empty[tile]);
+    const uint32_t bar_p_full = smem_u32(&p_full[tile]), bar_o_full = smem_u32(&o_full[tile]);
     // Named barriers 1 and 2 (both tiles' 256 softmax threads) pass the SFU turn:
     // tile 0 syncs on 1 and arrives on 2, tile 1 the reverse.  Tile 1 hands
     // tile 0 the first turn and skips its hand-back after the last block, so
@@ -223,9 +225,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         asm volatile("bar.arrive %0, %1;" ::"r"(tile == 0 ? 2 : 1), "r"(kSoftmaxThreads) : "memory");
     };
     if (tile == 1) asm volatile("bar.arrive 1, %0;" ::"r"(kSoftmaxThreads) : "memory");
-    const uint64_t scale2 = f2_pack(p.scale_log2, p.scale_log2);
     for (int j = 0; j < n_blocks; ++j) {
-      ok = __all_sync(0xffffffffu, ok && mbar_wait(&s_full[tile], j & 1, abort_flag));
+      ok = __all_sync(0xffffffffu, ok && mbar_wait_u32(bar_s_full, j & 1, abort_flag));
       const int valid = p.kv_len - j * kFaN;
       // All 128 scores of the row into registers with one TMEM round trip; the
       // S columns are released at once so S_{j+1} can be computed meanwhile.
@@ -236,7 +237,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv_[c * 32]));
         tmem_ld_wait();
         tc_fence_before();
-        mbar_arrive(&s_empty[tile]);
+        mbar_arrive_u32(bar_s_empty);
       } else {
 #pragma unroll
         for (int k = 0; k < 128; ++k) sv_[k] = 0xff800000u;   // -inf
@@ -260,31 +261,29 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       const float m_new = move ? m_blk : m;
       const float alpha = move ? ex2_approx(m - m_new) : 1.0f;
       // P V of block j-1 has finished: the P buffer is free and O(t) is stable.
-      if (j > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[tile], (j - 1) & 1, abort_flag));
+      if (j > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait_u32(bar_o_full, (j - 1) & 1, abort_flag));
       // The two tiles take turns on the SFU: tile 0 exponentiates block j after
       // tile 1 finished block j-1, tile 1 after tile 0 finished block j, so one
       // tile's exponentials overlap the other's TMEM reads, maximum and waits.
       exp_turn_begin();
       // P_j = exp2(S * scale - m) over the 128 keys
-      const uint64_t negm2 = f2_pack(-m_new, -m_new);
-      uint64_t sum2[2] = {f2_pack(0.0f, 0.0f), f2_pack(0.0f, 0.0f)};
+      const float negm = -m_new;
+      float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
         __align__(16) __half2 hv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int k = q * 8 + 2 * e;
-          float x0, x1;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(sv_[k]), __uint_as_float(sv_[k + 1])), scale2, negm2), x0, x1);
-          const float p0 = ex2_approx(x0);
-          const float p1 = ex2_approx(x1);
-          sum2[e & 1] = f2_add(sum2[e & 1], f2_pack(p0, p1));
+          const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(sv_[k]), p.scale_log2, negm));
+          const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(sv_[k + 1]), p.scale_log2, negm));
+          sums[e] += p0 + p1;
           hv[e] = __floats2half2_rn(p0, p1);
         }
         // keys q*8..q*8+7: swizzle column q/8, 16-byte chunk q%8 of this row
         if (ok)
-          *reinterpret_cast<uint4*>(prow + (q >> 3) * (kFaPBytes / 2) + (((q & 7) ^ (row & 7)) << 4)) =
-              *reinterpret_cast<const uint4*>(hv);
+          st_shared_v4(prow + (q >> 3) * (kFaPBytes / 2) + (((q & 7) ^ (row & 7)) << 4),
+                       *reinterpret_cast<const uint4*>(hv));
       }
       exp_turn_end(j);
       // O(t) rescale when the reference max moved (before P V of block j reads
@@ -308,14 +307,12 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       if (ok) {
         tc_fence_before();
         fence_proxy_async_smem();
-        mbar_arrive(&p_full[tile]);
+        mbar_arrive_u32(bar_p_full);
       }
-      float sa, sb_;
-      f2_unpack(f2_add(sum2[0], sum2[1]), sa, sb_);
-      l = __fmaf_rn(l, alpha, sa + sb_);
+      l = __fmaf_rn(l, alpha, (sums[0] + sums[1]) + (sums[2] + sums[3]));
       m = m_new;
     }
-    if (n_blocks > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait(&o_full[tile], (n_blocks - 1) & 1, abort_flag));
+    if (n_blocks > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait_u32(bar_o_full, (n_blocks - 1) & 1, abort_flag));
     const int qrow = (qt0 + tile) * kFaM + row;
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
     __half* dst = p.out + b * p.os[0] + h * p.os[1] + static_cast<int64_t>(qrow) * p.os[2];

@@ -99,6 +99,68 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// The same waits on a 32-bit shared-memory address (keeps register pressure
+// down in kernels that hold many values per thread).
+__device__ __forceinline__ bool mbar_try_wait_u32(uint32_t bar, uint32_t parity) {
+  uint32_t done = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+__device__ __forceinline__ bool mbar_wait_u32(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+    if (mbar_try_wait_u32(bar, parity)) return true;
+    if ((i & 1023u) == 1023u && abort_flag != nullptr && *abort_flag) return false;
+  }
+  record_error(kErrBarrierTimeout);
+  if (abort_flag != nullptr) *abort_flag = 1;
+  return false;
+}
+
+__device__ __forceinline__ void mbar_arrive_u32(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b64 st;\n\t"
+      "mbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
+  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded polling wait for the single-thread roles (TMA producer, MMA issuer):
+// test_wait never suspends, so the thread sees the phase flip at once instead
+// of after try_wait's suspend interval.  Same bound and error reporting as
+// mbar_wait.
+__device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  for (uint32_t i = 0; i < 4 * kSpinLimit; ++i) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((i & 4095u) == 4095u && abort_flag != nullptr && *abort_flag) return false;
+  }
+  record_error(kErrBarrierTimeout);
+  if (abort_flag != nullptr) *abort_flag = 1;
+  return false;
+}
+
 // Bounded wait on a phase parity.  Returns false (and records the error) if
 // the phase never completes or if another role already aborted the CTA.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
