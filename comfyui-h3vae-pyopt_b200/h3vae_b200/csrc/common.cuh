@@ -384,6 +384,37 @@ __device__ __forceinline__ int8_t quant_half_away_fast(float x, float scale, flo
   return static_cast<int8_t>(s < 0.0f ? -k : k);
 }
 
+// Per-tensor half-away quantization for the producers' hot loop.  Returns a
+// float whose low byte is the int8 result: s + 1.5 * 2^23 rounds s to the
+// nearest integer (ties to even) and keeps it in the low mantissa bits, so
+// the byte needs no float->int conversion, clamp or sign handling; bytes are
+// packed with byte permutes.  Only within 2^-13 of a .5 boundary can the
+// reciprocal-based quotient or the tie rule differ from the reference's
+// half-away rounding of the true quotient, and there the exact path runs.
+// |z| <= amax (the scale's own absmax) keeps |s| <= 127 up to rounding, so
+// no clamp is needed on the fast path.
+__device__ __noinline__ float quant_exact_bits(float z, float scale) {
+  constexpr float kMagic = 12582912.0f;
+  const float s = __fdiv_rn(z, scale);
+  float r = (s >= 0.0f) ? floorf(__fadd_rn(s, 0.5f)) : -floorf(__fadd_rn(-s, 0.5f));
+  r = fminf(fmaxf(r, -127.0f), 127.0f);
+  return __fadd_rn(r, kMagic);
+}
+
+__device__ __forceinline__ uint32_t quant_byte_bits(float z, float scale, float inv_scale) {
+  constexpr float kMagic = 12582912.0f;
+  const float s = __fmul_rn(z, inv_scale);
+  float t = __fadd_rn(s, kMagic);
+  const float d = __fsub_rn(s, __fsub_rn(t, kMagic));   // s - rne(s), in [-0.5, 0.5]
+  if (fabsf(d) > 0.5f - 1.0f / 8192.0f) t = quant_exact_bits(z, scale);
+  return __float_as_uint(t);
+}
+
+// Low bytes of four words into one word (byte 0 from a).
+__device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
+}
+
 // Order-preserving map of fp32 to uint32 (for atomicMin/atomicMax of signed
 // floats): non-negative values set the top bit, negative values are inverted.
 __device__ __forceinline__ unsigned int float_to_ordered(float f) {

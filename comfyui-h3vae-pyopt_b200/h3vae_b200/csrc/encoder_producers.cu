@@ -346,6 +346,8 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
     w = w < 0 ? -w : (w >= s.Wu ? 2 * s.Wu - 2 - w : w);
     return s.us == 2 ? (w >> 1) : w;
   };
+  // GroupNorm affine -> fp16 -> SiLU -> fp16 for 8 channels; every fp16
+  // rounding converts two values with one packed conversion.
   auto values = [&](const uint4& raw, float (&z)[8]) {
     const __half2* xv = reinterpret_cast<const __half2*>(&raw);
     const __half2* g2 = reinterpret_cast<const __half2*>(&gm);
@@ -361,8 +363,14 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
       const float2 gf = __half22float2(g2[e]);
       const float2 bf = __half22float2(b2[e]);
       const int g0 = (2 * e) / kPerGroup, g1 = (2 * e + 1) / kPerGroup;
-      z[2 * e] = norm_silu_value(f.x, mean[g0], rstd[g0], gf.x, bf.x);
-      z[2 * e + 1] = norm_silu_value(f.y, mean[g1], rstd[g1], gf.y, bf.y);
+      const float y0 = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(f.x, mean[g0]), rstd[g0]), gf.x), bf.x);
+      const float y1 = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(f.y, mean[g1]), rstd[g1]), gf.y), bf.y);
+      const float2 y = __half22float2(__floats2half2_rn(y0, y1));
+      const float s0 = __fdividef(y.x, __fadd_rn(1.0f, __expf(-y.x)));
+      const float s1 = __fdividef(y.y, __fadd_rn(1.0f, __expf(-y.y)));
+      const float2 zz = __half22float2(__floats2half2_rn(s0, s1));
+      z[2 * e] = zz.x;
+      z[2 * e + 1] = zz.y;
     }
   };
   float local_max = 0.0f;
@@ -386,10 +394,11 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
 #pragma unroll
         for (int j = 0; j < 8; ++j) local_max = fmaxf(local_max, fabsf(z[j]));
       } else if (MODE == 1) {
-        __align__(8) int8_t q[8];
+        uint32_t tb[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) q[j] = quant_half_away_fast(z[j], scale, inv_scale);
-        reinterpret_cast<uint2*>(out)[out_row + i] = *reinterpret_cast<const uint2*>(q);
+        for (int j = 0; j < 8; ++j) tb[j] = quant_byte_bits(z[j], scale, inv_scale);
+        reinterpret_cast<uint2*>(out)[out_row + i] =
+            make_uint2(pack_low_bytes(tb[0], tb[1], tb[2], tb[3]), pack_low_bytes(tb[4], tb[5], tb[6], tb[7]));
       } else {
         store_h8(reinterpret_cast<__half*>(out) + (out_row + i) * kVec, z);
       }
