@@ -6,3 +6,4 @@
 #include "decoder_producers.cu"
 #include "attention_tc.cu"
 #include "conv_in.cu"
+#include "conv_rgb.cu"

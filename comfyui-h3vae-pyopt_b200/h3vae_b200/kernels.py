@@ -177,6 +177,37 @@ def conv3d_f16(x: torch.Tensor, wpacked: torch.Tensor, bias: torch.Tensor | None
     return out
 
 
+def pack_rgb_weight(weight: torch.Tensor) -> torch.Tensor:
+    """[3, C, 3, 3, 3] -> fp16 [3*32, C]: row kd*32 + kh*9 + kw*3 + o = W[o, :, kd, kh, kw], rest zero."""
+    o, c = weight.shape[:2]
+    if o != 3 or tuple(weight.shape[2:]) != (3, 3, 3):
+        raise ValueError("RGB conv weight must be [3, C, 3, 3, 3]")
+    w = weight.detach().to(F16)
+    packed = torch.zeros((3, 32, c), dtype=F16, device=weight.device)
+    packed[:, :27] = w.permute(2, 3, 4, 0, 1).reshape(3, 27, c)   # [kd, kh*9 + kw*3 + o, C]
+    return packed.reshape(3 * 32, c).contiguous()
+
+
+def conv3d_rgb_f16(x: torch.Tensor, wpacked: torch.Tensor, bias: torch.Tensor | None) -> torch.Tensor:
+    """Valid 3x3x3 conv of a padded NDHWC fp16 activation to 3 channels (+bias) -> planar fp16
+    [B, 3, T, H, W]."""
+    dev = _require_cuda(x, wpacked, bias)
+    if x.ndim != 5 or x.dtype != F16 or not is_ndhwc(x):
+        raise ValueError("x must be a channels_last_3d fp16 [B,C,D,H,W] tensor")
+    _require(wpacked, F16, "weight")
+    _require(bias, F16, "bias")
+    b, c, d, h, w = x.shape
+    if wpacked.shape != (3 * 32, c) or (bias is not None and bias.shape != (3,)):
+        raise ValueError("packed RGB weight must be [96, C] and bias [3]")
+    if min(d, h, w) < 3:
+        raise ValueError("input too small for a valid 3x3x3 conv")
+    out = torch.empty((b, 3, d - 2, h - 2, w - 2), device=dev, dtype=F16)
+    _lib.check(_lib.load().h3b_conv3d_rgb_f16(x.data_ptr(), _lib.i64_array((b, d, h, w, c)), wpacked.data_ptr(),
+                                              _ptr(bias), out.data_ptr(), _stream(dev)))
+    _count(1)
+    return out
+
+
 def conv_in_f16(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
                 norm: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
     """Encoder input conv: optional pixel normalization fp16(((x+1)*0.5 - mean)/std), causal +

@@ -83,19 +83,22 @@ def conv_f16(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, stride=(1
 class Conv3dF16:
     """One fp16 valid conv of the model.  Input channel counts that are a multiple of 64 with at
     least 16 outputs run on the tcgen05 fp16 implicit-GEMM kernel (bias and an optional residual
-    add fused, stride-2 through TMA element strides).  The narrow ones stay on cuDNN: 16-channel
-    latents and the 32-channel quant conv (inputs narrower than one 128-byte K row) and the
-    3-channel RGB output conv, whose one 16-wide N tile would re-read the 27 shifted input taps
-    from L2 for very little MMA work."""
+    add fused, stride-2 through TMA element strides); the 3-channel RGB output conv runs on the
+    tap-packing kernel (h3b_conv3d_rgb_f16).  The narrow-input ones stay on cuDNN: 16-channel
+    latents and the 32-channel quant conv (inputs narrower than one 128-byte K row)."""
 
     def __init__(self, w: torch.Tensor, b: torch.Tensor | None, stride=(1, 1, 1)):
         self.w, self.b, self.stride = w, b, tuple(stride)
         self.kernel = tuple(int(k) for k in w.shape[2:])
         self.packed = K.pack_conv_weight_f16(w) if (w.shape[1] % 64 == 0 and w.shape[0] >= 16) else None
+        self.rgb = (K.pack_rgb_weight(w) if (w.shape[0] == 3 and w.shape[1] % 64 == 0 and w.shape[1] <= 256
+                                             and self.kernel == (3, 3, 3) and self.stride == (1, 1, 1)) else None)
 
     def __call__(self, x: torch.Tensor, *, residual: torch.Tensor | None = None, causal: bool = False,
                  bias: bool = True) -> torch.Tensor:
         b = self.b if bias else None
+        if self.rgb is not None and residual is None:
+            return K.conv3d_rgb_f16(K.ndhwc(x), self.rgb, b)
         if self.packed is not None:
             return K.conv3d_f16(K.ndhwc(x), self.packed, b, self.kernel, self.stride,
                                 causal_zero_frames=2 if causal else 0, residual=residual)

@@ -109,6 +109,20 @@ int h3b_conv_in_f16(const void* x, const int64_t* dims5, const int64_t* strides5
                     const float* norm_std, const void* w, int64_t out_channels, const void* bias,
                     void* out, void* workspace, size_t workspace_bytes, h3b_stream_t stream);
 
+/* Decoder output conv to RGB: 3x3x3 valid conv from C channels (C % 64 == 0,
+ * C <= 256) to 3, fp32 accumulate, + bias.  The 27 taps are packed into the
+ * MMA's N dimension (see conv_rgb.cu) so each input row is read once per
+ * temporal tap.
+ *   x         fp16 NDHWC contiguous padded [B, T+2, H+2, W+2, C]; x_dims {B, T+2, H+2, W+2, C}
+ *   w_packed  fp16 [3 * 32, C]: row kd*32 + kh*9 + kw*3 + o holds W[o, :, kd, kh, kw]
+ *             (rows kd*32 + 27..31 are zero)
+ *   bias      fp16 [3] or NULL
+ *   out       fp16 planar [B, 3, T, H, W]
+ * Replaces the cuDNN F.conv3d of the decoder's last conv (the reference runs
+ * the model's conv_out through cuDNN, h3vae_runtime.py:524-564 decode path) */
+int h3b_conv3d_rgb_f16(const void* x, const int64_t* x_dims, const void* w_packed, const void* bias, void* out,
+                       h3b_stream_t stream);
+
 /* ---- (a2) per-tensor activation quantization ---------------------------- */
 
 /* scale = max|x| * fp32(1/127) (0 -> 1);  q = clamp(half_away(x / scale), +-127)

@@ -110,3 +110,19 @@ def test_conv_in_matches_fp32_reference(cuda_lib, shape, normalize):
     y = K.conv_in_f16(x.cuda(), w.cuda(), b.cuda(), (mean.cuda(), std.cuda()) if normalize else None)
     assert y.is_contiguous(memory_format=torch.channels_last_3d)
     _close(y.cpu(), ref)
+
+
+@pytest.mark.parametrize("shape", [(1, 128, 7, 18, 258), (2, 64, 5, 11, 40), (1, 256, 3, 9, 131), (1, 128, 19, 34, 130)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_conv_rgb_matches_fp32_reference(cuda_lib, shape, with_bias):
+    """Decoder RGB output conv (taps packed into N, kw shift across TMEM lanes) vs PyTorch fp32."""
+    from h3vae_b200 import kernels as K
+    g = torch.Generator().manual_seed(sum(shape) + int(with_bias))
+    c = shape[1]
+    x = torch.randn(shape, generator=g).half()
+    w = (torch.randn((3, c, 3, 3, 3), generator=g) / (27 * c) ** 0.5).half()
+    b = (torch.randn(3, generator=g) * 0.1).half() if with_bias else None
+    y = K.conv3d_rgb_f16(x.cuda().contiguous(memory_format=torch.channels_last_3d), K.pack_rgb_weight(w).cuda(),
+                         None if b is None else b.cuda())
+    assert y.is_contiguous()
+    _close(y.cpu(), _ref(x, w, b, (1, 1, 1)))
