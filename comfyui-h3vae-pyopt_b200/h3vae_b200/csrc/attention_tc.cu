@@ -233,8 +233,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       uint32_t sv_[128];
       if (ok) {
         tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(t_s + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv_[c * 32]));
+        tmem_ld128(t_s, sv_);
         tmem_ld_wait();
         tc_fence_before();
         mbar_arrive_u32(bar_s_empty);
