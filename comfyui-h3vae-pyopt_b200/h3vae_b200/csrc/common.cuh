@@ -391,6 +391,41 @@ __device__ __forceinline__ int8_t quant_half_away_fast(float x, float scale, flo
   return static_cast<int8_t>(s < 0.0f ? -k : k);
 }
 
+// Packed fp32 pair arithmetic (Blackwell f32x2): one instruction per pair, each
+// lane rounded exactly like the scalar op.
+__device__ __forceinline__ float2 f2x_fma(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 x, y, z;\n\t"
+      "mov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\tmov.b64 z, {%5, %6};\n\t"
+      "fma.rn.f32x2 %0, x, y, z;\n\t}"
+      : "=l"(d) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(d)), __uint_as_float(static_cast<uint32_t>(d >> 32)));
+}
+__device__ __forceinline__ float2 f2x_mul(float2 a, float2 b) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 x, y;\n\t"
+      "mov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
+      "mul.rn.f32x2 %0, x, y;\n\t}"
+      : "=l"(d) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(d)), __uint_as_float(static_cast<uint32_t>(d >> 32)));
+}
+__device__ __forceinline__ float2 f2x_add(float2 a, float2 b) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 x, y;\n\t"
+      "mov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
+      "add.rn.f32x2 %0, x, y;\n\t}"
+      : "=l"(d) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(d)), __uint_as_float(static_cast<uint32_t>(d >> 32)));
+}
+__device__ __forceinline__ float2 f2x_sub(float2 a, float2 b) {
+  uint64_t d;
+  asm("{\n\t.reg .b64 x, y;\n\t"
+      "mov.b64 x, {%1, %2};\n\tmov.b64 y, {%3, %4};\n\t"
+      "sub.rn.f32x2 %0, x, y;\n\t}"
+      : "=l"(d) : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return make_float2(__uint_as_float(static_cast<uint32_t>(d)), __uint_as_float(static_cast<uint32_t>(d >> 32)));
+}
+
 // Per-tensor half-away quantization for the producers' hot loop.  Returns a
 // float whose low byte is the int8 result: s + 1.5 * 2^23 rounds s to the
 // nearest integer (ties to even) and keeps it in the low mantissa bits, so
@@ -415,6 +450,19 @@ __device__ __forceinline__ uint32_t quant_byte_bits(float z, float scale, float 
   const float d = __fsub_rn(s, __fsub_rn(t, kMagic));   // s - rne(s), in [-0.5, 0.5]
   if (fabsf(d) > 0.5f - 1.0f / 8192.0f) t = quant_exact_bits(z, scale);
   return __float_as_uint(t);
+}
+
+// quant_byte_bits for two values with packed fp32 pair arithmetic.
+__device__ __forceinline__ void quant_byte_bits2(float z0, float z1, float scale, float inv_scale, uint32_t& t0,
+                                                 uint32_t& t1) {
+  constexpr float kMagic = 12582912.0f;
+  const float2 m2 = make_float2(kMagic, kMagic);
+  const float2 sv = f2x_mul(make_float2(z0, z1), make_float2(inv_scale, inv_scale));
+  const float2 tv = f2x_add(sv, m2);
+  const float2 dv = f2x_sub(sv, f2x_sub(tv, m2));   // s - rne(s)
+  constexpr float kNearTie = 0.5f - 1.0f / 8192.0f;
+  t0 = fabsf(dv.x) > kNearTie ? __float_as_uint(quant_exact_bits(z0, scale)) : __float_as_uint(tv.x);
+  t1 = fabsf(dv.y) > kNearTie ? __float_as_uint(quant_exact_bits(z1, scale)) : __float_as_uint(tv.y);
 }
 
 // Low bytes of four words into one word (byte 0 from a).

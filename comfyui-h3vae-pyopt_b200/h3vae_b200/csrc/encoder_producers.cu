@@ -143,8 +143,20 @@ __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* 
   const int valid_pos = min(s.positions_per_chunk, HW - p0);
   const int cg = s.C / kGroups;
 
-  float pb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (pre_bias != nullptr) load_h8(pre_bias + c0, pb);
+  // fp16(x + pre_bias) as one fp16 add per pair: identical to rounding the fp32
+  // sum to fp16 (fp32 carries more than 2*11 + 2 bits).
+  const uint4 pbv = pre_bias != nullptr ? *reinterpret_cast<const uint4*>(pre_bias + c0) : make_uint4(0, 0, 0, 0);
+  auto load_biased = [&](const __half* src, float (&v)[8]) {
+    uint4 raw = *reinterpret_cast<const uint4*>(src);
+    __half2* h = reinterpret_cast<__half2*>(&raw);
+    const __half2* pb = reinterpret_cast<const __half2*>(&pbv);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(pre_bias != nullptr ? __hadd2(h[j], pb[j]) : h[j]);
+      v[2 * j] = f.x;
+      v[2 * j + 1] = f.y;
+    }
+  };
 
   const __half* base = x + (static_cast<int64_t>(bt) * HW + p0) * s.C + c0;
   float shift[GPV], s1[GPV], s2[GPV];
@@ -153,13 +165,7 @@ __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* 
   const int n = p_first < valid_pos ? (valid_pos - p_first + pos_per_iter - 1) / pos_per_iter : 0;
   {
     float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (n > 0) {
-      load_h8(base + static_cast<int64_t>(p_first) * s.C, f);
-      if (pre_bias != nullptr) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
-      }
-    }
+    if (n > 0) load_biased(base + static_cast<int64_t>(p_first) * s.C, f);
 #pragma unroll
     for (int g = 0; g < GPV; ++g) {
       shift[g] = f[g * kPerGroup];
@@ -177,11 +183,7 @@ __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* 
 #pragma unroll 4
   for (int p = p_first; p < valid_pos; p += pos_per_iter) {
     float f[8];
-    load_h8(base + static_cast<int64_t>(p) * s.C, f);
-    if (pre_bias != nullptr) {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) f[j] = round_fp16(__fadd_rn(f[j], pb[j]));
-    }
+    load_biased(base + static_cast<int64_t>(p) * s.C, f);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int g = j / kPerGroup;
@@ -348,6 +350,10 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
   };
   // GroupNorm affine -> fp16 -> SiLU -> fp16 for 8 channels; every fp16
   // rounding converts two values with one packed conversion.
+  // GroupNorm affine -> fp16 -> SiLU -> fp16 for 8 channels, two at a time.
+  // fp16(x + pre_bias) is one fp16 add (an fp16 sum rounded once equals the
+  // fp32 sum rounded to fp16: fp32 carries more than 2*11 + 2 bits), the fp32
+  // steps run as packed pairs, every fp16 rounding is one packed conversion.
   auto values = [&](const uint4& raw, float (&z)[8]) {
     const __half2* xv = reinterpret_cast<const __half2*>(&raw);
     const __half2* g2 = reinterpret_cast<const __half2*>(&gm);
@@ -355,19 +361,13 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
     const __half2* p2 = reinterpret_cast<const __half2*>(&pbv);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float2 f = __half22float2(xv[e]);
-      if (pre_bias != nullptr) {
-        const float2 pb = __half22float2(p2[e]);
-        f = __half22float2(__floats2half2_rn(__fadd_rn(f.x, pb.x), __fadd_rn(f.y, pb.y)));
-      }
-      const float2 gf = __half22float2(g2[e]);
-      const float2 bf = __half22float2(b2[e]);
+      const float2 f = __half22float2(pre_bias != nullptr ? __hadd2(xv[e], p2[e]) : xv[e]);
       const int g0 = (2 * e) / kPerGroup, g1 = (2 * e + 1) / kPerGroup;
-      const float y0 = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(f.x, mean[g0]), rstd[g0]), gf.x), bf.x);
-      const float y1 = __fadd_rn(__fmul_rn(__fmul_rn(__fsub_rn(f.y, mean[g1]), rstd[g1]), gf.y), bf.y);
-      const float2 y = __half22float2(__floats2half2_rn(y0, y1));
-      const float s0 = __fdividef(y.x, __fadd_rn(1.0f, __expf(-y.x)));
-      const float s1 = __fdividef(y.y, __fadd_rn(1.0f, __expf(-y.y)));
+      const float2 n = f2x_mul(f2x_sub(f, make_float2(mean[g0], mean[g1])), make_float2(rstd[g0], rstd[g1]));
+      const float2 ya = f2x_add(f2x_mul(n, __half22float2(g2[e])), __half22float2(b2[e]));
+      const float2 yr = __half22float2(__floats2half2_rn(ya.x, ya.y));
+      const float s0 = __fdividef(yr.x, __fadd_rn(1.0f, __expf(-yr.x)));
+      const float s1 = __fdividef(yr.y, __fadd_rn(1.0f, __expf(-yr.y)));
       const float2 zz = __half22float2(__floats2half2_rn(s0, s1));
       z[2 * e] = zz.x;
       z[2 * e + 1] = zz.y;
@@ -396,7 +396,7 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
       } else if (MODE == 1) {
         uint32_t tb[8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) tb[j] = quant_byte_bits(z[j], scale, inv_scale);
+        for (int j = 0; j < 8; j += 2) quant_byte_bits2(z[j], z[j + 1], scale, inv_scale, tb[j], tb[j + 1]);
         reinterpret_cast<uint2*>(out)[out_row + i] =
             make_uint2(pack_low_bytes(tb[0], tb[1], tb[2], tb[3]), pack_low_bytes(tb[4], tb[5], tb[6], tb[7]));
       } else {
