@@ -32,6 +32,10 @@ _SIGNATURES = {
     "h3b_conv3d_f16": (c_int, [c_void_p, _i64p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
                                c_void_p, c_void_p, _i64p, c_void_p, c_int, c_void_p]),
     "h3b_conv3d_rgb_f16": (c_int, [c_void_p, _i64p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "h3b_conv3d_i8_token": (c_int, [c_void_p, _i64p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
+                                    c_void_p, c_void_p, c_void_p, c_void_p, _i64p, c_void_p, c_int, c_void_p]),
+    "h3b_norm_pad_quant_token": (c_int, [c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                                         c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "h3b_conv_in_workspace_size": (c_size_t, [c_int64] * 4),
     "h3b_conv_in_f16": (c_int, [c_void_p, _i64p, _i64p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                                 c_void_p, c_size_t, c_void_p]),

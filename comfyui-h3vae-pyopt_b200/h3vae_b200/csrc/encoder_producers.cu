@@ -418,6 +418,94 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
 }
 
 // ---------------------------------------------------------------------------
+// Per-token INT8 producer: GroupNorm affine -> fp16 -> SiLU -> fp16 -> reflect /
+// causal pad, then one scale per padded position (absmax over its C channels
+// * fp32(1/127), 0 -> 1) and half-away quantization.  One warp per position:
+// lane l owns channels [l*CPL, (l+1)*CPL) with CPL = C/32, which is exactly
+// GroupNorm group l, so each lane needs one (mean, rstd) pair; the position's
+// absmax is a warp max.
+// ---------------------------------------------------------------------------
+template <int CPL>
+__global__ void __launch_bounds__(256) norm_pack_token_kernel(const __half* __restrict__ x,
+                                                              const __half* __restrict__ pre_bias,
+                                                              const __half* __restrict__ gamma,
+                                                              const __half* __restrict__ beta,
+                                                              const float2* __restrict__ stats, NormShape s,
+                                                              int8_t* __restrict__ q, float* __restrict__ scales) {
+  static_assert(CPL == 4 || CPL == 8 || CPL == 16, "128, 256 or 512 channels");
+  constexpr int kPairs = CPL / 2;
+  const int lane = threadIdx.x & 31;
+  const int64_t warp0 = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+  const int Dp = s.D + 2, Hp = s.H + 2, Wp = s.W + 2;
+  const int64_t npos = static_cast<int64_t>(s.B) * Dp * Hp * Wp;
+  const int c0 = lane * CPL;
+  __half2 g2[kPairs], b2[kPairs], p2[kPairs];
+#pragma unroll
+  for (int k = 0; k < kPairs; ++k) {
+    g2[k] = reinterpret_cast<const __half2*>(gamma + c0)[k];
+    b2[k] = reinterpret_cast<const __half2*>(beta + c0)[k];
+    p2[k] = pre_bias != nullptr ? reinterpret_cast<const __half2*>(pre_bias + c0)[k] : __floats2half2_rn(0.f, 0.f);
+  }
+  for (int64_t pos = warp0; pos < npos; pos += nwarps) {
+    int64_t r = pos;
+    const int wp = static_cast<int>(r % Wp); r /= Wp;
+    const int hp = static_cast<int>(r % Hp); r /= Hp;
+    const int tp = static_cast<int>(r % Dp);
+    const int b = static_cast<int>(r / Dp);
+    const int t = tp - 2;
+    int h = hp - 1, w = wp - 1;
+    h = h < 0 ? -h : (h >= s.H ? 2 * s.H - 2 - h : h);
+    w = w < 0 ? -w : (w >= s.W ? 2 * s.W - 2 - w : w);
+    float z[CPL];
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) z[k] = 0.0f;
+    if (t >= 0) {
+      const __half2* src = reinterpret_cast<const __half2*>(
+          x + (((static_cast<int64_t>(b) * s.D + t) * s.H + h) * s.W + w) * s.C + c0);
+      __half2 xv[kPairs];
+#pragma unroll
+      for (int k = 0; k < kPairs; ++k) xv[k] = src[k];
+      const float2 mr = stats[(static_cast<int64_t>(b) * s.D + t) * kGroups + lane];
+#pragma unroll
+      for (int k = 0; k < kPairs; ++k) {
+        const float2 f = __half22float2(pre_bias != nullptr ? __hadd2(xv[k], p2[k]) : xv[k]);
+        const float2 n = f2x_mul(f2x_sub(f, make_float2(mr.x, mr.x)), make_float2(mr.y, mr.y));
+        const float2 ya = f2x_add(f2x_mul(n, __half22float2(g2[k])), __half22float2(b2[k]));
+        const float2 yr = __half22float2(__floats2half2_rn(ya.x, ya.y));
+        const float s0 = __fdividef(yr.x, __fadd_rn(1.0f, __expf(-yr.x)));
+        const float s1 = __fdividef(yr.y, __fadd_rn(1.0f, __expf(-yr.y)));
+        const float2 zz = __half22float2(__floats2half2_rn(s0, s1));
+        z[2 * k] = zz.x;
+        z[2 * k + 1] = zz.y;
+      }
+    }
+    float amax = 0.0f;
+#pragma unroll
+    for (int k = 0; k < CPL; ++k) amax = fmaxf(amax, fabsf(z[k]));
+    amax = warp_max(amax);
+    float scale = __fmul_rn(amax, 1.0f / 127.0f);
+    if (!(scale > 0.0f)) scale = 1.0f;
+    const float inv_scale = __frcp_rn(scale);
+    uint32_t tb[CPL];
+#pragma unroll
+    for (int k = 0; k < CPL; k += 2) quant_byte_bits2(z[k], z[k + 1], scale, inv_scale, tb[k], tb[k + 1]);
+    int8_t* dst = q + pos * s.C + c0;
+    if constexpr (CPL == 4) {
+      *reinterpret_cast<uint32_t*>(dst) = pack_low_bytes(tb[0], tb[1], tb[2], tb[3]);
+    } else if constexpr (CPL == 8) {
+      *reinterpret_cast<uint2*>(dst) =
+          make_uint2(pack_low_bytes(tb[0], tb[1], tb[2], tb[3]), pack_low_bytes(tb[4], tb[5], tb[6], tb[7]));
+    } else {
+      *reinterpret_cast<uint4*>(dst) =
+          make_uint4(pack_low_bytes(tb[0], tb[1], tb[2], tb[3]), pack_low_bytes(tb[4], tb[5], tb[6], tb[7]),
+                     pack_low_bytes(tb[8], tb[9], tb[10], tb[11]), pack_low_bytes(tb[12], tb[13], tb[14], tb[15]));
+    }
+    if (lane == 0) scales[pos] = scale;
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Residual + bias pack with right/bottom reflect (+1) and two causal zero
 // frames: y = fp16(r + (x + bias)) in fp32.  One CTA per output row.
 // ---------------------------------------------------------------------------
@@ -686,6 +774,36 @@ int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H
   rc = h3b_host::check_launch(name);
   if (rc) return rc;
   launch_norm_pack<1>((unsigned)(B * (s.Du + 2) * (s.Hu + 2)), st, xh, pb, gh, bh, w.stats, s, w.amax, scale, q);
+  return h3b_host::check_launch(name);
+}
+
+int h3b_norm_pad_quant_token(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
+                             const void* pre_bias, const void* gamma, const void* beta, float eps, int8_t* q,
+                             float* scales, void* workspace, size_t workspace_bytes, h3b_stream_t stream) {
+  const char* name = "h3b_norm_pad_quant_token";
+  NormShape s;
+  NormWorkspace w;
+  int rc = check_norm_args(x, pre_bias, gamma, beta, q, workspace, workspace_bytes, B, C, D, H, W, &s, &w, name);
+  if (rc) return rc;
+  if (!scales) return h3b_host::set_error(H3B_EINVAL, "%s: NULL scales", name);
+  if (C != 128 && C != 256 && C != 512)
+    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: per-token producer supports C = 128, 256, 512 (got %lld)", name,
+                               (long long)C);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  rc = run_norm_stats(x, pre_bias, gamma, beta, eps, s, w, false, st, name);
+  if (rc) return rc;
+  const int64_t npos = B * (D + 2) * (H + 2) * (W + 2);
+  const int64_t blocks = std::min<int64_t>((npos * 32 + 255) / 256, static_cast<int64_t>(h3b_host::num_sms()) * 16);
+  const __half* xh = static_cast<const __half*>(x);
+  const __half* pb = static_cast<const __half*>(pre_bias);
+  const __half* gh = static_cast<const __half*>(gamma);
+  const __half* bh = static_cast<const __half*>(beta);
+  if (C == 128)
+    norm_pack_token_kernel<4><<<(unsigned)blocks, 256, 0, st>>>(xh, pb, gh, bh, w.stats, s, q, scales);
+  else if (C == 256)
+    norm_pack_token_kernel<8><<<(unsigned)blocks, 256, 0, st>>>(xh, pb, gh, bh, w.stats, s, q, scales);
+  else
+    norm_pack_token_kernel<16><<<(unsigned)blocks, 256, 0, st>>>(xh, pb, gh, bh, w.stats, s, q, scales);
   return h3b_host::check_launch(name);
 }
 

@@ -489,6 +489,212 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// INT8 conv with per-token activation scales (one fp32 scale per padded input
+// position).  The scale is not constant along a row of the im2col matrix --
+// every tap reads a different input position -- so it cannot be applied after
+// the int32 reduction.  The MMA warp therefore closes the accumulation after
+// every 128-channel k-block (|partial| <= 128*127*127 < 2^22) into one of two
+// TMEM buffers, and the epilogue warps fold each partial into fp32 registers
+// as acc += float(P) * s_x[input position of that tap] (int32 -> fp32 through
+// the 1.5 * 2^23 magic constant, exact below 2^22), then write
+// fp16(fma(acc, s_w[n], bias[n])) (+ residual) once per tile.  BN = 128; each
+// epilogue thread keeps one row x 64 columns.
+// ---------------------------------------------------------------------------
+template <int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_i8_token_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                         const MmaParams p, const float* __restrict__ x_scales, int Dp, int Hp, int Wp) {
+  constexpr int BN = 128;
+  constexpr uint32_t kBTileBytes = BN * kBK;
+  constexpr uint32_t kStageBytes = kATileBytes + kBTileBytes;
+  constexpr uint32_t kIdesc = make_idesc_i8(kBM, BN);
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + STAGES * kATileBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * kStageBytes);
+  uint64_t* full_bar = bars;
+  uint64_t* empty_bar = bars + STAGES;
+  uint64_t* pfull_bar = bars + 2 * STAGES;        // [2] partial accumulator ready
+  uint64_t* pempty_bar = bars + 2 * STAGES + 2;   // [2] partial consumed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_tiles = p.m_tiles * p.n_tiles;
+
+  auto conv_tile = [&](int m_tile, int& b, int& od, int& oh0, int& ow0) {
+    int t = m_tile;
+    const int tw = t % p.w_tiles; t /= p.w_tiles;
+    const int th = t % p.h_tiles; t /= p.h_tiles;
+    od = t % p.Do;
+    b = t / p.Do;
+    oh0 = th * p.bh;
+    ow0 = tw * p.bw;
+  };
+  auto first_kblock = [&](int m_tile) {
+    if (!p.causal) return 0;
+    const int od = (m_tile / (p.w_tiles * p.h_tiles)) % p.Do;
+    return max(0, 2 - od * p.sd) * p.kh * p.kw * p.c_chunks;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&pfull_bar[a], 1);
+      mbar_init(&pempty_bar[a], 32 * kEpiWarps);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------ TMA producer ------------------------------
+    if (elect_one_sync()) {
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m_tile = tile / p.n_tiles;
+        const int n_tile = tile - m_tile * p.n_tiles;
+        int b, od, oh0, ow0;
+        conv_tile(m_tile, b, od, oh0, ow0);
+        for (int kb = first_kblock(m_tile); kb < p.k_blocks; ++kb, ++it) {
+          const uint32_t s = it % STAGES;
+          if (!mbar_poll(&empty_bar[s], ((it / STAGES) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full_bar[s], kStageBytes);
+          const int tap = kb / p.c_chunks;
+          const int cc = kb - tap * p.c_chunks;
+          const int tkw = tap % p.kw, tkh = (tap / p.kw) % p.kh, tkd = tap / (p.kw * p.kh);
+          tma_load_5d(smem_a + s * kATileBytes, &map_a, &full_bar[s], cc * kBK, ow0 * p.sw + tkw, oh0 * p.sh + tkh,
+                      od * p.sd + tkd, b);
+          tma_load_2d(smem_b + s * kBTileBytes, &map_b, &full_bar[s], kb * kBK, n_tile * BN);
+        }
+      }
+      for (uint32_t s = 0; s < STAGES && s < it; ++s) {
+        const uint32_t last = it - 1 - ((it - 1 - s) % STAGES);
+        mbar_wait(&full_bar[s], (last / STAGES) & 1u, nullptr);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------- MMA issuer -------------------------------
+    if (elect_one_sync()) {
+      uint32_t it = 0, part = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        for (int kb = first_kblock(tile / p.n_tiles); kb < p.k_blocks && ok; ++kb, ++it, ++part) {
+          const uint32_t buf = part & 1u;
+          if (!mbar_poll(&pempty_bar[buf], ((part >> 1) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
+          const uint32_t s = it % STAGES;
+          if (!mbar_poll(&full_bar[s], (it / STAGES) & 1u, abort_flag)) { ok = false; break; }
+          tc_fence_after();
+          const uint64_t adesc = make_sw128_desc(smem_u32(smem_a + s * kATileBytes));
+          const uint64_t bdesc = make_sw128_desc(smem_u32(smem_b + s * kBTileBytes));
+#pragma unroll
+          for (int k = 0; k < kBK / 32; ++k)
+            mma_i8(tmem_base + buf * BN, adesc + 2 * k, bdesc + 2 * k, kIdesc, k > 0 ? 1u : 0u);
+          tc_commit(&empty_bar[s]);
+          tc_commit(&pfull_bar[buf]);
+        }
+      }
+    }
+  } else {
+    // -------------------------------- epilogue --------------------------------
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const int half = (warp - 2) >> 2;   // columns half*64 .. +64
+    constexpr float kMagic = 12582912.0f;
+    uint32_t part = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m_tile = tile / p.n_tiles;
+      const int n_tile = tile - m_tile * p.n_tiles;
+      int b, od, oh0, ow0;
+      conv_tile(m_tile, b, od, oh0, ow0);
+      const int oh = oh0 + row / p.bw;
+      const int ow = ow0 + row % p.bw;
+      const bool valid = (oh < p.Ho) && (ow < p.Wo);
+      float acc[64];
+#pragma unroll
+      for (int j = 0; j < 64; ++j) acc[j] = 0.0f;
+      bool ok = true;
+      for (int kb = first_kblock(m_tile); kb < p.k_blocks; ++kb, ++part) {
+        const uint32_t buf = part & 1u;
+        ok = __all_sync(0xffffffffu, ok && mbar_wait(&pfull_bar[buf], (part >> 1) & 1u, abort_flag));
+        const int tap = kb / p.c_chunks;
+        const int tkw = tap % p.kw, tkh = (tap / p.kw) % p.kh, tkd = tap / (p.kw * p.kh);
+        float sx = 0.0f;
+        if (valid) {
+          const int64_t ip = ((static_cast<int64_t>(b) * Dp + od * p.sd + tkd) * Hp + oh * p.sh + tkh) * Wp +
+                             ow * p.sw + tkw;
+          sx = __ldg(x_scales + ip);
+        }
+        if (ok) {
+          tc_fence_after();
+          const uint32_t t_row = tmem_base + buf * BN + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            uint32_t r[32];
+            tmem_ld32(t_row + c * 32, r);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+              // exact int32 -> fp32 below 2^22: (M + P) - M
+              const float2 f = f2x_sub(make_float2(__int_as_float(0x4B400000 + static_cast<int>(r[j])),
+                                                   __int_as_float(0x4B400000 + static_cast<int>(r[j + 1]))),
+                                       make_float2(kMagic, kMagic));
+              const float2 v = f2x_fma(f, make_float2(sx, sx), make_float2(acc[c * 32 + j], acc[c * 32 + j + 1]));
+              acc[c * 32 + j] = v.x;
+              acc[c * 32 + j + 1] = v.y;
+            }
+          }
+          tc_fence_before();
+        }
+        mbar_arrive(&pempty_bar[buf]);
+      }
+      if (!ok || !valid) continue;
+      const int64_t obase = b * p.osB + od * p.osD + static_cast<int64_t>(oh) * p.osH + static_cast<int64_t>(ow) * p.osW;
+      const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0) && (p.osW % 8 == 0) &&
+                          (p.osH % 8 == 0) && (p.osD % 8 == 0) && (p.osB % 8 == 0);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int n0 = n_tile * BN + half * 64 + c * 32;
+        const int valid_cols = p.N - n0;
+        if (valid_cols <= 0) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int n = min(n0 + j, p.N - 1);
+          v[j] = p.bias != nullptr ? __fmaf_rn(acc[c * 32 + j], p.w_scale[n], __half2float(p.bias[n]))
+                                   : __fmul_rn(acc[c * 32 + j], p.w_scale[n]);
+        }
+        if (p.residual != nullptr) add_residual_chunk(v, p.residual + obase + n0, valid_cols, vec_ok);
+        store_row_chunk(p.out + obase + n0, v, valid_cols, vec_ok);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, 256);
+}
+
+// ---------------------------------------------------------------------------
 // Generic SIMT fallback for conv geometries outside the TMA contract
 // (channel counts not a multiple of 128, stride 2, 1-wide temporal kernels
 // mixed with strides).  Exact int32 accumulation, same epilogue.
@@ -728,6 +934,67 @@ int h3b_conv3d_i8(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int
     return h3b_host::check_launch(name);
   }
   return conv3d_tc<false>(a, Do, Ho, Wo, name);
+}
+
+int h3b_conv3d_i8_token(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int64_t out_channels, int kd,
+                        int kh, int kw, int sd, int sh, int sw, const float* x_scales, const float* w_scale,
+                        const void* bias, void* out, const int64_t* out_strides, const void* residual,
+                        int causal_zero_frames, h3b_stream_t stream) {
+  const char* name = "h3b_conv3d_i8_token";
+  ConvArgs a{qx, x_dims, qw, out_channels, kd, kh, kw, sd, sh, sw, x_scales, w_scale, bias, out, out_strides,
+             residual, nullptr, causal_zero_frames, reinterpret_cast<cudaStream_t>(stream)};
+  if (!x_scales || !w_scale) return h3b_host::set_error(H3B_EINVAL, "%s: NULL scale", name);
+  int64_t o3[3];
+  int rc = check_conv_geometry(a, name, o3);
+  if (rc) return rc;
+  const int64_t B = x_dims[0], D = x_dims[1], H = x_dims[2], W = x_dims[3], C = x_dims[4];
+  if (C % kBK != 0) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: C=%lld must be a multiple of 128", name, (long long)C);
+  if (B * o3[0] > (int64_t(1) << 30)) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: too many frames", name);
+  const int64_t Do = o3[0], Ho = o3[1], Wo = o3[2];
+  const int64_t taps = static_cast<int64_t>(kd) * kh * kw;
+  MmaParams p{};
+  int bw = 1;
+  while (bw < Wo && bw < kBM) bw <<= 1;
+  const int bh = kBM / bw;
+  p.B = (int)B; p.Do = (int)Do; p.Ho = (int)Ho; p.Wo = (int)Wo;
+  p.kd = kd; p.kh = kh; p.kw = kw; p.sd = sd; p.sh = sh; p.sw = sw;
+  p.taps = (int)taps; p.C = (int)C; p.c_chunks = (int)(C / kBK);
+  p.bw = bw; p.bh = bh;
+  p.w_tiles = (int)((Wo + bw - 1) / bw);
+  p.h_tiles = (int)((Ho + bh - 1) / bh);
+  p.causal = (causal_zero_frames == 2 && kd == 3) ? 1 : 0;
+  p.N = (int)out_channels;
+  p.K = (int)(taps * C);
+  p.k_blocks = p.taps * p.c_chunks;
+  p.m_tiles = (int)(B * Do) * p.h_tiles * p.w_tiles;
+  p.m_groups = p.m_tiles;
+  p.n_tiles = (int)((out_channels + 127) / 128);
+  p.w_scale = w_scale; p.bias = static_cast<const __half*>(bias);
+  p.out = static_cast<__half*>(out);
+  p.osB = out_strides[0]; p.osD = out_strides[1]; p.osH = out_strides[2]; p.osW = out_strides[3];
+  p.residual = static_cast<const __half*>(residual);
+  CUtensorMap ma, mb;
+  uint64_t adims[5] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)D, (uint64_t)B};
+  uint64_t astr[4] = {(uint64_t)C, (uint64_t)(C * W), (uint64_t)(C * W * H), (uint64_t)(C * W * H * D)};
+  uint32_t abox[5] = {kBK, (uint32_t)(bw * sw), (uint32_t)(bh * sh), 1, 1};
+  uint32_t aes[5] = {1, (uint32_t)sw, (uint32_t)sh, 1, 1};
+  rc = h3b_host::encode_tiled(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, qx, adims, astr, abox, aes, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  uint64_t bdims[2] = {(uint64_t)(taps * C), (uint64_t)out_channels};
+  uint64_t bstr[1] = {(uint64_t)(taps * C)};
+  uint32_t bbox[2] = {kBK, 128};
+  uint32_t es[2] = {1, 1};
+  rc = h3b_host::encode_tiled(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, qw, bdims, bstr, bbox, es, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  constexpr int kStages = 6;
+  constexpr size_t smem = kStages * (kATileBytes + 128 * kBK) + 1024 + 256;
+  auto kern = conv_i8_token_kernel<kStages>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return h3b_host::set_error(H3B_ECUDA, "%s: smem attribute: %s", name, cudaGetErrorString(e));
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < h3b_host::num_sms() ? tiles : h3b_host::num_sms();
+  kern<<<grid, kThreads, smem, a.stream>>>(ma, mb, p, x_scales, (int)D, (int)H, (int)W);
+  return h3b_host::check_launch(name);
 }
 
 int h3b_conv3d_f16(const void* x, const int64_t* x_dims, const void* w, int64_t out_channels, int kd, int kh, int kw,

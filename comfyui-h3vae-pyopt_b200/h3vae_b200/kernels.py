@@ -87,17 +87,24 @@ def conv3d_i8(qx: torch.Tensor, x_scale: torch.Tensor, qweight: torch.Tensor, we
               residual: torch.Tensor | None = None, acc_out: torch.Tensor | None = None) -> torch.Tensor:
     """Valid INT8 conv3d of a padded NDHWC int8 activation (logical [B,C,D,H,W]).
 
-    With `residual` (fp16, same shape and strides as the output) the epilogue returns
-    fp16(fp16(conv) + residual), the residual block's skip add."""
+    x_scale is one fp32 value (per-tensor quantization, the reference's scheme) or fp32 [B,D,H,W]
+    scales per padded input position (per-token quantization).  With `residual` (fp16, same
+    shape and strides as the output) the epilogue returns fp16(fp16(conv) + residual), the
+    residual block's skip add."""
     dev = _require_cuda(qx, x_scale, qweight, weight_scale, bias, out, acc_out, residual)
     if qx.ndim != 5 or qx.dtype != I8 or not is_ndhwc(qx):
         raise ValueError("qx must be a channels_last_3d int8 [B,C,D,H,W] tensor")
     _require(qweight, I8, "qweight")
     _require(weight_scale, F32, "weight_scale")
     _require(bias, F16, "bias")
-    if x_scale.dtype != F32 or x_scale.numel() != 1:
-        raise ValueError("x_scale must be one fp32 value")
     b, c, d, h, w = qx.shape
+    per_token = x_scale.ndim == 4
+    if x_scale.dtype != F32 or (x_scale.numel() != 1 and not per_token):
+        raise ValueError("x_scale must be one fp32 value or per-position fp32 scales [B,D,H,W]")
+    if per_token and (tuple(x_scale.shape) != (b, d, h, w) or not x_scale.is_contiguous()):
+        raise ValueError("per-token x_scale must be contiguous fp32 [B,D,H,W] of the padded input")
+    if per_token and acc_out is not None:
+        raise ValueError("acc_out is not available with per-token scales (the int32 partials are per k-block)")
     kd, kh, kw = (int(k) for k in kernel)
     sd, sh, sw = (int(s) for s in stride)
     o = qweight.shape[0]
@@ -123,11 +130,18 @@ def conv3d_i8(qx: torch.Tensor, x_scale: torch.Tensor, qweight: torch.Tensor, we
     if timing is not None:
         ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         ev0.record()
-    _lib.check(lib.h3b_conv3d_i8(
-        qx.data_ptr(), _lib.i64_array((b, d, h, w, c)), qweight.data_ptr(), o, kd, kh, kw, sd, sh, sw,
-        x_scale.data_ptr(), weight_scale.data_ptr(), _ptr(bias), out.data_ptr(),
-        _lib.i64_array((out.stride(0), out.stride(2), out.stride(3), out.stride(4))), _ptr(residual),
-        _ptr(acc_out), int(causal_zero_frames), _stream(dev)))
+    if per_token:
+        _lib.check(lib.h3b_conv3d_i8_token(
+            qx.data_ptr(), _lib.i64_array((b, d, h, w, c)), qweight.data_ptr(), o, kd, kh, kw, sd, sh, sw,
+            x_scale.data_ptr(), weight_scale.data_ptr(), _ptr(bias), out.data_ptr(),
+            _lib.i64_array((out.stride(0), out.stride(2), out.stride(3), out.stride(4))), _ptr(residual),
+            int(causal_zero_frames), _stream(dev)))
+    else:
+        _lib.check(lib.h3b_conv3d_i8(
+            qx.data_ptr(), _lib.i64_array((b, d, h, w, c)), qweight.data_ptr(), o, kd, kh, kw, sd, sh, sw,
+            x_scale.data_ptr(), weight_scale.data_ptr(), _ptr(bias), out.data_ptr(),
+            _lib.i64_array((out.stride(0), out.stride(2), out.stride(3), out.stride(4))), _ptr(residual),
+            _ptr(acc_out), int(causal_zero_frames), _stream(dev)))
     _count(1)
     if timing is not None:
         ev1.record()
@@ -287,6 +301,21 @@ def norm_pad_quant(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps
                                       ws_bytes, _stream(dev)))
     _count(4)
     return q, scale
+
+
+def norm_pad_quant_token(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float,
+                         pre_bias: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """GroupNorm(32)->SiLU->reflect/causal pad->INT8 with one scale per padded position:
+    (q NDHWC [B,C,D+2,H+2,W+2], scales fp32 [B,D+2,H+2,W+2])."""
+    dev, x, lib, ws, ws_bytes = _norm_common(x, pre_bias, gamma, beta)
+    b, c, d, h, w = x.shape
+    q = torch.empty((b, c, d + 2, h + 2, w + 2), device=dev, dtype=I8, memory_format=torch.channels_last_3d)
+    scales = torch.empty((b, d + 2, h + 2, w + 2), device=dev, dtype=F32)
+    _lib.check(lib.h3b_norm_pad_quant_token(x.data_ptr(), b, c, d, h, w, _ptr(pre_bias), gamma.data_ptr(),
+                                            beta.data_ptr(), float(eps), q.data_ptr(), scales.data_ptr(),
+                                            ws.data_ptr(), ws_bytes, _stream(dev)))
+    _count(3)
+    return q, scales
 
 
 def norm_pad_f16(x: torch.Tensor, gamma: torch.Tensor, beta: torch.Tensor, eps: float,

@@ -126,6 +126,7 @@ class EncoderConfig:
     groups: int = 32
     eps: float = 1e-6
     int8_stages: tuple[int, ...] = (0, 1, 2, 3)   # "reference" scope is (0, 1): the 8 prefix convs
+    act_scale_mode: str = "tensor"                 # "tensor" (the reference's scheme) or "token"
 
     @property
     def spatial_ratio(self) -> int:
@@ -139,6 +140,9 @@ class EncoderConfig:
 class _ResBlock:
     def __init__(self, cin, cout, int8, gen, device, cfg: EncoderConfig):
         self.cin, self.cout, self.int8, self.eps = cin, cout, int8, cfg.eps
+        if cfg.act_scale_mode not in ("tensor", "token"):
+            raise ValueError("act_scale_mode must be 'tensor' or 'token'")
+        self.quant = K.norm_pad_quant_token if cfg.act_scale_mode == "token" else K.norm_pad_quant
         std1 = 1.0 / math.sqrt(cin * 27)
         std2 = 1.0 / math.sqrt(cout * 27)
         self.gn1_w = (1.0 + 0.1 * torch.randn(cin, generator=gen)).half().to(device)
@@ -171,9 +175,9 @@ class _ResBlock:
         [B,C,D+2,H+1,W+1] that the strided downsample conv consumes."""
         skip = self.shortcut(x)
         if self.int8:
-            q1, s1 = K.norm_pad_quant(x, self.gn1_w, self.gn1_b, self.eps)
+            q1, s1 = self.quant(x, self.gn1_w, self.gn1_b, self.eps)
             h = K.conv3d_i8(q1, s1, self.q1, self.s1, None, (3, 3, 3), causal_zero_frames=2)
-            q2, s2 = K.norm_pad_quant(h, self.gn2_w, self.gn2_b, self.eps, pre_bias=self.b1)
+            q2, s2 = self.quant(h, self.gn2_w, self.gn2_b, self.eps, pre_bias=self.b1)
             if pack_for_downsample:
                 h2 = K.conv3d_i8(q2, s2, self.q2, self.s2, None, (3, 3, 3), causal_zero_frames=2)
                 return K.residual_pack(h2, skip, self.b2)

@@ -71,6 +71,10 @@ class H3VAEPyOptLoader:
                                                        "SwiGLU FFN) on sm_100a."}),
                 "int8_encode": ("BOOLEAN", {"default": False,
                                             "tooltip": "tcgen05 INT8 causal conv3d encoder on sm_100a."}),
+                "act_scale_mode": (["tensor", "token"], {"default": "tensor",
+                                                          "tooltip": "INT8 encoder activation scales: one per tensor "
+                                                                     "(the reference's scheme) or one per "
+                                                                     "spatio-temporal position."}),
                 "model_code_dir": ("STRING", {"default": DEFAULT_MODEL_CODE_DIR}),
                 "weights_path": ("STRING", {"default": ""}),
             },
@@ -85,13 +89,14 @@ class H3VAEPyOptLoader:
     def load(self, vae_name, dtype, decoder_tile_size, tile_batch, compile_decoder, compile_encoder,
              encoder_staged_batch, cudnn_benchmark, warmup, warmup_frames, warmup_width, warmup_height,
              log_calls, model_code_dir=DEFAULT_MODEL_CODE_DIR, weights_path="", encoder_tile_size=0,
-             fast_linear=False, int8_decode=False, int8_encode=False, decode_fusions=False):
+             fast_linear=False, int8_decode=False, int8_encode=False, decode_fusions=False, act_scale_mode="tensor"):
         """ref: h3vae_nodes.py:134-191."""
         if bool(fast_linear) and bool(int8_decode):
             raise ValueError("int8_decode and fast_linear are mutually exclusive; choose one")
         key = (vae_name, weights_path, dtype, int(decoder_tile_size), int(encoder_tile_size), int(tile_batch),
                bool(compile_decoder), bool(compile_encoder), int(encoder_staged_batch), model_code_dir,
-               bool(log_calls), bool(fast_linear), bool(int8_decode), bool(int8_encode), bool(decode_fusions))
+               bool(log_calls), bool(fast_linear), bool(int8_decode), bool(int8_encode), bool(decode_fusions),
+               act_scale_mode)
         vae = _VAE_CACHE.get(key)
         if vae is None:
             weights = _resolve_weights(vae_name, weights_path)
@@ -103,7 +108,7 @@ class H3VAEPyOptLoader:
                 tile_batch=int(tile_batch), compile_decoder=bool(compile_decoder),
                 compile_encoder=bool(compile_encoder), encoder_staged_batch=int(encoder_staged_batch),
                 fast_linear=bool(fast_linear), int8_decode=bool(int8_decode), int8_encode=bool(int8_encode),
-                decode_fusions=bool(decode_fusions), log_calls=bool(log_calls))
+                decode_fusions=bool(decode_fusions), log_calls=bool(log_calls), act_scale_mode=act_scale_mode)
             vae = build_comfy_vae(runtime)
             _VAE_CACHE[key] = vae
             logger.info("[H3VAE-B200] loaded %s (%s, tile=%d, batch=%d)", weights or "synthetic weights", dtype,

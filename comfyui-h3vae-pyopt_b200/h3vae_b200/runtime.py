@@ -146,7 +146,7 @@ class H3VAEPyOptRuntime(torch.nn.Module):
                  fast_linear: bool = False, int8_decode: bool = False, int8_encode: bool = False,
                  decode_fusions: bool = False, *, encoder_config: EncoderConfig | None = None,
                  decoder_config: DecoderConfig | None = None, tile_overlap_min: int = 32, seed: int = 0,
-                 process_group=None):
+                 process_group=None, act_scale_mode: str = "tensor"):
         super().__init__()
         int8_decode, int8_encode = bool(int8_decode), bool(int8_encode)
         if fast_linear:
@@ -173,9 +173,11 @@ class H3VAEPyOptRuntime(torch.nn.Module):
             logger.info("[H3VAE-B200] compile_* options ignored: kernels are precompiled sm_100a code")
         if dtype != torch.float16:
             raise RuntimeError("the B200 path runs fp16 activations (dtype=fp16)")
+        if act_scale_mode not in ("tensor", "token"):
+            raise ValueError("act_scale_mode must be 'tensor' (per-tensor, the reference's scheme) or 'token'")
 
         self.dev = torch.device(device)
-        enc_cfg = encoder_config or EncoderConfig()
+        enc_cfg = EncoderConfig(**{**(encoder_config or EncoderConfig()).__dict__, "act_scale_mode": act_scale_mode})
         if not int8_encode:
             enc_cfg = EncoderConfig(**{**enc_cfg.__dict__, "int8_stages": ()})
         self.encoder = H3Encoder(enc_cfg, device=self.dev, seed=seed)

@@ -123,6 +123,30 @@ int h3b_conv_in_f16(const void* x, const int64_t* dims5, const int64_t* strides5
 int h3b_conv3d_rgb_f16(const void* x, const int64_t* x_dims, const void* w_packed, const void* bias, void* out,
                        h3b_stream_t stream);
 
+/* Per-token activation scales (one fp32 scale per spatio-temporal position;
+ * BASELINE config 1 / the north_star's per-token quantisation): INT8 conv whose
+ * input carries scales x_scales[B, D, H, W] for the padded positions.  Every
+ * 128-channel k-block's integer partial is dequantized with the scale of the
+ * input position it read: out = fp16(fma(sum_kb float(P_kb) * s_x, w_scale[o],
+ * bias[o])) (+ residual as in h3b_conv3d_i8).  C % 128 == 0.  The reference's
+ * encoder path is per-tensor (h3b_conv3d_i8); this is the per-token variant of
+ * ref: opt/encoder_int8.py:509-588 with the per-row scales of
+ * opt/int8_swiglu_fused.py:28-38 moved to the conv's input positions. */
+int h3b_conv3d_i8_token(const int8_t* qx, const int64_t* x_dims, const int8_t* qw, int64_t out_channels,
+                        int kd, int kh, int kw, int sd, int sh, int sw, const float* x_scales,
+                        const float* w_scale, const void* bias, void* out, const int64_t* out_strides,
+                        const void* residual, int causal_zero_frames, h3b_stream_t stream);
+
+/* Per-token INT8 producer: the GroupNorm/SiLU/pad of h3b_norm_pad_quant, then
+ * per padded position scale = absmax over its C channels * fp32(1/127) (0 -> 1)
+ * and q = clamp(half_away(z / scale), +-127).  C in {128, 256, 512}.
+ *   q       int8 NDHWC [B, D+2, H+2, W+2, C];  scales fp32 [B, D+2, H+2, W+2]
+ *   workspace >= h3b_norm_workspace_size(B, C, D, H, W)
+ * ref: opt/encoder_int8_norm.py:77-110 with per-position instead of per-tensor scales */
+int h3b_norm_pad_quant_token(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
+                             const void* pre_bias, const void* gamma, const void* beta, float eps, int8_t* q,
+                             float* scales, void* workspace, size_t workspace_bytes, h3b_stream_t stream);
+
 /* ---- (a2) per-tensor activation quantization ---------------------------- */
 
 /* scale = max|x| * fp32(1/127) (0 -> 1);  q = clamp(half_away(x / scale), +-127)

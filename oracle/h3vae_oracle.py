@@ -234,6 +234,57 @@ def norm_pad_quant(x, gamma, beta, eps, pre_bias=None):
 
 
 # ---------------------------------------------------------------------------
+# per-token (per spatio-temporal position) activation quantization and the conv that consumes it
+# (BASELINE config 1 / north_star "per-token activation quantisation"; the reference's encoder uses the
+# per-tensor scheme above, its decoder GEMMs the per-row CK scheme -- this mode applies the per-tensor
+# arithmetic to each position's C channels)
+# ---------------------------------------------------------------------------
+def quantize_activation_per_token(x: np.ndarray):
+    """fp16 values [B,C,D,H,W] -> (int8 [B,C,D,H,W], fp32 scales [B,D,H,W]): per position
+    scale = absmax_c * fp32(1/127) (0 -> 1), q = clamp(half_away(x / scale), +-127)."""
+    xf = np.asarray(x).astype(F32)
+    amax = np.abs(xf).max(axis=1)                                  # [B,D,H,W]
+    scale = (amax.astype(F32) * RECIP_127).astype(F32)
+    scale = np.where(scale > 0, scale, F32(1.0)).astype(F32)
+    s = xf / scale[:, None]
+    r = np.where(s >= 0, np.floor(s + F32(0.5)), -np.floor(-s + F32(0.5)))
+    return np.clip(r, -127, 127).astype(np.int8), scale
+
+
+def norm_pad_quant_per_token(x, gamma, beta, eps, pre_bias=None):
+    """INT8 producer with one scale per padded position: [B,C,D+2,H+2,W+2] int8 + [B,D+2,H+2,W+2]."""
+    y = pad_reflect_causal(norm_silu(x, gamma, beta, eps, pre_bias))
+    return quantize_activation_per_token(y)
+
+
+def conv3d_per_token(q: np.ndarray, x_scales: np.ndarray, qweight: np.ndarray, w_scale: np.ndarray, kernel,
+                     stride=(1, 1, 1), bias=None) -> np.ndarray:
+    """Valid conv of per-token-quantized input: every tap's integer partial sum is dequantized with
+    the scale of the input position it reads, out = fp16(sum_tap s_x * P_tap * s_w + bias), in
+    float64 (exact partials)."""
+    kd, kh, kw = kernel
+    sd, sh, sw = stride
+    c = q.shape[1]
+    w = unpack_weight(qweight, c, kernel).astype(np.float64)          # [O,C,kd,kh,kw]
+    qt = torch.from_numpy(np.asarray(q, np.float64))
+    st = torch.from_numpy(np.asarray(x_scales, np.float64))
+    b, _, d, h, wd = q.shape
+    do, ho, wo = (d - kd) // sd + 1, (h - kh) // sh + 1, (wd - kw) // sw + 1
+    out = torch.zeros((b, w.shape[0], do, ho, wo), dtype=torch.float64)
+    for a in range(kd):
+        for e in range(kh):
+            for f in range(kw):
+                xs = qt[:, :, a:a + sd * (do - 1) + 1:sd, e:e + sh * (ho - 1) + 1:sh, f:f + sw * (wo - 1) + 1:sw]
+                ss = st[:, a:a + sd * (do - 1) + 1:sd, e:e + sh * (ho - 1) + 1:sh, f:f + sw * (wo - 1) + 1:sw]
+                part = torch.einsum("bcdhw,oc->bodhw", xs, torch.from_numpy(w[:, :, a, e, f]))
+                out += part * ss[:, None]
+    v = out.numpy() * np.asarray(w_scale, np.float64).reshape(1, -1, 1, 1, 1)
+    if bias is not None:
+        v = v + f16(bias).astype(np.float64).reshape(1, -1, 1, 1, 1)
+    return v.astype(F16)
+
+
+# ---------------------------------------------------------------------------
 # (a6) residual + bias + downsample pad pack
 # ---------------------------------------------------------------------------
 def residual_pack(x, r, bias) -> np.ndarray:

@@ -24,7 +24,7 @@ def test_library_exports_every_header_symbol():
     build_lib.build()
     lib = _lib.load()
     symbols = _header_symbols()
-    assert len(symbols) == 28
+    assert len(symbols) == 30
     missing = [s for s in symbols if not hasattr(lib, s)]
     assert not missing, f"declared in the header but not exported: {missing}"
     assert set(symbols) == set(_lib._SIGNATURES), "ctypes signature table out of sync with the header"
@@ -101,6 +101,7 @@ def test_int8_encode_and_fusion_validation_policy():
     (dict(model_code_dir="/nonexistent"), NotImplementedError, "synthetic"),
     (dict(dtype=torch.float32), RuntimeError, "fp16"),
     (dict(int8_decode=True, device="cpu"), RuntimeError, "CUDA device"),
+    (dict(act_scale_mode="channel"), ValueError, "act_scale_mode"),
 ])
 def test_runtime_rejects_bad_options_before_building(kwargs, exc, match):
     from h3vae_b200.runtime import H3VAEPyOptRuntime
@@ -126,7 +127,8 @@ def test_node_inputs_and_mappings():
                         "warmup_height": 768, "log_calls": True}
     optional = {k: v[1].get("default") for k, v in types["optional"].items()}
     assert optional.keys() == {"encoder_tile_size", "fast_linear", "decode_fusions", "int8_decode", "int8_encode",
-                               "model_code_dir", "weights_path"}
+                               "model_code_dir", "weights_path", "act_scale_mode"}
+    assert optional["act_scale_mode"] == "tensor"
     assert node.RETURN_TYPES == ("VAE",) and node.FUNCTION == "load"
     with pytest.raises(ValueError, match="mutually exclusive"):
         node().load("use default", "fp16", 256, 2, True, True, 4, True, "none", 124, 1344, 768, True,
@@ -175,3 +177,27 @@ def test_kitchen_static_weight_matches_oracle():
     lin.weight.data[0, 0] = float("inf")
     with pytest.raises(ValueError, match="non-finite"):
         KitchenInt8Linear(lin)
+
+
+def test_oracle_per_token_quantization_known_answer():
+    """One scale per position: absmax over the channels * fp32(1/127); half-away rounding."""
+    from oracle import h3vae_oracle as O
+    x = np.zeros((1, 3, 1, 1, 2), np.float16)
+    x[0, :, 0, 0, 0] = [1.0, -2.0, 0.5]        # position 0: absmax 2
+    x[0, :, 0, 0, 1] = [0.0, 0.0, 0.0]         # position 1: all zero -> scale 1
+    q, s = O.quantize_activation_per_token(x)
+    s0 = np.float32(2.0) * np.float32(1.0 / 127.0)
+    assert s[0, 0, 0, 0] == s0 and s[0, 0, 0, 1] == 1.0
+    expect = np.where(x[0, :, 0, 0, 0] / s0 >= 0, np.floor(x[0, :, 0, 0, 0] / s0 + 0.5),
+                      -np.floor(-x[0, :, 0, 0, 0] / s0 + 0.5))
+    assert np.array_equal(q[0, :, 0, 0, 0], expect.astype(np.int8)) and q[0, 1, 0, 0, 0] == -127
+    assert not q[..., 1].any()
+    # per-token conv of a constant-scale input equals the per-tensor conv
+    rng = np.random.default_rng(1)
+    qa = rng.integers(-127, 128, (1, 4, 3, 4, 4), dtype=np.int8)
+    sc = np.full((1, 3, 4, 4), 0.02, np.float32)
+    qw = rng.integers(-127, 128, (2, 27 * 4), dtype=np.int8)
+    ws = np.array([0.001, 0.002], np.float32)
+    a = O.conv3d_per_token(qa, sc, qw, ws, (3, 3, 3)).astype(np.float32)
+    b = O.conv_epilogue(O.conv3d_int_acc(qa, qw, (3, 3, 3)), np.float32(0.02), ws, None).astype(np.float32)
+    assert np.allclose(a, b, atol=2e-3, rtol=2e-3)
