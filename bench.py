@@ -59,6 +59,8 @@ def parse_args():
                          "one config-4 decoder call per step (small enough for ncu captures)")
     ap.add_argument("--tile-batch", type=int, default=4,
                     help="tile workload: clips per encoder call and tiles per decoder call (4 = configs 3/4)")
+    ap.add_argument("--tile-part", choices=("both", "encoder", "decoder"), default="both",
+                    help="tile workload: run the encoder call, the decoder call or both per step")
     return ap.parse_args()
 
 
@@ -282,17 +284,22 @@ def run_tile(args):
     tb = args.tile_batch
     x = (torch.rand((tb, 3, 17, 256, 256), generator=g, device="cuda") * 2 - 1).half()
     z = torch.randn((tb, 16, 5, 32, 32), generator=g, device="cuda").half()
+    run_enc, run_dec = args.tile_part in ("both", "encoder"), args.tile_part in ("both", "decoder")
     for _ in range(args.warmup):
-        rt.encoder(x)
-        rt.decoder(z)
+        if run_enc:
+            rt.encoder(x)
+        if run_dec:
+            rt.decoder(z)
     torch.cuda.synchronize()
     enc, dec = [], []
     for _ in range(args.steps):
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record()
-        rt.encoder(x)
+        if run_enc:
+            rt.encoder(x)
         e1.record()
-        rt.decoder(z)
+        if run_dec:
+            rt.decoder(z)
         e2.record()
         torch.cuda.synchronize()
         enc.append(e0.elapsed_time(e1))
