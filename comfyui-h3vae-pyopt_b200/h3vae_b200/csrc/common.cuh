@@ -465,6 +465,27 @@ __device__ __forceinline__ void quant_byte_bits2(float z0, float z1, float scale
   t1 = fabsf(dv.y) > kNearTie ? __float_as_uint(quant_exact_bits(z1, scale)) : __float_as_uint(tv.y);
 }
 
+// quant_byte_bits for eight values: one near-tie test for all of them (the
+// largest |s - rne(s)|), the exact path for all eight in the rare case.
+__device__ __forceinline__ void quant_bytes8(const float (&z)[8], float scale, float inv_scale, uint32_t (&t)[8]) {
+  constexpr float kMagic = 12582912.0f;
+  const float2 m2 = make_float2(kMagic, kMagic);
+  float dmax = 0.0f;
+#pragma unroll
+  for (int j = 0; j < 8; j += 2) {
+    const float2 sv = f2x_mul(make_float2(z[j], z[j + 1]), make_float2(inv_scale, inv_scale));
+    const float2 tv = f2x_add(sv, m2);
+    const float2 dv = f2x_sub(sv, f2x_sub(tv, m2));   // s - rne(s)
+    t[j] = __float_as_uint(tv.x);
+    t[j + 1] = __float_as_uint(tv.y);
+    dmax = fmaxf(dmax, fmaxf(fabsf(dv.x), fabsf(dv.y)));
+  }
+  if (dmax > 0.5f - 1.0f / 8192.0f) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) t[j] = quant_byte_bits(z[j], scale, inv_scale);
+  }
+}
+
 // Low bytes of four words into one word (byte 0 from a).
 __device__ __forceinline__ uint32_t pack_low_bytes(uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   return __byte_perm(__byte_perm(a, b, 0x0040), __byte_perm(c, d, 0x0040), 0x5410);
@@ -517,59 +538,97 @@ __device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
 // embedding on the first R dims of one 64-wide head vector held in registers.
 // Products are rounded to fp16 individually before the fp32 sum, and the sum
 // is rounded to fp16 on store.  R is a compile-time constant so the vector
-// stays in registers; cos/sin rows and dst must be 16-byte aligned.
+// stays in registers; the token's cos / sin values arrive as R / 8 16-byte
+// vectors each (loaded early by the caller), dst must be 16-byte aligned.
 template <int R>
-__device__ __forceinline__ void qk_norm_rope_store_t(float (&x)[64], float eps, const __half* cs, const __half* sn,
-                                                     __half* dst) {
+__device__ __forceinline__ void qk_norm_rope_regs_t(__half2 (&xh)[32], float eps, const uint4 (&rc)[8],
+                                                    const uint4 (&rs)[8], __half* dst) {
+  // xh holds the 64 fp16-rounded linear outputs; every intermediate that the
+  // reference rounds to fp16 is exact in a half, so pairs stay packed.
   float ss = 0.0f;
 #pragma unroll
-  for (int d = 0; d < 64; ++d) ss = __fmaf_rn(x[d], x[d], ss);
+  for (int d = 0; d < 32; ++d) {
+    const float2 f = __half22float2(xh[d]);
+    ss = __fmaf_rn(f.x, f.x, ss);
+    ss = __fmaf_rn(f.y, f.y, ss);
+  }
   const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / 64.0f), eps));
 #pragma unroll
-  for (int d = 0; d < 64; ++d) x[d] = round_fp16(__fmul_rn(x[d], inv));
-  float c[R > 0 ? R : 1], sv[R > 0 ? R : 1];
-#pragma unroll
-  for (int q = 0; q < R / 8; ++q) {
-    const uint4 rc = reinterpret_cast<const uint4*>(cs)[q];
-    const uint4 rs = reinterpret_cast<const uint4*>(sn)[q];
-    const __half2* hc = reinterpret_cast<const __half2*>(&rc);
-    const __half2* hs = reinterpret_cast<const __half2*>(&rs);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const float2 fc = __half22float2(hc[j]);
-      const float2 fs = __half22float2(hs[j]);
-      c[q * 8 + 2 * j] = fc.x;
-      c[q * 8 + 2 * j + 1] = fc.y;
-      sv[q * 8 + 2 * j] = fs.x;
-      sv[q * 8 + 2 * j + 1] = fs.y;
-    }
+  for (int d = 0; d < 32; ++d) {
+    const float2 f = __half22float2(xh[d]);
+    xh[d] = __floats2half2_rn(__fmul_rn(f.x, inv), __fmul_rn(f.y, inv));
   }
-  __align__(16) __half outv[64];
+  auto xv = [&](int d) { return d & 1 ? __high2float(xh[d >> 1]) : __low2float(xh[d >> 1]); };
+  // element d of a row of 8 x uint4 tables, by register selects only (no
+  // address is taken, so the tables stay in registers)
+  auto tab = [&](const uint4 (&t)[8], int d) {
+    const uint4 v = t[d >> 3];
+    const int w = (d & 7) >> 1;
+    const uint32_t u = w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(d & 1 ? u >> 16 : u & 0xffffu)));
+  };
 #pragma unroll
-  for (int d = 0; d < 64; ++d) {
-    float o = x[d];
-    if (d < R) {
-      const float rot = (d < R / 2) ? -x[(d + R / 2) % 64] : x[(d + 64 - R / 2) % 64];
-      const float a = round_fp16(__fmul_rn(x[d], c[d % (R > 0 ? R : 1)]));
-      const float b = round_fp16(__fmul_rn(rot, sv[d % (R > 0 ? R : 1)]));
-      o = __fadd_rn(a, b);
+  for (int q = 0; q < 8; ++q) {
+    uint32_t ow[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float pr[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int d = q * 8 + 2 * e + k;
+        float val = xv(d);
+        if (d < R) {
+          const float rot = (d < R / 2) ? -xv((d + R / 2) % 64) : xv((d + 64 - R / 2) % 64);
+          const float a = round_fp16(__fmul_rn(val, tab(rc, d)));
+          const float b = round_fp16(__fmul_rn(rot, tab(rs, d)));
+          val = __fadd_rn(a, b);
+        }
+        pr[k] = val;
+      }
+      const __half2 h = __floats2half2_rn(pr[0], pr[1]);
+      ow[e] = (static_cast<uint32_t>(__half_as_ushort(__high2half(h))) << 16) | __half_as_ushort(__low2half(h));
     }
-    outv[d] = __float2half_rn(o);
+    reinterpret_cast<uint4*>(dst)[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
-#pragma unroll
-  for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(dst)[q] = reinterpret_cast<const uint4*>(outv)[q];
 }
 
-// Runtime-R dispatch over the supported rotary widths {0, 16, 32, 48, 64}.
-__device__ __forceinline__ void qk_norm_rope_store(float (&x)[64], float eps, int R, const __half* cs,
-                                                   const __half* sn, __half* dst) {
-  switch (R) {
-    case 48: qk_norm_rope_store_t<48>(x, eps, cs, sn, dst); break;
-    case 64: qk_norm_rope_store_t<64>(x, eps, cs, sn, dst); break;
-    case 32: qk_norm_rope_store_t<32>(x, eps, cs, sn, dst); break;
-    case 16: qk_norm_rope_store_t<16>(x, eps, cs, sn, dst); break;
-    default: qk_norm_rope_store_t<0>(x, eps, cs, sn, dst); break;
+// The R cos / sin values of one token as 16-byte vectors (R / 8 of each).
+__device__ __forceinline__ void load_rope_row(const __half* cs, const __half* sn, int R, uint4 (&rc)[8],
+                                              uint4 (&rs)[8]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    if (q < R / 8) {
+      rc[q] = __ldg(reinterpret_cast<const uint4*>(cs) + q);
+      rs[q] = __ldg(reinterpret_cast<const uint4*>(sn) + q);
+    } else {
+      rc[q] = make_uint4(0, 0, 0, 0);
+      rs[q] = make_uint4(0, 0, 0, 0);
+    }
   }
+}
+
+// Runtime-R dispatch with the token's tables already in registers.
+__device__ __forceinline__ void qk_norm_rope_regs(__half2 (&x)[32], float eps, int R, const uint4 (&rc)[8],
+                                                  const uint4 (&rs)[8], __half* dst) {
+  switch (R) {
+    case 48: qk_norm_rope_regs_t<48>(x, eps, rc, rs, dst); break;
+    case 64: qk_norm_rope_regs_t<64>(x, eps, rc, rs, dst); break;
+    case 32: qk_norm_rope_regs_t<32>(x, eps, rc, rs, dst); break;
+    case 16: qk_norm_rope_regs_t<16>(x, eps, rc, rs, dst); break;
+    default: qk_norm_rope_regs_t<0>(x, eps, rc, rs, dst); break;
+  }
+}
+
+// Runtime-R dispatch over the supported rotary widths {0, 16, 32, 48, 64},
+// loading the token's cos / sin rows first.
+__device__ __forceinline__ void qk_norm_rope_store(const float (&x)[64], float eps, int R, const __half* cs,
+                                                   const __half* sn, __half* dst) {
+  uint4 rc[8], rs[8];
+  load_rope_row(cs, sn, R, rc, rs);
+  __half2 xh[32];
+#pragma unroll
+  for (int d = 0; d < 32; ++d) xh[d] = __floats2half2_rn(x[2 * d], x[2 * d + 1]);
+  qk_norm_rope_regs(xh, eps, R, rc, rs, dst);
 }
 
 }  // namespace h3b

@@ -124,7 +124,7 @@ __device__ __forceinline__ Moments merge_moments(Moments a, Moments b) {
 // to `partials`.  The shift is taken before the loop so the loop body is
 // branch-free and its unrolled loads overlap.
 template <int GPV, bool MINMAX>
-__global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* __restrict__ x,
+__global__ void __launch_bounds__(kStatThreads, 3) gn_partial_kernel(const __half* __restrict__ x,
                                                                   const __half* __restrict__ pre_bias,
                                                                   NormShape s, float2* __restrict__ partials,
                                                                   unsigned int* __restrict__ cmin,
@@ -159,6 +159,7 @@ __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* 
   };
 
   const __half* base = x + (static_cast<int64_t>(bt) * HW + p0) * s.C + c0;
+  const __half2* pb2 = reinterpret_cast<const __half2*>(&pbv);
   float shift[GPV], s1[GPV], s2[GPV];
   float mn[MINMAX ? 8 : 1], mx[MINMAX ? 8 : 1];
   const int p_first = tid / vpp;
@@ -167,33 +168,62 @@ __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* 
     float f[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (n > 0) load_biased(base + static_cast<int64_t>(p_first) * s.C, f);
 #pragma unroll
-    for (int g = 0; g < GPV; ++g) {
-      shift[g] = f[g * kPerGroup];
-      s1[g] = 0.0f;
-      s2[g] = 0.0f;
-    }
+    for (int g = 0; g < GPV; ++g) shift[g] = f[g * kPerGroup];
   }
-  if constexpr (MINMAX) {
+  // Per channel pair (2e, 2e+1): shifted sum and sum of squares as packed
+  // fp32 pairs, min / max on the fp16 values themselves (exact).
+  float2 sp[4], s1p[4], s2p[4];
+  __half2 mn2[4], mx2[4];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      mn[j] = INFINITY;
-      mx[j] = -INFINITY;
-    }
+  for (int e = 0; e < 4; ++e) {
+    sp[e] = make_float2(shift[(2 * e) / kPerGroup], shift[(2 * e + 1) / kPerGroup]);
+    s1p[e] = make_float2(0.0f, 0.0f);
+    s2p[e] = make_float2(0.0f, 0.0f);
+    mn2[e] = __floats2half2_rn(INFINITY, INFINITY);
+    mx2[e] = __floats2half2_rn(-INFINITY, -INFINITY);
   }
-#pragma unroll 4
-  for (int p = p_first; p < valid_pos; p += pos_per_iter) {
-    float f[8];
-    load_biased(base + static_cast<int64_t>(p) * s.C, f);
+  auto accumulate = [&](const uint4& raw) {
+    const __half2* h = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int g = j / kPerGroup;
-      const float d = f[j] - shift[g];
-      s1[g] += d;
-      s2[g] = __fmaf_rn(d, d, s2[g]);
+    for (int e = 0; e < 4; ++e) {
+      const __half2 hv = pre_bias != nullptr ? __hadd2(h[e], pb2[e]) : h[e];
       if constexpr (MINMAX) {
-        mn[j] = fminf(mn[j], f[j]);
-        mx[j] = fmaxf(mx[j], f[j]);
+        mn2[e] = __hmin2(mn2[e], hv);
+        mx2[e] = __hmax2(mx2[e], hv);
       }
+      const float2 d = f2x_sub(__half22float2(hv), sp[e]);
+      s1p[e] = f2x_add(s1p[e], d);
+      s2p[e] = f2x_fma(d, d, s2p[e]);
+    }
+  };
+  // Eight 16-byte loads in flight per thread, then the tail one at a time.
+  const int64_t step = static_cast<int64_t>(pos_per_iter) * s.C;
+  const __half* src = base + static_cast<int64_t>(p_first) * s.C;
+  int left = n;
+  for (; left >= 8; left -= 8, src += 8 * step) {
+    uint4 raw[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) raw[k] = __ldg(reinterpret_cast<const uint4*>(src + k * step));
+#pragma unroll
+    for (int k = 0; k < 8; ++k) accumulate(raw[k]);
+  }
+  for (; left > 0; --left, src += step) accumulate(__ldg(reinterpret_cast<const uint4*>(src)));
+#pragma unroll
+  for (int g = 0; g < GPV; ++g) {
+    s1[g] = 0.0f;
+    s2[g] = 0.0f;
+  }
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    s1[(2 * e) / kPerGroup] += s1p[e].x;
+    s2[(2 * e) / kPerGroup] += s2p[e].x;
+    s1[(2 * e + 1) / kPerGroup] += s1p[e].y;
+    s2[(2 * e + 1) / kPerGroup] += s2p[e].y;
+    if constexpr (MINMAX) {
+      mn[2 * e] = __low2float(mn2[e]);
+      mn[2 * e + 1] = __high2float(mn2[e]);
+      mx[2 * e] = __low2float(mx2[e]);
+      mx[2 * e + 1] = __high2float(mx2[e]);
     }
   }
   const float fn = static_cast<float>(n * kPerGroup);
@@ -227,12 +257,29 @@ __global__ void __launch_bounds__(kStatThreads) gn_partial_kernel(const __half* 
   }
 }
 
+__device__ __forceinline__ float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // The producer's per-element value: GroupNorm affine -> fp16 -> SiLU -> fp16.
 // exp / divide are the fast SFU forms, the lowering of the reference kernels.
+// The affine is folded per channel into one fp32 fma (a = rstd * gamma,
+// b = beta - mean * a); SiLU uses the SFU's ex2 and rcp.  norm_pack_kernel
+// evaluates exactly this arithmetic, so absmax candidates taken from the
+// per-channel extremes match the values it writes.
 __device__ __forceinline__ float norm_silu_value(float v, float mean, float rstd, float gamma, float beta) {
-  float y = __fmul_rn(__fsub_rn(v, mean), rstd);
-  y = round_fp16(__fadd_rn(__fmul_rn(y, gamma), beta));
-  return round_fp16(__fdividef(y, __fadd_rn(1.0f, __expf(-y))));
+  const float a = __fmul_rn(rstd, gamma);
+  const float b = __fsub_rn(beta, __fmul_rn(mean, a));
+  const float y = round_fp16(__fmaf_rn(v, a, b));
+  const float d = __fadd_rn(ex2_ftz(__fmul_rn(y, -1.4426950408889634f)), 1.0f);
+  return round_fp16(__fmul_rn(y, rcp_ftz(d)));
 }
 
 // GroupNorm statistics, pass 2: one warp per group of one (b, frame).  With
@@ -296,7 +343,6 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
                                                                     const __half* __restrict__ beta,
                                                                     const float2* __restrict__ stats, NormShape s,
                                                                     float* amax, float* scale_out, void* out) {
-  constexpr int kPerGroup = kVec / GPV;
   const int vpp = s.C / kVec;
   const int vshift = __ffs(vpp) - 1;
   const int cg = s.C / kGroups;
@@ -329,79 +375,79 @@ __global__ void __launch_bounds__(kPackThreads, GPV == 8 ? 3 : 4) norm_pack_kern
   const float2* st = stats + (static_cast<int64_t>(b) * s.D + (frame_ok ? t : 0)) * kGroups;
   const int64_t out_row = static_cast<int64_t>(blockIdx.x) * row_vecs;
   // The block stride (256 vectors) is a multiple of C/8, so every thread keeps
-  // one channel vector: its affine constants (packed fp16) and the statistics
-  // of the GPV groups it touches are loaded once.
+  // one channel vector: its folded affine constants are computed once.
   const int v = threadIdx.x & (vpp - 1);
   const int c0 = v * kVec;
-  const uint4 gm = *reinterpret_cast<const uint4*>(gamma + c0);
-  const uint4 bt = *reinterpret_cast<const uint4*>(beta + c0);
   const uint4 pbv = pre_bias != nullptr ? *reinterpret_cast<const uint4*>(pre_bias + c0) : make_uint4(0, 0, 0, 0);
-  float mean[GPV], rstd[GPV];
+  // GroupNorm affine folded per channel: ((v - mean) * rstd) * gamma + beta
+  // = v * a + b with a = rstd * gamma, b = beta - mean * a (fp32; the fp16
+  // rounding that follows absorbs the reassociation).
+  float2 aff_a[4], aff_b[4];
+  {
+    const uint4 gm = *reinterpret_cast<const uint4*>(gamma + c0);
+    const uint4 bt = *reinterpret_cast<const uint4*>(beta + c0);
+    const __half2* g2 = reinterpret_cast<const __half2*>(&gm);
+    const __half2* b2 = reinterpret_cast<const __half2*>(&bt);
 #pragma unroll
-  for (int g = 0; g < GPV; ++g) {
-    const float2 mr = st[(c0 + g * kPerGroup) / cg];
-    mean[g] = mr.x;
-    rstd[g] = mr.y;
+    for (int e = 0; e < 4; ++e) {
+      const float2 mr0 = st[(c0 + 2 * e) / cg];
+      const float2 mr1 = st[(c0 + 2 * e + 1) / cg];
+      const float2 gf = __half22float2(g2[e]), bf = __half22float2(b2[e]);
+      aff_a[e] = make_float2(__fmul_rn(mr0.y, gf.x), __fmul_rn(mr1.y, gf.y));
+      aff_b[e] = make_float2(__fsub_rn(bf.x, __fmul_rn(mr0.x, aff_a[e].x)), __fsub_rn(bf.y, __fmul_rn(mr1.x, aff_a[e].y)));
+    }
   }
   auto column = [&](int i) {
     int w = (i >> vshift) - ((MODE == 0) ? 0 : 1);
     w = w < 0 ? -w : (w >= s.Wu ? 2 * s.Wu - 2 - w : w);
     return s.us == 2 ? (w >> 1) : w;
   };
-  // GroupNorm affine -> fp16 -> SiLU -> fp16 for 8 channels; every fp16
-  // rounding converts two values with one packed conversion.
   // GroupNorm affine -> fp16 -> SiLU -> fp16 for 8 channels, two at a time.
   // fp16(x + pre_bias) is one fp16 add (an fp16 sum rounded once equals the
   // fp32 sum rounded to fp16: fp32 carries more than 2*11 + 2 bits), the fp32
   // steps run as packed pairs, every fp16 rounding is one packed conversion.
+  // SiLU(y) = y / (1 + 2^(-y log2 e)) with the SFU's ex2 and rcp (the fast
+  // exp / divide of the reference kernels' lowering).
   auto values = [&](const uint4& raw, float (&z)[8]) {
     const __half2* xv = reinterpret_cast<const __half2*>(&raw);
-    const __half2* g2 = reinterpret_cast<const __half2*>(&gm);
-    const __half2* b2 = reinterpret_cast<const __half2*>(&bt);
     const __half2* p2 = reinterpret_cast<const __half2*>(&pbv);
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
       const float2 f = __half22float2(pre_bias != nullptr ? __hadd2(xv[e], p2[e]) : xv[e]);
-      const int g0 = (2 * e) / kPerGroup, g1 = (2 * e + 1) / kPerGroup;
-      const float2 n = f2x_mul(f2x_sub(f, make_float2(mean[g0], mean[g1])), make_float2(rstd[g0], rstd[g1]));
-      const float2 ya = f2x_add(f2x_mul(n, __half22float2(g2[e])), __half22float2(b2[e]));
+      const float2 ya = f2x_fma(f, aff_a[e], aff_b[e]);
       const float2 yr = __half22float2(__floats2half2_rn(ya.x, ya.y));
-      const float s0 = __fdividef(yr.x, __fadd_rn(1.0f, __expf(-yr.x)));
-      const float s1 = __fdividef(yr.y, __fadd_rn(1.0f, __expf(-yr.y)));
-      const float2 zz = __half22float2(__floats2half2_rn(s0, s1));
+      const float2 t = f2x_mul(yr, make_float2(-1.4426950408889634f, -1.4426950408889634f));
+      const float2 d = f2x_add(make_float2(ex2_ftz(t.x), ex2_ftz(t.y)), make_float2(1.0f, 1.0f));
+      const float2 sv = f2x_mul(yr, make_float2(rcp_ftz(d.x), rcp_ftz(d.y)));
+      const float2 zz = __half22float2(__floats2half2_rn(sv.x, sv.y));
       z[2 * e] = zz.x;
       z[2 * e + 1] = zz.y;
     }
   };
   float local_max = 0.0f;
-  // Two vectors per thread per step: both loads are issued before either is
-  // used, so each thread keeps two 16-byte reads in flight.
-  for (int i0 = threadIdx.x; i0 < row_vecs; i0 += 2 * kPackThreads) {
-    const int i1 = i0 + kPackThreads;
-    const bool has1 = i1 < row_vecs;
-    uint4 raw0 = make_uint4(0, 0, 0, 0), raw1 = make_uint4(0, 0, 0, 0);
-    if (frame_ok) {
-      raw0 = __ldg(reinterpret_cast<const uint4*>(xrow + static_cast<int64_t>(column(i0)) * s.C + c0));
-      if (has1) raw1 = __ldg(reinterpret_cast<const uint4*>(xrow + static_cast<int64_t>(column(i1)) * s.C + c0));
-    }
+  auto load = [&](int i) {
+    if (!frame_ok || i >= row_vecs) return make_uint4(0, 0, 0, 0);
+    return __ldg(reinterpret_cast<const uint4*>(xrow + static_cast<int64_t>(column(i)) * s.C + c0));
+  };
+  // Software pipeline: while one vector is computed, the next two of this
+  // thread are already in flight.
+  uint4 nxt0 = load(threadIdx.x), nxt1 = load(threadIdx.x + kPackThreads);
+  for (int i = threadIdx.x; i < row_vecs; i += kPackThreads) {
+    const uint4 raw = nxt0;
+    nxt0 = nxt1;
+    nxt1 = load(i + 2 * kPackThreads);
+    float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    if (frame_ok) values(raw, z);
+    if (MODE == 0) {
 #pragma unroll
-    for (int k = 0; k < 2; ++k) {
-      if (k == 1 && !has1) break;
-      const int i = k == 0 ? i0 : i1;
-      float z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (frame_ok) values(k == 0 ? raw0 : raw1, z);
-      if (MODE == 0) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) local_max = fmaxf(local_max, fabsf(z[j]));
-      } else if (MODE == 1) {
-        uint32_t tb[8];
-#pragma unroll
-        for (int j = 0; j < 8; j += 2) quant_byte_bits2(z[j], z[j + 1], scale, inv_scale, tb[j], tb[j + 1]);
-        reinterpret_cast<uint2*>(out)[out_row + i] =
-            make_uint2(pack_low_bytes(tb[0], tb[1], tb[2], tb[3]), pack_low_bytes(tb[4], tb[5], tb[6], tb[7]));
-      } else {
-        store_h8(reinterpret_cast<__half*>(out) + (out_row + i) * kVec, z);
-      }
+      for (int j = 0; j < 8; ++j) local_max = fmaxf(local_max, fabsf(z[j]));
+    } else if (MODE == 1) {
+      uint32_t tb[8];
+      quant_bytes8(z, scale, inv_scale, tb);
+      reinterpret_cast<uint2*>(out)[out_row + i] =
+          make_uint2(pack_low_bytes(tb[0], tb[1], tb[2], tb[3]), pack_low_bytes(tb[4], tb[5], tb[6], tb[7]));
+    } else {
+      store_h8(reinterpret_cast<__half*>(out) + (out_row + i) * kVec, z);
     }
   }
   if (MODE == 0) {

@@ -79,31 +79,63 @@ struct TmemLayout {
   static constexpr uint32_t cols = 2 * acc_stride;
 };
 
-// Output value of one accumulator column: INT8 dequantization, or the fp32
-// accumulator of an fp16 conv plus its bias.
-template <bool F16>
-__device__ __forceinline__ float epi_value(uint32_t acc_bits, float sx, const float* w_scale, const __half* bias,
-                                           int n);
-
 // ---------------------------------------------------------------------------
 // Epilogue helpers
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ float dequant(uint32_t acc_bits, float sx, float ws, const __half* bias, int n) {
-  float v = __fmul_rn(static_cast<float>(static_cast<int32_t>(acc_bits)), sx);
-  if (bias != nullptr) return __fmaf_rn(v, ws, __half2float(bias[n]));
-  return __fmul_rn(v, ws);
+// Column constants of the tile being finished: the epilogue warps stage the
+// per-column weight scale and bias (as fp32) of the current N tile in shared
+// memory, so the per-element dequantization reads them with broadcast 16-byte
+// shared loads instead of one global load per element and column.
+//
+// 32 output columns of one row: INT8 dequantization fp32(acc) * sx * ws + b
+// (the CK contract's fma(acc * sx, ws, b); b = 0 without a bias), or the fp32
+// accumulator of an fp16 conv plus its bias.
+template <bool F16>
+__device__ __forceinline__ void dequant_chunk(const uint32_t (&r)[32], float sx, const float* ws, const float* bs,
+                                              float (&v)[32]) {
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const float4 b4 = reinterpret_cast<const float4*>(bs)[q];
+    const float b[4] = {b4.x, b4.y, b4.z, b4.w};
+    if constexpr (F16) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v[4 * q + j] = __fadd_rn(__uint_as_float(r[4 * q + j]), b[j]);
+    } else {
+      const float4 w4 = reinterpret_cast<const float4*>(ws)[q];
+      const float w[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        v[4 * q + j] = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[4 * q + j])), sx), w[j], b[j]);
+    }
+  }
 }
 
-template <>
-__device__ __forceinline__ float epi_value<false>(uint32_t acc_bits, float sx, const float* w_scale,
-                                                  const __half* bias, int n) {
-  return dequant(acc_bits, sx, w_scale[n], bias, n);
+// Barrier over the epilogue warps (named barrier 1) that also ANDs a predicate
+// across them: every epilogue warp leaves the tile loop at the same tile when
+// any of their bounded waits gave up, and the shared-memory column constants
+// written before it are visible after it.
+__device__ __forceinline__ bool epi_barrier_and(bool pred, int threads) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, %2, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(threads)
+      : "memory");
+  return r != 0;
 }
 
-template <>
-__device__ __forceinline__ float epi_value<true>(uint32_t acc_bits, float, const float*, const __half* bias, int n) {
-  const float v = __uint_as_float(acc_bits);
-  return bias != nullptr ? __fadd_rn(v, __half2float(bias[n])) : v;
+__device__ __forceinline__ float ex2_approx_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcp_approx_ftz(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 __device__ __forceinline__ void store_row_chunk(__half* dst, const float (&v)[32], int valid_cols, bool vec_ok) {
@@ -178,6 +210,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  // [2 buffers][scale | bias][BN] fp32 column constants of the epilogue
+  float* cst = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 256);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -340,14 +374,59 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;          // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;   // tile row == TMEM lane
     const int half = (warp - 2) >> 2;   // 0 / 1: which alternate column chunks this warp owns
+    const int etid = threadIdx.x - 64;  // 0 .. 255 over the epilogue warps
+    // Column constants of a tile, one column per epilogue thread (BN <= 256):
+    // weight scale and bias of column etid of the tile's N range (SwiGLU: gate
+    // columns in [0, BN/2), the matching up columns in [BN/2, BN)).  They are
+    // loaded one tile ahead so the global-load latency hides behind a tile.
+    auto load_column = [&](int tile, float& w, float& bv) {
+      w = 1.0f;
+      bv = 0.0f;
+      if (tile >= num_tiles || etid >= BN) return;
+      const int n_tile = tile % p.n_tiles;
+      int col;
+      bool in;
+      if constexpr (EP == Epi::kSwiGLU) {
+        const int j = n_tile * (BN / 2) + (etid < BN / 2 ? etid : etid - BN / 2);
+        in = j < p.F;
+        col = etid < BN / 2 ? j : p.F + j;
+      } else {
+        col = n_tile * BN + etid;
+        in = col < p.N;
+      }
+      if (!in) return;
+      if constexpr (!F16) w = __ldg(p.w_scale + col);
+      if (p.bias != nullptr) bv = __half2float(p.bias[col]);
+    };
+    float next_w, next_b;
+    load_column(blockIdx.x, next_w, next_b);
     uint32_t local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int m_group = tile / p.n_tiles;
       const int n_tile = tile - m_group * p.n_tiles;
       const uint32_t acc = local & 1u;
       const uint32_t aph = (local >> 1) & 1u;
-      // tcgen05.ld is warp-collective: leave together if any lane's wait gave up
-      if (!__all_sync(0xffffffffu, mbar_wait(&tfull_bar[acc], aph, abort_flag))) break;
+      // Double-buffered constants: every epilogue warp has passed the barrier
+      // of tile local-1, hence finished tile local-2, before buffer local&1 is
+      // rewritten here.
+      float* cw = cst + (local & 1u) * (2 * BN);
+      float* cb = cw + BN;
+      if (etid < BN) {
+        cw[etid] = next_w;
+        cb[etid] = next_b;
+      }
+      load_column(tile + gridDim.x, next_w, next_b);
+      // Row data that does not come from the MMA is fetched before the wait.
+      float sx_pre = 0.0f;
+      int64_t m_pre = 0;
+      if constexpr (EP == Epi::kLinear || EP == Epi::kSwiGLU || EP == Epi::kQkvRope) {
+        m_pre = static_cast<int64_t>(m_group * MT) * kBM + row;
+        if (MT == 1 && m_pre < p.M) sx_pre = __ldg(p.a_scale + m_pre);
+      }
+      // tcgen05.ld is warp-collective and the barrier spans all epilogue warps:
+      // they leave together if any thread's bounded wait gave up.
+      const bool ready = __all_sync(0xffffffffu, mbar_wait(&tfull_bar[acc], aph, abort_flag));
+      if (!epi_barrier_and(ready, 32 * kEpiWarps)) break;
       tc_fence_after();
       const uint32_t t_acc = tmem_base + acc * kAccStride + (static_cast<uint32_t>(quad * 32) << 16);
 
@@ -357,7 +436,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t t_row = t_acc + i * BN;
           const int64_t m = static_cast<int64_t>(m_group * MT + i) * kBM + row;
           const bool valid = m < p.M;
-          const float sx = valid ? p.a_scale[m] : 0.0f;
+          const float sx = MT == 1 ? sx_pre : (valid ? p.a_scale[m] : 0.0f);
           const bool vec_ok = (p.ldo % 8) == 0;
 #pragma unroll 1
           for (int c = half; c < BN / 32; c += 2) {
@@ -368,11 +447,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int valid_cols = p.N - n0;
             if (valid && valid_cols > 0) {
               float v[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int n = min(n0 + j, p.N - 1);
-                v[j] = dequant(r[j], sx, p.w_scale[n], p.bias, n);
-              }
+              dequant_chunk<false>(r, sx, cw + c * 32, cb + c * 32, v);
               store_row_chunk(p.out + m * p.ldo + n0, v, valid_cols, vec_ok);
               if (p.acc_out != nullptr) store_acc_chunk(p.acc_out + m * p.N + n0, r, valid_cols);
             }
@@ -403,8 +478,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int valid_cols = p.N - n0;
             if (valid && valid_cols > 0) {
               float v[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) v[j] = epi_value<F16>(r[j], sx, p.w_scale, p.bias, min(n0 + j, p.N - 1));
+              dequant_chunk<F16>(r, sx, cw + c * 32, cb + c * 32, v);
               if (p.residual != nullptr) add_residual_chunk(v, p.residual + obase + n0, valid_cols, vec_ok);
               store_row_chunk(p.out + obase + n0, v, valid_cols, vec_ok);
               if (!F16 && p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
@@ -413,10 +487,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else if constexpr (EP == Epi::kSwiGLU) {
         const uint32_t t_row = t_acc;
-        const int64_t m = static_cast<int64_t>(m_group) * kBM + row;
+        const int64_t m = m_pre;
         const bool valid = m < p.M;
-        const float sx = valid ? p.a_scale[m] : 0.0f;
+        const float sx = sx_pre;
         const bool vec_ok = (p.F % 8) == 0;
+        constexpr float kNegLog2e = -1.4426950408889634f;
 #pragma unroll 1
         for (int c = half; c < BN / 64; c += 2) {
           uint32_t rg[32], ru[32];
@@ -426,56 +501,67 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int j0 = n_tile * (BN / 2) + c * 32;
           const int valid_cols = p.F - j0;
           if (valid && valid_cols > 0) {
-            float v[32];
+            float g[32], u[32];
+            dequant_chunk<false>(rg, sx, cw + c * 32, cb + c * 32, g);
+            dequant_chunk<false>(ru, sx, cw + BN / 2 + c * 32, cb + BN / 2 + c * 32, u);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int jj = min(j0 + j, p.F - 1);
-              const float g = round_fp16(dequant(rg[j], sx, p.w_scale[jj], p.bias, jj));
-              const float u = round_fp16(dequant(ru[j], sx, p.w_scale[p.F + jj], p.bias, p.F + jj));
-              const float sg = __fdividef(g, __fadd_rn(1.0f, expf(-g)));
-              v[j] = __fmul_rn(sg, u);
+            for (int j = 0; j < 32; j += 2) {
+              // gate and up rounded to fp16 (the linear's fp16 output), then
+              // silu(g) * u = g / (1 + 2^(-g log2 e)) * u in fp32
+              const float2 gg = __half22float2(__floats2half2_rn(g[j], g[j + 1]));
+              const float2 uu = __half22float2(__floats2half2_rn(u[j], u[j + 1]));
+              const float e0 = ex2_approx_ftz(__fmul_rn(gg.x, kNegLog2e));
+              const float e1 = ex2_approx_ftz(__fmul_rn(gg.y, kNegLog2e));
+              g[j] = __fmul_rn(__fmul_rn(gg.x, rcp_approx_ftz(__fadd_rn(1.0f, e0))), uu.x);
+              g[j + 1] = __fmul_rn(__fmul_rn(gg.y, rcp_approx_ftz(__fadd_rn(1.0f, e1))), uu.y);
             }
-            store_row_chunk(p.out + m * p.F + j0, v, valid_cols, vec_ok);
+            store_row_chunk(p.out + m * p.F + j0, g, valid_cols, vec_ok);
           }
         }
       } else if constexpr (EP == Epi::kQkvRope) {
-        // BN == 192: this tile is one head's [q | k | v] for 128 tokens.
+        // BN == 192: this tile is one head's [q | k | v] for 128 tokens.  Half
+        // 0 finishes q and v columns 0..31, half 1 k and v columns 32..63.
         const uint32_t t_row = t_acc;
-        const int64_t m = static_cast<int64_t>(m_group) * kBM + row;
+        const int64_t m = m_pre;
         const bool valid = m < p.M;
-        const float sx = valid ? p.a_scale[m] : 0.0f;
+        const float sx = sx_pre;
         const int h = n_tile;
         const int64_t bb = valid ? m / p.tokens : 0;
         const int64_t tt = valid ? m - bb * p.tokens : 0;
         const int64_t dst_off = ((bb * p.heads + h) * p.tokens + tt) * 64;
-#pragma unroll 1
-        for (int part = half; part < 3; part += 2) {
-          float x[64];
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            uint32_t r[32];
-            tmem_ld32(t_row + part * 64 + c * 32, r);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int n = h * 192 + part * 64 + c * 32 + j;
-              x[c * 32 + j] = valid ? round_fp16(dequant(r[j], sx, p.w_scale[n], p.bias, n)) : 0.0f;
-            }
-          }
+        uint4 rc[8], rs[8];
+        {
+          uint32_t r[32];
+          tmem_ld32(t_row + 128 + half * 32, r);
+          tmem_ld_wait();
           if (valid) {
-            if (part < 2) {
-              qk_norm_rope_store(x, p.eps, p.R, p.cos_t + m * p.R, p.sin_t + m * p.R,
-                                 (part == 0 ? p.q_out : p.k_out) + dst_off);
-            } else {
-              __align__(16) __half outv[64];
-#pragma unroll
-              for (int d = 0; d < 64; ++d) outv[d] = __float2half_rn(x[d]);
-#pragma unroll
-              for (int q = 0; q < 8; ++q)
-                reinterpret_cast<uint4*>(p.v_out + dst_off)[q] = reinterpret_cast<const uint4*>(outv)[q];
-            }
+            float v[32];
+            dequant_chunk<false>(r, sx, cw + 128 + half * 32, cb + 128 + half * 32, v);
+            store_row_chunk(p.v_out + dst_off + half * 32, v, 32, true);
           }
         }
+        // the token's rope tables, in flight while q (or k) is dequantized
+        if (valid) load_rope_row(p.cos_t + m * p.R, p.sin_t + m * p.R, p.R, rc, rs);
+        __half2 x[32];   // the 64 fp16-rounded q (or k) outputs of this row
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          uint32_t r[32];
+          tmem_ld32(t_row + half * 64 + c * 32, r);
+          tmem_ld_wait();
+          const float* ws = cw + half * 64 + c * 32;
+          const float* bs = cb + half * 64 + c * 32;
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float4 w4 = reinterpret_cast<const float4*>(ws)[q];
+            const float4 b4 = reinterpret_cast<const float4*>(bs)[q];
+            const auto dq = [&](int j, float w, float b) {
+              return __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[4 * q + j])), sx), w, b);
+            };
+            x[c * 16 + 2 * q] = __floats2half2_rn(dq(0, w4.x, b4.x), dq(1, w4.y, b4.y));
+            x[c * 16 + 2 * q + 1] = __floats2half2_rn(dq(2, w4.z, b4.z), dq(3, w4.w, b4.w));
+          }
+        }
+        if (valid) qk_norm_rope_regs(x, p.eps, p.R, rc, rs, (half == 0 ? p.q_out : p.k_out) + dst_off);
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -748,7 +834,7 @@ using namespace h3b;
 template <int BN, int STAGES, AMode AM, Epi EP, int MT = 1, bool F16 = false>
 int launch_mma(const CUtensorMap& ma, const CUtensorMap& mb, const MmaParams& p, cudaStream_t stream,
                const char* name) {
-  constexpr size_t smem = STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256;
+  constexpr size_t smem = STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256 + 2 * 2 * BN * sizeof(float);
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = mma_tc_kernel<BN, STAGES, AM, EP, MT, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
