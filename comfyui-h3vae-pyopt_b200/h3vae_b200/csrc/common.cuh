@@ -543,8 +543,12 @@ __device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
 template <int R>
 __device__ __forceinline__ void qk_norm_rope_regs_t(__half2 (&xh)[32], float eps, const uint4 (&rc)[8],
                                                     const uint4 (&rs)[8], __half* dst) {
-  // xh holds the 64 fp16-rounded linear outputs; every intermediate that the
-  // reference rounds to fp16 is exact in a half, so pairs stay packed.
+  static_assert(R % 4 == 0, "rotary width: pairs of halves on both sides of R/2");
+  // xh holds the 64 fp16-rounded linear outputs.  The normalized values are
+  // fp16 again, and the rotary products fp16(x * cos), fp16(rot * sin) are
+  // exactly fp16 multiplies (an 11 x 11-bit product is exact before its one
+  // rounding), so the rotation runs on packed halves; the sum of the two
+  // products is one fp16 add.
   float ss = 0.0f;
 #pragma unroll
   for (int d = 0; d < 32; ++d) {
@@ -558,35 +562,27 @@ __device__ __forceinline__ void qk_norm_rope_regs_t(__half2 (&xh)[32], float eps
     const float2 f = __half22float2(xh[d]);
     xh[d] = __floats2half2_rn(__fmul_rn(f.x, inv), __fmul_rn(f.y, inv));
   }
-  auto xv = [&](int d) { return d & 1 ? __high2float(xh[d >> 1]) : __low2float(xh[d >> 1]); };
-  // element d of a row of 8 x uint4 tables, by register selects only (no
+  // pair i of a row of 8 x uint4 tables, by register selects only (no
   // address is taken, so the tables stay in registers)
-  auto tab = [&](const uint4 (&t)[8], int d) {
-    const uint4 v = t[d >> 3];
-    const int w = (d & 7) >> 1;
+  auto tab = [&](const uint4 (&t)[8], int i) {
+    const uint4 v = t[i >> 2];
+    const int w = i & 3;
     const uint32_t u = w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w));
-    return __half2float(__ushort_as_half(static_cast<unsigned short>(d & 1 ? u >> 16 : u & 0xffffu)));
+    return *reinterpret_cast<const __half2*>(&u);
   };
+  auto bits = [](__half2 h) { return *reinterpret_cast<const uint32_t*>(&h); };
 #pragma unroll
   for (int q = 0; q < 8; ++q) {
     uint32_t ow[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) {
-      float pr[2];
-#pragma unroll
-      for (int k = 0; k < 2; ++k) {
-        const int d = q * 8 + 2 * e + k;
-        float val = xv(d);
-        if (d < R) {
-          const float rot = (d < R / 2) ? -xv((d + R / 2) % 64) : xv((d + 64 - R / 2) % 64);
-          const float a = round_fp16(__fmul_rn(val, tab(rc, d)));
-          const float b = round_fp16(__fmul_rn(rot, tab(rs, d)));
-          val = __fadd_rn(a, b);
-        }
-        pr[k] = val;
+      const int i = q * 4 + e;        // pair (2i, 2i+1)
+      __half2 o = xh[i];
+      if (2 * i < R) {
+        const __half2 rot = (2 * i < R / 2) ? __hneg2(xh[i + R / 4]) : xh[i - R / 4];
+        o = __hadd2(__hmul2(xh[i], tab(rc, i)), __hmul2(rot, tab(rs, i)));
       }
-      const __half2 h = __floats2half2_rn(pr[0], pr[1]);
-      ow[e] = (static_cast<uint32_t>(__half_as_ushort(__high2half(h))) << 16) | __half_as_ushort(__low2half(h));
+      ow[e] = bits(o);
     }
     reinterpret_cast<uint4*>(dst)[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }

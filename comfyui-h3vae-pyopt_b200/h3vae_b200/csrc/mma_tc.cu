@@ -101,11 +101,19 @@ __device__ __forceinline__ void dequant_chunk(const uint32_t (&r)[32], float sx,
 #pragma unroll
       for (int j = 0; j < 4; ++j) v[4 * q + j] = __fadd_rn(__uint_as_float(r[4 * q + j]), b[j]);
     } else {
+      // packed fp32 pairs: the same two roundings per element
       const float4 w4 = reinterpret_cast<const float4*>(ws)[q];
-      const float w[4] = {w4.x, w4.y, w4.z, w4.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j)
-        v[4 * q + j] = __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[4 * q + j])), sx), w[j], b[j]);
+      const float2 s2 = make_float2(sx, sx);
+      const float2 lo = f2x_fma(f2x_mul(make_float2(static_cast<float>(static_cast<int32_t>(r[4 * q])),
+                                                    static_cast<float>(static_cast<int32_t>(r[4 * q + 1]))), s2),
+                                make_float2(w4.x, w4.y), make_float2(b4.x, b4.y));
+      const float2 hi = f2x_fma(f2x_mul(make_float2(static_cast<float>(static_cast<int32_t>(r[4 * q + 2])),
+                                                    static_cast<float>(static_cast<int32_t>(r[4 * q + 3]))), s2),
+                                make_float2(w4.z, w4.w), make_float2(b4.z, b4.w));
+      v[4 * q] = lo.x;
+      v[4 * q + 1] = lo.y;
+      v[4 * q + 2] = hi.x;
+      v[4 * q + 3] = hi.y;
     }
   }
 }
@@ -554,11 +562,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < 8; ++q) {
             const float4 w4 = reinterpret_cast<const float4*>(ws)[q];
             const float4 b4 = reinterpret_cast<const float4*>(bs)[q];
-            const auto dq = [&](int j, float w, float b) {
-              return __fmaf_rn(__fmul_rn(static_cast<float>(static_cast<int32_t>(r[4 * q + j])), sx), w, b);
+            const float2 s2 = make_float2(sx, sx);
+            const auto dq = [&](int j, float w0, float w1, float b0, float b1) {
+              const float2 a = make_float2(static_cast<float>(static_cast<int32_t>(r[4 * q + j])),
+                                           static_cast<float>(static_cast<int32_t>(r[4 * q + j + 1])));
+              const float2 v2 = f2x_fma(f2x_mul(a, s2), make_float2(w0, w1), make_float2(b0, b1));
+              return __floats2half2_rn(v2.x, v2.y);
             };
-            x[c * 16 + 2 * q] = __floats2half2_rn(dq(0, w4.x, b4.x), dq(1, w4.y, b4.y));
-            x[c * 16 + 2 * q + 1] = __floats2half2_rn(dq(2, w4.z, b4.z), dq(3, w4.w, b4.w));
+            x[c * 16 + 2 * q] = dq(0, w4.x, w4.y, b4.x, b4.y);
+            x[c * 16 + 2 * q + 1] = dq(2, w4.z, w4.w, b4.z, b4.w);
           }
         }
         if (valid) qk_norm_rope_regs(x, p.eps, p.R, rc, rs, (half == 0 ? p.q_out : p.k_out) + dst_off);
