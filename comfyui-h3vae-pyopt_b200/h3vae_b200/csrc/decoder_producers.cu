@@ -251,6 +251,191 @@ __global__ void __launch_bounds__(kRowThreads) final_ln_kernel(const __half* __r
   }
 }
 
+// ---------------------------------------------------------------------------
+// Row kernels for K a multiple of 1024 (the decoder's hidden / FFN widths):
+// WPR = K / 1024 warps per row, 8 / WPR rows per 256-thread CTA; lane l of
+// warp w of a row owns the 16-byte vectors v * 32 * WPR + w * 32 + l (v < 4),
+// so every load / store instruction of a warp covers 512 contiguous bytes.
+// The row stays in registers as packed halves; the reductions are warp
+// shuffles (plus one shared-memory step when a row spans several warps).
+// ---------------------------------------------------------------------------
+constexpr int kFastV = 4;   // vectors per lane
+
+template <int WPR>
+__device__ __forceinline__ float row_reduce_max(float v, float* red) {
+  v = warp_max(v);
+  if constexpr (WPR > 1) {
+    const int warp = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    const int w0 = warp - warp % WPR;
+#pragma unroll
+    for (int i = 0; i < WPR; ++i) v = fmaxf(v, red[w0 + i]);
+  }
+  return v;
+}
+
+template <int WPR>
+__device__ __forceinline__ float row_reduce_sum(float v, float* red) {
+  v = warp_sum(v);
+  if constexpr (WPR > 1) {
+    const int warp = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) red[warp] = v;
+    __syncthreads();
+    const int w0 = warp - warp % WPR;
+    v = 0.0f;
+#pragma unroll
+    for (int i = 0; i < WPR; ++i) v = __fadd_rn(v, red[w0 + i]);
+  }
+  return v;
+}
+
+// CK row quantization of 8 fp16 values (quant_row_ck for each): the quotient
+// act / denom is formed with the correctly rounded reciprocal of denom, which
+// is within 2 ulp of the IEEE quotient; fp16 rounding of the two can differ
+// only within that distance of an fp16 midpoint (low 13 mantissa bits
+// 0x1000), so those vectors -- and inf / NaN -- take the exact path.  Clamping
+// the fp16 value to [-128, 127] before the round-to-nearest-even equals
+// clamping after it.  Returns the 8 bytes (byte j = element j).
+__device__ __forceinline__ uint2 quant8_ck(const uint4& raw, float denom, float inv, bool exact_row) {
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+  constexpr float kMagic = 12582912.0f;
+  uint32_t tb[8];
+  uint32_t near = exact_row ? 1u : 0u;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    const float2 v = f2x_mul(__half22float2(h[e]), make_float2(inv, inv));
+    const uint32_t b0 = __float_as_uint(v.x), b1 = __float_as_uint(v.y);
+    near |= (((b0 & 0x1fffu) - 0x0ffdu) < 7u) | (((b1 & 0x1fffu) - 0x0ffdu) < 7u) |
+            ((b0 & 0x7f800000u) == 0x7f800000u) | ((b1 & 0x7f800000u) == 0x7f800000u);
+    __half2 hv = __floats2half2_rn(v.x, v.y);
+    hv = __hmax2(__hmin2(hv, __float2half2_rn(127.0f)), __float2half2_rn(-128.0f));
+    const float2 t = f2x_add(__half22float2(hv), make_float2(kMagic, kMagic));
+    tb[2 * e] = __float_as_uint(t.x);
+    tb[2 * e + 1] = __float_as_uint(t.y);
+  }
+  if (near) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = __half22float2(h[e]);
+      tb[2 * e] = static_cast<uint8_t>(quant_row_ck(f.x, denom));
+      tb[2 * e + 1] = static_cast<uint8_t>(quant_row_ck(f.y, denom));
+    }
+  }
+  return make_uint2(pack_low_bytes(tb[0], tb[1], tb[2], tb[3]), pack_low_bytes(tb[4], tb[5], tb[6], tb[7]));
+}
+
+// Row scale from the row's absmax and the quantized bytes of this lane's
+// vectors, written to qrow (vector index vec(v)).
+template <int WPR>
+__device__ __forceinline__ void row_quant_fast_store(const uint4 (&act)[kFastV], float amax_local, bool valid,
+                                                     int64_t row, int wr, int lane, int8_t* __restrict__ q,
+                                                     float* __restrict__ s, int K, float* red) {
+  const float amax = row_reduce_max<WPR>(amax_local, red);
+  const float scale = row_scale_ck(amax);
+  const float denom = round_fp16(scale);
+  const float inv = __frcp_rn(denom);
+  const bool exact_row = !(denom >= 6.103515625e-05f && denom <= 65504.0f);   // fp16 normal range
+  if (!valid) return;
+  uint2* qrow = reinterpret_cast<uint2*>(q + row * K);
+#pragma unroll
+  for (int v = 0; v < kFastV; ++v) qrow[(v * WPR + wr) * 32 + lane] = quant8_ck(act[v], denom, inv, exact_row);
+  if (wr == 0 && lane == 0) s[row] = scale;
+}
+
+__device__ __forceinline__ float absmax_h8(const uint4& raw, float m) {
+  const __half2* h = reinterpret_cast<const __half2*>(&raw);
+  const __half2 a = __hmax2(__hmax2(__habs2(h[0]), __habs2(h[1])), __hmax2(__habs2(h[2]), __habs2(h[3])));
+  return fmaxf(m, fmaxf(__low2float(a), __high2float(a)));
+}
+
+template <int WPR>
+__global__ void __launch_bounds__(256) row_quant_fast_kernel(const __half* __restrict__ x, int64_t M, int K,
+                                                             int64_t ldx, int8_t* __restrict__ q,
+                                                             float* __restrict__ s) {
+  __shared__ float red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wr = warp % WPR;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (8 / WPR) + warp / WPR;
+  const bool valid = row < M;
+  uint4 act[kFastV];
+  float amax = 0.0f;
+#pragma unroll
+  for (int v = 0; v < kFastV; ++v) {
+    act[v] = valid ? __ldg(reinterpret_cast<const uint4*>(x + row * ldx) + (v * WPR + wr) * 32 + lane)
+                   : make_uint4(0, 0, 0, 0);
+    amax = absmax_h8(act[v], amax);
+  }
+  row_quant_fast_store<WPR>(act, amax, valid, row, wr, lane, q, s, K, red);
+}
+
+// residual_rms_quant_kernel for K a multiple of 1024 (same arithmetic).
+template <int WPR>
+__global__ void __launch_bounds__(256) residual_rms_quant_fast_kernel(
+    const __half* x, const __half* __restrict__ a, const __half* __restrict__ g, const __half* __restrict__ w,
+    int64_t M, int K, float eps, int round_stats, __half* h, int8_t* __restrict__ q, float* __restrict__ s,
+    __half* __restrict__ norm_out) {
+  __shared__ float red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wr = warp % WPR;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (8 / WPR) + warp / WPR;
+  const bool valid = row < M;
+  uint4 hv[kFastV];
+  float ss = 0.0f;
+#pragma unroll
+  for (int v = 0; v < kFastV; ++v) {
+    const int vec = (v * WPR + wr) * 32 + lane;
+    uint4 xr = make_uint4(0, 0, 0, 0), ar = make_uint4(0, 0, 0, 0);
+    if (valid) {
+      xr = reinterpret_cast<const uint4*>(x + row * K)[vec];
+      ar = __ldg(reinterpret_cast<const uint4*>(a + row * K) + vec);
+    }
+    const uint4 gr = __ldg(reinterpret_cast<const uint4*>(g) + vec);
+    const __half2* xh = reinterpret_cast<const __half2*>(&xr);
+    const __half2* ah = reinterpret_cast<const __half2*>(&ar);
+    const __half2* gh = reinterpret_cast<const __half2*>(&gr);
+    uint32_t ow[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 raw = f2x_fma(__half22float2(ah[e]), __half22float2(gh[e]), __half22float2(xh[e]));
+      const __half2 hh = __floats2half2_rn(raw.x, raw.y);
+      const float2 st = round_stats ? __half22float2(hh) : raw;
+      ss = __fadd_rn(ss, __fmul_rn(st.x, st.x));
+      ss = __fadd_rn(ss, __fmul_rn(st.y, st.y));
+      ow[e] = *reinterpret_cast<const uint32_t*>(&hh);
+    }
+    hv[v] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+  }
+  // Each lane read its own x vectors above, so an in-place h (aliasing x) is safe.
+  if (valid && h != nullptr) {
+#pragma unroll
+    for (int v = 0; v < kFastV; ++v) reinterpret_cast<uint4*>(h + row * K)[(v * WPR + wr) * 32 + lane] = hv[v];
+  }
+  ss = row_reduce_sum<WPR>(ss, red);
+  const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / static_cast<float>(K)), eps));
+  float amax = 0.0f;
+#pragma unroll
+  for (int v = 0; v < kFastV; ++v) {
+    const int vec = (v * WPR + wr) * 32 + lane;
+    const uint4 wr4 = __ldg(reinterpret_cast<const uint4*>(w) + vec);
+    const __half2* hh = reinterpret_cast<const __half2*>(&hv[v]);
+    const __half2* wh = reinterpret_cast<const __half2*>(&wr4);
+    uint32_t ow[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = f2x_mul(f2x_mul(__half22float2(hh[e]), make_float2(inv, inv)), __half22float2(wh[e]));
+      const __half2 r = __floats2half2_rn(t.x, t.y);
+      ow[e] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+    hv[v] = make_uint4(ow[0], ow[1], ow[2], ow[3]);   // now the normalized act
+    amax = absmax_h8(hv[v], amax);
+    if (valid && norm_out != nullptr) reinterpret_cast<uint4*>(norm_out + row * K)[vec] = hv[v];
+  }
+  row_quant_fast_store<WPR>(hv, amax, valid, row, wr, lane, q, s, K, red);
+}
+
 // Standalone QK RMSNorm + rotary: one thread per (token, head).
 __global__ void qk_rope_kernel(const __half* __restrict__ qkv, const __half* __restrict__ cos_t,
                                const __half* __restrict__ sin_t, int64_t rows, int heads, int R, float eps,
@@ -287,6 +472,13 @@ int row_check(int64_t M, int64_t K, const char* name, int max_k = 32768) {
                                (long long)K, max_k);
   if (M > 0x7fffffffLL) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: too many rows", name);
   return H3B_OK;
+}
+
+// Widths served by the warp-per-row kernels: 1024, 2048, 4096 or 8192.
+bool fast_row_width(int64_t K) { return K == 1024 || K == 2048 || K == 4096 || K == 8192; }
+unsigned fast_row_grid(int64_t M, int wpr) {
+  const int64_t rows_per_cta = 8 / wpr;
+  return static_cast<unsigned>((M + rows_per_cta - 1) / rows_per_cta);
 }
 
 // Dispatch on the number of 8-wide vectors each thread keeps in registers.
@@ -357,6 +549,17 @@ int h3b_row_quant(const void* x, int64_t M, int64_t K, int64_t ldx, int8_t* q, f
   int rc = row_check(M, K, name);
   if (rc) return rc;
   if (ldx < K || ldx % 8 || !al16(x)) return h3b_host::set_error(H3B_EINVAL, "%s: x must be 16-byte aligned rows", name);
+  if (fast_row_width(K) && al16(q)) {
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const __half* xh = static_cast<const __half*>(x);
+    switch (K / 1024) {
+      case 1: row_quant_fast_kernel<1><<<fast_row_grid(M, 1), 256, 0, st>>>(xh, M, (int)K, ldx, q, s); break;
+      case 2: row_quant_fast_kernel<2><<<fast_row_grid(M, 2), 256, 0, st>>>(xh, M, (int)K, ldx, q, s); break;
+      case 4: row_quant_fast_kernel<4><<<fast_row_grid(M, 4), 256, 0, st>>>(xh, M, (int)K, ldx, q, s); break;
+      default: row_quant_fast_kernel<8><<<fast_row_grid(M, 8), 256, 0, st>>>(xh, M, (int)K, ldx, q, s); break;
+    }
+    return h3b_host::check_launch(name);
+  }
   return dispatch_maxv<LaunchRowQuant>(K, static_cast<const __half*>(x), M, (int)K, ldx, q, s,
                                        reinterpret_cast<cudaStream_t>(stream));
 }
@@ -381,6 +584,23 @@ int h3b_residual_rms_quant(const void* x, const void* a, const void* g, const vo
     if (!al16(p)) return h3b_host::set_error(H3B_EINVAL, "%s: tensors must be 16-byte aligned", name);
   if ((h && !al16(h)) || (norm_out && !al16(norm_out)))
     return h3b_host::set_error(H3B_EINVAL, "%s: outputs must be 16-byte aligned", name);
+  if (fast_row_width(K) && al16(q)) {
+    const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    const __half *xh = static_cast<const __half*>(x), *ah = static_cast<const __half*>(a);
+    const __half *gh = static_cast<const __half*>(g), *wh = static_cast<const __half*>(w);
+    __half *hh = static_cast<__half*>(h), *nh = static_cast<__half*>(norm_out);
+    switch (K / 1024) {
+      case 1: residual_rms_quant_fast_kernel<1><<<fast_row_grid(M, 1), 256, 0, st>>>(xh, ah, gh, wh, M, (int)K, eps,
+                                                                                      round_stats, hh, q, s, nh); break;
+      case 2: residual_rms_quant_fast_kernel<2><<<fast_row_grid(M, 2), 256, 0, st>>>(xh, ah, gh, wh, M, (int)K, eps,
+                                                                                      round_stats, hh, q, s, nh); break;
+      case 4: residual_rms_quant_fast_kernel<4><<<fast_row_grid(M, 4), 256, 0, st>>>(xh, ah, gh, wh, M, (int)K, eps,
+                                                                                      round_stats, hh, q, s, nh); break;
+      default: residual_rms_quant_fast_kernel<8><<<fast_row_grid(M, 8), 256, 0, st>>>(xh, ah, gh, wh, M, (int)K, eps,
+                                                                                       round_stats, hh, q, s, nh); break;
+    }
+    return h3b_host::check_launch(name);
+  }
   return dispatch_maxv<LaunchResidualRms>(K, static_cast<const __half*>(x), static_cast<const __half*>(a),
                                           static_cast<const __half*>(g), static_cast<const __half*>(w), M, (int)K, eps,
                                           round_stats, static_cast<__half*>(h), q, s, static_cast<__half*>(norm_out),

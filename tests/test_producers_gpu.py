@@ -140,12 +140,16 @@ def test_finalize_pixels(cuda_lib):
         assert np.array_equal(np.nan_to_num(got), np.nan_to_num(ref))
 
 
-@pytest.mark.parametrize("m,k", [(1, 2048), (17, 1024), (129, 2048), (7188, 2048), (64, 8192), (3, 16384)])
+@pytest.mark.parametrize("m,k", [(1, 2048), (17, 1024), (129, 2048), (7188, 2048), (64, 8192), (3, 16384),
+                                 (300, 4096), (9, 1000)])
 def test_row_quant_and_swiglu_quant(cuda_lib, m, k):
     from h3vae_b200 import kernels as K
     g = torch.Generator().manual_seed(m + k)
     x = torch.randn(m, k, generator=g).half()
     x[0, :] = 0
+    if m > 2:
+        x[1, :] *= 1e-5   # row scale below the fp16 normal range: every element takes the exact path
+        x[2, :] = torch.round(x[2, :] * 8) / 8   # many quotients on fp16 midpoints
     q, s = K.row_quant(x.cuda())
     rq, rs = O.row_quant_ck(x.float().numpy())
     assert np.array_equal(s.cpu().numpy(), rs)
