@@ -52,8 +52,14 @@ CASES = [
     (7, 19, (2, 7, 5, 9, 11), (3, 3, 3), (1, 2, 2)),
     (128, 128, (1, 128, 5, 17, 33), (3, 3, 3), (1, 2, 2)),
     (256, 256, (1, 256, 11, 33, 35), (3, 3, 3), (2, 2, 2)),
-    # two M tiles per CTA (O <= 128 with enough tiles to fill the SMs), an odd tile count
+    # two M tiles per CTA (O <= 128 with enough tiles to fill the SMs), an odd tile count; with
+    # 128-column rows these take the kw-strip kernel (three kw taps from one input strip)
     (128, 128, (1, 128, 5, 131, 130), (3, 3, 3), (1, 1, 1)),
+    # kw-strip kernel: two channel chunks, an output-channel tail, two M tiles per output row
+    (256, 96, (1, 256, 5, 62, 258), (3, 3, 3), (1, 1, 1)),
+    # kw-strip kernel with 256 output columns (one M tile per CTA), and with a tail of 200
+    (128, 256, (1, 128, 4, 76, 130), (3, 3, 3), (1, 1, 1)),
+    (256, 200, (1, 256, 4, 76, 130), (3, 3, 3), (1, 1, 1)),
 ]
 
 
