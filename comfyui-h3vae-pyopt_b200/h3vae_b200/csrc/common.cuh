@@ -135,6 +135,13 @@ __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint4 v) {
                : "memory");
 }
 
+__device__ __forceinline__ uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
 __device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done = 0;
   asm volatile(
@@ -542,7 +549,7 @@ __device__ __forceinline__ void atomic_max_nonneg(float* addr, float v) {
 // vectors each (loaded early by the caller), dst must be 16-byte aligned.
 template <int R>
 __device__ __forceinline__ void qk_norm_rope_regs_t(__half2 (&xh)[32], float eps, const uint4 (&rc)[8],
-                                                    const uint4 (&rs)[8], __half* dst) {
+                                                    const uint4 (&rs)[8], uint4 (&out)[8]) {
   static_assert(R % 4 == 0, "rotary width: pairs of halves on both sides of R/2");
   // xh holds the 64 fp16-rounded linear outputs.  The normalized values are
   // fp16 again, and the rotary products fp16(x * cos), fp16(rot * sin) are
@@ -584,7 +591,7 @@ __device__ __forceinline__ void qk_norm_rope_regs_t(__half2 (&xh)[32], float eps
       }
       ow[e] = bits(o);
     }
-    reinterpret_cast<uint4*>(dst)[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    out[q] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
   }
 }
 
@@ -603,15 +610,16 @@ __device__ __forceinline__ void load_rope_row(const __half* cs, const __half* sn
   }
 }
 
-// Runtime-R dispatch with the token's tables already in registers.
+// Runtime-R dispatch with the token's tables already in registers; the
+// normalized, rotated 64-wide row comes back as eight 16-byte vectors.
 __device__ __forceinline__ void qk_norm_rope_regs(__half2 (&x)[32], float eps, int R, const uint4 (&rc)[8],
-                                                  const uint4 (&rs)[8], __half* dst) {
+                                                  const uint4 (&rs)[8], uint4 (&out)[8]) {
   switch (R) {
-    case 48: qk_norm_rope_regs_t<48>(x, eps, rc, rs, dst); break;
-    case 64: qk_norm_rope_regs_t<64>(x, eps, rc, rs, dst); break;
-    case 32: qk_norm_rope_regs_t<32>(x, eps, rc, rs, dst); break;
-    case 16: qk_norm_rope_regs_t<16>(x, eps, rc, rs, dst); break;
-    default: qk_norm_rope_regs_t<0>(x, eps, rc, rs, dst); break;
+    case 48: qk_norm_rope_regs_t<48>(x, eps, rc, rs, out); break;
+    case 64: qk_norm_rope_regs_t<64>(x, eps, rc, rs, out); break;
+    case 32: qk_norm_rope_regs_t<32>(x, eps, rc, rs, out); break;
+    case 16: qk_norm_rope_regs_t<16>(x, eps, rc, rs, out); break;
+    default: qk_norm_rope_regs_t<0>(x, eps, rc, rs, out); break;
   }
 }
 
@@ -624,7 +632,10 @@ __device__ __forceinline__ void qk_norm_rope_store(const float (&x)[64], float e
   __half2 xh[32];
 #pragma unroll
   for (int d = 0; d < 32; ++d) xh[d] = __floats2half2_rn(x[2 * d], x[2 * d + 1]);
-  qk_norm_rope_regs(xh, eps, R, rc, rs, dst);
+  uint4 o[8];
+  qk_norm_rope_regs(xh, eps, R, rc, rs, o);
+#pragma unroll
+  for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(dst)[q] = o[q];
 }
 
 }  // namespace h3b

@@ -168,6 +168,40 @@ __device__ __forceinline__ void store_acc_chunk(int32_t* dst, const uint32_t (&r
     if (j < valid_cols) dst[j] = static_cast<int32_t>(r[j]);
 }
 
+// 32 fp32 values as fp16 in four 16-byte vectors.
+__device__ __forceinline__ void pack_row32(const float (&v)[32], uint4 (&o)[4]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    __align__(16) __half2 h[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) h[j] = __floats2half2_rn(v[k * 8 + 2 * j], v[k * 8 + 2 * j + 1]);
+    o[k] = *reinterpret_cast<const uint4*>(h);
+  }
+}
+
+// Stores a 32-row x 32-column fp16 chunk (row r = lane r's four vectors) to
+// dst0 + r * row_stride through this warp's 2 KB shared staging buffer: the
+// lanes write their rows (16-byte chunks XOR-swizzled by row, so both the
+// shared stores and loads are bank-conflict free), then each global store
+// instruction writes 8 rows x 64 contiguous bytes instead of 32 rows x 16 B.
+// Warp-collective; rows >= valid_rows are not written.  dst0 and row_stride
+// must keep every row 16-byte aligned.
+__device__ __forceinline__ void store_chunk32_staged(uint32_t stage, const uint4 (&row)[4], __half* dst0,
+                                                     int64_t row_stride, int valid_rows) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) st_shared_v4(stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4), row[k]);
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (lane >> 2) + 8 * i;
+    const int k = lane & 3;
+    const uint4 val = ld_shared_v4(stage + r * 64 + ((k ^ ((r >> 1) & 3)) << 4));
+    if (r < valid_rows) *reinterpret_cast<uint4*>(dst0 + r * row_stride + k * 8) = val;
+  }
+  __syncwarp();
+}
+
 // v = fp16(fp16(v) + residual): the residual block's `x + h` on fp16 tensors.
 __device__ __forceinline__ void add_residual_chunk(float (&v)[32], const __half* res, int valid_cols, bool vec_ok) {
   if (valid_cols >= 32 && vec_ok) {
@@ -218,8 +252,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // [2 buffers][scale | bias][BN] fp32 column constants of the epilogue
+  // [2 buffers][scale | bias][BN] fp32 column constants of the epilogue, then
+  // (GEMM epilogues) one 2 KB store-staging buffer per epilogue warp
   float* cst = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 256);
+  const uint32_t stage_base = smem_u32(cst + 2 * 2 * BN);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -383,6 +419,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quad * 32 + lane;   // tile row == TMEM lane
     const int half = (warp - 2) >> 2;   // 0 / 1: which alternate column chunks this warp owns
     const int etid = threadIdx.x - 64;  // 0 .. 255 over the epilogue warps
+    const uint32_t stage = stage_base + (warp - 2) * 2048;
     // Column constants of a tile, one column per epilogue thread (BN <= 256):
     // weight scale and bias of column etid of the tile's N range (SwiGLU: gate
     // columns in [0, BN/2), the matching up columns in [BN/2, BN)).  They are
@@ -445,7 +482,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t m = static_cast<int64_t>(m_group * MT + i) * kBM + row;
           const bool valid = m < p.M;
           const float sx = MT == 1 ? sx_pre : (valid ? p.a_scale[m] : 0.0f);
-          const bool vec_ok = (p.ldo % 8) == 0;
+          const bool vec_ok = (p.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
+          const int64_t m_warp = m - lane;
+          const int valid_rows = static_cast<int>(p.M - m_warp < 32 ? p.M - m_warp : 32);
 #pragma unroll 1
           for (int c = half; c < BN / 32; c += 2) {
             uint32_t r[32];
@@ -453,7 +492,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld_wait();
             const int n0 = n_tile * BN + c * 32;
             const int valid_cols = p.N - n0;
-            if (valid && valid_cols > 0) {
+            if (valid_cols >= 32 && vec_ok && valid_rows > 0) {
+              float v[32];
+              dequant_chunk<false>(r, sx, cw + c * 32, cb + c * 32, v);
+              uint4 row[4];
+              pack_row32(v, row);
+              store_chunk32_staged(stage, row, p.out + m_warp * p.ldo + n0, p.ldo, valid_rows);
+              if (valid && p.acc_out != nullptr) store_acc_chunk(p.acc_out + m * p.N + n0, r, valid_cols);
+            } else if (valid && valid_cols > 0) {
               float v[32];
               dequant_chunk<false>(r, sx, cw + c * 32, cb + c * 32, v);
               store_row_chunk(p.out + m * p.ldo + n0, v, valid_cols, vec_ok);
@@ -498,7 +544,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t m = m_pre;
         const bool valid = m < p.M;
         const float sx = sx_pre;
-        const bool vec_ok = (p.F % 8) == 0;
+        const bool vec_ok = (p.F % 8) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
+        const int64_t m_warp = m - lane;
+        const int valid_rows = static_cast<int>(p.M - m_warp < 32 ? p.M - m_warp : 32);
         constexpr float kNegLog2e = -1.4426950408889634f;
 #pragma unroll 1
         for (int c = half; c < BN / 64; c += 2) {
@@ -508,7 +556,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           const int j0 = n_tile * (BN / 2) + c * 32;
           const int valid_cols = p.F - j0;
-          if (valid && valid_cols > 0) {
+          const bool staged = valid_cols >= 32 && vec_ok && valid_rows > 0;
+          if (staged || (valid && valid_cols > 0)) {
             float g[32], u[32];
             dequant_chunk<false>(rg, sx, cw + c * 32, cb + c * 32, g);
             dequant_chunk<false>(ru, sx, cw + BN / 2 + c * 32, cb + BN / 2 + c * 32, u);
@@ -523,7 +572,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               g[j] = __fmul_rn(__fmul_rn(gg.x, rcp_approx_ftz(__fadd_rn(1.0f, e0))), uu.x);
               g[j + 1] = __fmul_rn(__fmul_rn(gg.y, rcp_approx_ftz(__fadd_rn(1.0f, e1))), uu.y);
             }
-            store_row_chunk(p.out + m * p.F + j0, g, valid_cols, vec_ok);
+            if (staged) {
+              uint4 row[4];
+              pack_row32(g, row);
+              store_chunk32_staged(stage, row, p.out + m_warp * p.F + j0, p.F, valid_rows);
+            } else {
+              store_row_chunk(p.out + m * p.F + j0, g, valid_cols, vec_ok);
+            }
           }
         }
       } else if constexpr (EP == Epi::kQkvRope) {
@@ -537,19 +592,35 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t bb = valid ? m / p.tokens : 0;
         const int64_t tt = valid ? m - bb * p.tokens : 0;
         const int64_t dst_off = ((bb * p.heads + h) * p.tokens + tt) * 64;
+        // The warp's 32 rows are consecutive tokens of one batch entry (the
+        // common case): then their q / k / v rows are consecutive 128-byte rows
+        // of [B, H, n, 64] and the stores go through the staging buffer.
+        const int64_t dst_off0 = __shfl_sync(0xffffffffu, dst_off, 0);
+        const int64_t bb0 = __shfl_sync(0xffffffffu, bb, 0);
+        const bool staged = __all_sync(0xffffffffu, !valid || (bb == bb0 && dst_off == dst_off0 + lane * 64));
+        const int valid_rows = static_cast<int>(p.M - (m - lane) < 32 ? p.M - (m - lane) : 32);
         uint4 rc[8], rs[8];
         {
           uint32_t r[32];
           tmem_ld32(t_row + 128 + half * 32, r);
           tmem_ld_wait();
-          if (valid) {
-            float v[32];
-            dequant_chunk<false>(r, sx, cw + 128 + half * 32, cb + 128 + half * 32, v);
+          float v[32];
+          dequant_chunk<false>(r, sx, cw + 128 + half * 32, cb + 128 + half * 32, v);
+          if (staged) {
+            uint4 row[4];
+            pack_row32(v, row);
+            store_chunk32_staged(stage, row, p.v_out + dst_off0 + half * 32, 64, valid_rows);
+          } else if (valid) {
             store_row_chunk(p.v_out + dst_off + half * 32, v, 32, true);
           }
         }
         // the token's rope tables, in flight while q (or k) is dequantized
-        if (valid) load_rope_row(p.cos_t + m * p.R, p.sin_t + m * p.R, p.R, rc, rs);
+        if (valid) {
+          load_rope_row(p.cos_t + m * p.R, p.sin_t + m * p.R, p.R, rc, rs);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) rc[q] = rs[q] = make_uint4(0, 0, 0, 0);
+        }
         __half2 x[32];   // the 64 fp16-rounded q (or k) outputs of this row
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
@@ -573,7 +644,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             x[c * 16 + 2 * q + 1] = dq(2, w4.z, w4.w, b4.z, b4.w);
           }
         }
-        if (valid) qk_norm_rope_regs(x, p.eps, p.R, rc, rs, (half == 0 ? p.q_out : p.k_out) + dst_off);
+        uint4 o[8];
+        qk_norm_rope_regs(x, p.eps, p.R, rc, rs, o);
+        __half* qk = half == 0 ? p.q_out : p.k_out;
+        if (staged) {
+          const uint4 lo[4] = {o[0], o[1], o[2], o[3]}, hi[4] = {o[4], o[5], o[6], o[7]};
+          store_chunk32_staged(stage, lo, qk + dst_off0, 64, valid_rows);
+          store_chunk32_staged(stage, hi, qk + dst_off0 + 32, 64, valid_rows);
+        } else if (valid) {
+#pragma unroll
+          for (int q = 0; q < 8; ++q) reinterpret_cast<uint4*>(qk + dst_off)[q] = o[q];
+        }
       }
       tc_fence_before();
       mbar_arrive(&tempty_bar[acc]);
@@ -849,7 +930,8 @@ using namespace h3b;
 template <int BN, int STAGES, AMode AM, Epi EP, int MT = 1, bool F16 = false>
 int launch_mma(const CUtensorMap& ma, const CUtensorMap& mb, const MmaParams& p, cudaStream_t stream,
                const char* name) {
-  constexpr size_t smem = STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256 + 2 * 2 * BN * sizeof(float);
+  constexpr size_t smem = STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256 + 2 * 2 * BN * sizeof(float) +
+                          (EP == Epi::kConv ? 0 : kEpiWarps * 2048);
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = mma_tc_kernel<BN, STAGES, AM, EP, MT, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
