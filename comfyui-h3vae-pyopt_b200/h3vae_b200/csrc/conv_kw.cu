@@ -27,7 +27,8 @@ template <int BN, int MT, int AST, int BST>
 struct KwCfg {
   static constexpr uint32_t a_stage = MT * kKwStripBytes;
   static constexpr uint32_t b_stage = BN * kBK;
-  static constexpr size_t smem = AST * a_stage + BST * b_stage + 1024 + 256 + 2 * BN * sizeof(float);
+  static constexpr size_t smem = AST * a_stage + BST * b_stage + 1024 + 256 + 2 * BN * sizeof(float) +
+                                 kEpiWarps * 2048;   // + one 2 KB load/store staging buffer per epilogue warp
 };
 
 template <int kKwBN, int kKwMT, int kKwAStages, int kKwBStages>
@@ -201,6 +202,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = quad * 32 + lane;
     const int half = (warp - 2) >> 2;
     const int etid = threadIdx.x - 64;
+    const uint32_t stage = smem_u32(cst + 2 * kKwBN) + (warp - 2) * 2048;
     // column constants (weight scale, bias) of the single N tile, staged once
     if (etid < kKwBN) {
       const bool in = etid < p.N;
@@ -231,6 +233,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int64_t obase =
             b * p.osB + od * p.osD + static_cast<int64_t>(oh) * p.osH + static_cast<int64_t>(ow) * p.osW;
         const int64_t pos = ((static_cast<int64_t>(b) * p.Do + od) * p.Ho + oh) * p.Wo + ow;
+        // a warp's 32 rows are consecutive positions of one output row (the
+        // valid ones a prefix): staged residual loads and output stores
+        const int valid_rows = __popc(__ballot_sync(0xffffffffu, valid));
+        const int64_t obase0 = __shfl_sync(0xffffffffu, obase, 0);
 #pragma unroll 1
         for (int c = half; c < kKwBN / 32; c += 2) {
           uint32_t r[32];
@@ -238,7 +244,19 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld_wait();
           const int n0 = c * 32;
           const int valid_cols = p.N - n0;
-          if (valid && valid_cols > 0) {
+          if (vec_ok && valid_cols >= 32 && valid_rows > 0) {
+            float v[32];
+            dequant_chunk<false>(r, sx, cw + n0, cb + n0, v);
+            if (p.residual != nullptr) {
+              uint4 res[4];
+              load_chunk32_staged(stage, p.residual + obase0 + n0, p.osW, valid_rows, res);
+              add_residual_row(v, res);
+            }
+            uint4 row[4];
+            pack_row32(v, row);
+            store_chunk32_staged(stage, row, p.out + obase0 + n0, p.osW, valid_rows);
+            if (valid && p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
+          } else if (valid && valid_cols > 0) {
             float v[32];
             dequant_chunk<false>(r, sx, cw + n0, cb + n0, v);
             if (p.residual != nullptr) add_residual_chunk(v, p.residual + obase + n0, valid_cols, vec_ok);

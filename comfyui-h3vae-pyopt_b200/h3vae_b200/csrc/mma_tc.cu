@@ -202,6 +202,41 @@ __device__ __forceinline__ void store_chunk32_staged(uint32_t stage, const uint4
   __syncwarp();
 }
 
+// The counterpart of store_chunk32_staged for loads: rows src0 + r * row_stride
+// (r < valid_rows) are read 8 rows x 64 B per instruction into the warp's
+// staging buffer, then each lane takes its own row's four 16-byte vectors
+// (rows >= valid_rows read as zeros).  Warp-collective.
+__device__ __forceinline__ void load_chunk32_staged(uint32_t stage, const __half* src0, int64_t row_stride,
+                                                    int valid_rows, uint4 (&row)[4]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int r = (lane >> 2) + 8 * i;
+    const int k = lane & 3;
+    const uint4 val = r < valid_rows ? __ldg(reinterpret_cast<const uint4*>(src0 + r * row_stride + k * 8))
+                                     : make_uint4(0, 0, 0, 0);
+    st_shared_v4(stage + r * 64 + ((k ^ ((r >> 1) & 3)) << 4), val);
+  }
+  __syncwarp();
+#pragma unroll
+  for (int k = 0; k < 4; ++k) row[k] = ld_shared_v4(stage + lane * 64 + ((k ^ ((lane >> 1) & 3)) << 4));
+  __syncwarp();
+}
+
+// v = fp16(fp16(v) + residual) for 32 values with the residual row in registers.
+__device__ __forceinline__ void add_residual_row(float (&v)[32], const uint4 (&res)[4]) {
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const __half2* h = reinterpret_cast<const __half2*>(&res[k]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __half22float2(h[j]);
+      v[k * 8 + 2 * j] = __fadd_rn(round_fp16(v[k * 8 + 2 * j]), f.x);
+      v[k * 8 + 2 * j + 1] = __fadd_rn(round_fp16(v[k * 8 + 2 * j + 1]), f.y);
+    }
+  }
+}
+
 // v = fp16(fp16(v) + residual): the residual block's `x + h` on fp16 tensors.
 __device__ __forceinline__ void add_residual_chunk(float (&v)[32], const __half* res, int valid_cols, bool vec_ok) {
   if (valid_cols >= 32 && vec_ok) {
@@ -253,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   // [2 buffers][scale | bias][BN] fp32 column constants of the epilogue, then
-  // (GEMM epilogues) one 2 KB store-staging buffer per epilogue warp
+  // one 2 KB load/store staging buffer per epilogue warp
   float* cst = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 256);
   const uint32_t stage_base = smem_u32(cst + 2 * 2 * BN);
 
@@ -523,6 +558,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int64_t obase =
               b * p.osB + od * p.osD + static_cast<int64_t>(oh) * p.osH + static_cast<int64_t>(ow) * p.osW;
           const int64_t pos = ((static_cast<int64_t>(b) * p.Do + od) * p.Ho + oh) * p.Wo + ow;
+          // With output tiles at least 32 columns wide a warp's 32 rows are
+          // consecutive positions of one output row (the valid ones a prefix):
+          // residual loads and output stores then go through the staging buffer.
+          const int valid_rows = __popc(__ballot_sync(0xffffffffu, valid));
+          const int64_t obase0 = __shfl_sync(0xffffffffu, obase, 0);
 #pragma unroll 1
           for (int c = half; c < BN / 32; c += 2) {
             uint32_t r[32];
@@ -530,7 +570,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             tmem_ld_wait();
             const int n0 = n_tile * BN + c * 32;
             const int valid_cols = p.N - n0;
-            if (valid && valid_cols > 0) {
+            if (p.bw >= 32 && vec_ok && valid_cols >= 32 && valid_rows > 0) {
+              float v[32];
+              dequant_chunk<F16>(r, sx, cw + c * 32, cb + c * 32, v);
+              if (p.residual != nullptr) {
+                uint4 res[4];
+                load_chunk32_staged(stage, p.residual + obase0 + n0, p.osW, valid_rows, res);
+                add_residual_row(v, res);
+              }
+              uint4 row[4];
+              pack_row32(v, row);
+              store_chunk32_staged(stage, row, p.out + obase0 + n0, p.osW, valid_rows);
+              if (valid && !F16 && p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
+            } else if (valid && valid_cols > 0) {
               float v[32];
               dequant_chunk<F16>(r, sx, cw + c * 32, cb + c * 32, v);
               if (p.residual != nullptr) add_residual_chunk(v, p.residual + obase + n0, valid_cols, vec_ok);
@@ -930,8 +982,8 @@ using namespace h3b;
 template <int BN, int STAGES, AMode AM, Epi EP, int MT = 1, bool F16 = false>
 int launch_mma(const CUtensorMap& ma, const CUtensorMap& mb, const MmaParams& p, cudaStream_t stream,
                const char* name) {
-  constexpr size_t smem = STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256 + 2 * 2 * BN * sizeof(float) +
-                          (EP == Epi::kConv ? 0 : kEpiWarps * 2048);
+  constexpr size_t smem =
+      STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256 + 2 * 2 * BN * sizeof(float) + kEpiWarps * 2048;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = mma_tc_kernel<BN, STAGES, AM, EP, MT, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -1067,7 +1119,7 @@ int conv3d_tc(const ConvArgs& a, int64_t Do, int64_t Ho, int64_t Wo, const char*
     if (a.O <= 128 && (p.m_tiles + 1) / 2 >= sms)
       return launch_conv_kw<128, 2, 3, 6>(a.x, a.x_dims, a.w, a.O, (int)taps, p, a.stream, name);
     if (a.O > 128 && a.O <= 256 && p.m_tiles >= sms)
-      return launch_conv_kw<256, 1, 3, 5>(a.x, a.x_dims, a.w, a.O, (int)taps, p, a.stream, name);
+      return launch_conv_kw<256, 1, 2, 5>(a.x, a.x_dims, a.w, a.O, (int)taps, p, a.stream, name);
   }
   if (a.O <= 64) {
     p.n_tiles = 1;
