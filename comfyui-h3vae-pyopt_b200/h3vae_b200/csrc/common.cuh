@@ -556,13 +556,15 @@ __device__ __forceinline__ void qk_norm_rope_regs_t(__half2 (&xh)[32], float eps
   // exactly fp16 multiplies (an 11 x 11-bit product is exact before its one
   // rounding), so the rotation runs on packed halves; the sum of the two
   // products is one fp16 add.
-  float ss = 0.0f;
+  // sum of squares in four independent chains (short dependency chains)
+  float ssa[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
   for (int d = 0; d < 32; ++d) {
     const float2 f = __half22float2(xh[d]);
-    ss = __fmaf_rn(f.x, f.x, ss);
-    ss = __fmaf_rn(f.y, f.y, ss);
+    ssa[d & 3] = __fmaf_rn(f.x, f.x, ssa[d & 3]);
+    ssa[d & 3] = __fmaf_rn(f.y, f.y, ssa[d & 3]);
   }
+  const float ss = (ssa[0] + ssa[1]) + (ssa[2] + ssa[3]);
   const float inv = rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / 64.0f), eps));
 #pragma unroll
   for (int d = 0; d < 32; ++d) {
