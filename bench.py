@@ -39,10 +39,10 @@ TILE = 256
 OVERLAP = 32
 METRIC = "768x1344x124 tile256 encode+decode round-trip seconds"
 # DRAM bytes (read + write) per INT8 conv launch at encoder batch 4: ncu dram__bytes_read.sum +
-# dram__bytes_write.sum summed over the 16 conv launches of one tile-batch-1 encoder call
-# (2.78 GB: 14 launches measured, the two stage-4 launches estimated from their twins), times 4 for
-# batch 4 (activation traffic scales with the batch), divided by the 16 launches.
-CONV_DRAM_BYTES_PER_LAUNCH = 2.78e9 * 4 / 16
+# dram__bytes_write.sum summed over the 16 INT8 conv launches of one tile-batch-1 encoder call
+# (2.84 GB: kw-strip kernels for stages 1-2, the generic implicit-GEMM kernel for stages 3-4), times 4
+# for batch 4 (activation traffic scales with the batch), divided by the 16 launches.
+CONV_DRAM_BYTES_PER_LAUNCH = 2.84e9 * 4 / 16
 UNIT = "s"
 
 
