@@ -1,6 +1,7 @@
-// INT8 implicit-GEMM causal conv3d with the three kw taps read from one input
-// strip (stride 1, kernel width 3, 128 output columns per M tile; C_out <= 128
-// with two M tiles per CTA, or C_out <= 256 with one).
+// Implicit-GEMM causal conv3d (INT8, or fp16 operands with fp32 accumulation)
+// with the three kw taps read from one input strip (stride 1, kernel width 3,
+// 128 output columns per M tile; C_out <= 128 with two M tiles per CTA, or
+// C_out <= 256 with one).
 //
 // In the mma_tc conv mainloop every k-block (tap, channel chunk) loads its own
 // 128-row A box, so each input row is fetched from L2 once per kw tap.  Here
@@ -31,15 +32,16 @@ struct KwCfg {
                                  kEpiWarps * 2048;   // + one 2 KB load/store staging buffer per epilogue warp
 };
 
-template <int kKwBN, int kKwMT, int kKwAStages, int kKwBStages>
+template <int kKwBN, int kKwMT, int kKwAStages, int kKwBStages, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
-    conv_i8_kw_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+    conv_kw_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                       const MmaParams p) {
   constexpr uint32_t kKwAStageBytes = KwCfg<kKwBN, kKwMT, kKwAStages, kKwBStages>::a_stage;
   constexpr uint32_t kKwBStageBytes = KwCfg<kKwBN, kKwMT, kKwAStages, kKwBStages>::b_stage;
   constexpr uint32_t kTmemCols = TmemLayout<kKwMT * kKwBN>::cols;
   constexpr uint32_t kAccStride = TmemLayout<kKwMT * kKwBN>::acc_stride;
-  constexpr uint32_t kIdesc = make_idesc_i8(kBM, kKwBN);
+  constexpr uint32_t kIdesc = F16 ? make_idesc_f16(kBM, kKwBN) : make_idesc_i8(kBM, kKwBN);
+  constexpr int kKE = F16 ? 64 : 128;   // K elements per 128-byte chunk
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -133,13 +135,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int i = 0; i < kKwMT; ++i)
             // An M tile past the last one decodes to b >= B: the box is out of range and loads zeros.
-            tma_load_5d(smem_a + sa * kKwAStageBytes + i * kKwStripBytes, &map_a, &a_full[sa], cc * kBK, cw[i],
+            tma_load_5d(smem_a + sa * kKwAStageBytes + i * kKwStripBytes, &map_a, &a_full[sa], cc * kKE, cw[i],
                         chh[i] + kh, cd[i] + kd, cb[i]);
           for (int kw = 0; kw < 3; ++kw, ++ib) {
             const uint32_t sb = ib % kKwBStages;
             if (!mbar_wait(&b_empty[sb], ((ib / kKwBStages) & 1u) ^ 1u, abort_flag)) { ok = false; break; }
             mbar_arrive_expect_tx(&b_full[sb], kKwBStageBytes);
-            tma_load_2d(smem_b + sb * kKwBStageBytes, &map_b, &b_full[sb], ((kd * 3 + kh) * 3 + kw) * p.C + cc * kBK,
+            tma_load_2d(smem_b + sb * kKwBStageBytes, &map_b, &b_full[sb], ((kd * 3 + kh) * 3 + kw) * p.C + cc * kKE,
                         0);
           }
         }
@@ -183,9 +185,13 @@ __global__ void __launch_bounds__(kThreads, 1)
               // bit-exactly against an exact conv).
               const uint64_t adesc = make_sw128_desc(a_base + i * kKwStripBytes + kw * kBK);
 #pragma unroll
-              for (int k = 0; k < kBK / 32; ++k)
-                mma_i8(d_tmem + i * kKwBN, adesc + 2 * k, bdesc + 2 * k, kIdesc,
-                       (g > g0 || kw > 0 || k > 0) ? 1u : 0u);
+              for (int k = 0; k < kBK / 32; ++k) {   // 32 bytes of K per MMA
+                const uint32_t accumulate = (g > g0 || kw > 0 || k > 0) ? 1u : 0u;
+                if constexpr (F16)
+                  mma_f16(d_tmem + i * kKwBN, adesc + 2 * k, bdesc + 2 * k, kIdesc, accumulate);
+                else
+                  mma_i8(d_tmem + i * kKwBN, adesc + 2 * k, bdesc + 2 * k, kIdesc, accumulate);
+              }
             }
             tc_commit(&b_empty[sb]);
           }
@@ -206,12 +212,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // column constants (weight scale, bias) of the single N tile, staged once
     if (etid < kKwBN) {
       const bool in = etid < p.N;
-      cst[etid] = in ? __ldg(p.w_scale + etid) : 1.0f;
+      cst[etid] = (in && !F16) ? __ldg(p.w_scale + etid) : 1.0f;
       cst[kKwBN + etid] = (in && p.bias != nullptr) ? __half2float(p.bias[etid]) : 0.0f;
     }
     const float* cw = cst;
     const float* cb = cst + kKwBN;
-    const float sx = *p.a_scale;
+    const float sx = F16 ? 0.0f : *p.a_scale;
     const bool vec_ok = ((reinterpret_cast<uintptr_t>(p.out) & 15u) == 0) && (p.osW % 8 == 0) &&
                         (p.osH % 8 == 0) && (p.osD % 8 == 0) && (p.osB % 8 == 0);
     uint32_t local = 0;
@@ -246,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int valid_cols = p.N - n0;
           if (vec_ok && valid_cols >= 32 && valid_rows > 0) {
             float v[32];
-            dequant_chunk<false>(r, sx, cw + n0, cb + n0, v);
+            dequant_chunk<F16>(r, sx, cw + n0, cb + n0, v);
             if (p.residual != nullptr) {
               uint4 res[4];
               load_chunk32_staged(stage, p.residual + obase0 + n0, p.osW, valid_rows, res);
@@ -255,13 +261,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint4 row[4];
             pack_row32(v, row);
             store_chunk32_staged(stage, row, p.out + obase0 + n0, p.osW, valid_rows);
-            if (valid && p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
+            if (!F16 && valid && p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
           } else if (valid && valid_cols > 0) {
             float v[32];
-            dequant_chunk<false>(r, sx, cw + n0, cb + n0, v);
+            dequant_chunk<F16>(r, sx, cw + n0, cb + n0, v);
             if (p.residual != nullptr) add_residual_chunk(v, p.residual + obase + n0, valid_cols, vec_ok);
             store_row_chunk(p.out + obase + n0, v, valid_cols, vec_ok);
-            if (p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
+            if (!F16 && p.acc_out != nullptr) store_acc_chunk(p.acc_out + pos * p.N + n0, r, valid_cols);
           }
         }
       }
@@ -283,7 +289,7 @@ namespace {
 // Launch of the kw-strip conv for an INT8 conv whose geometry conv3d_tc has
 // already validated and described in p (C % 128 == 0, 3x3x3 kernel, stride 1,
 // bw = 128 so one M tile is 128 columns of one output row, C_out <= BN).
-template <int BN, int MT, int AST, int BST>
+template <int BN, int MT, int AST, int BST, bool F16>
 int launch_conv_kw(const void* x, const int64_t* x_dims, const void* w, int64_t O, int taps, h3b::MmaParams p,
                    cudaStream_t stream, const char* name) {
   using namespace h3b;
@@ -292,22 +298,24 @@ int launch_conv_kw(const void* x, const int64_t* x_dims, const void* w, int64_t 
   CUtensorMap ma, mb;
   uint64_t adims[5] = {(uint64_t)C, (uint64_t)W, (uint64_t)H, (uint64_t)D, (uint64_t)B};
   uint64_t astr[4] = {(uint64_t)C, (uint64_t)(C * W), (uint64_t)(C * W * H), (uint64_t)(C * W * H * D)};
-  uint32_t abox[5] = {(uint32_t)kBK, (uint32_t)kKwStripRows, 1, 1, 1};
+  constexpr int kElt = F16 ? 2 : 1;
+  constexpr int kKE = kBK / kElt;
+  const CUtensorMapDataType dt = F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  for (auto& v : astr) v *= kElt;
+  uint32_t abox[5] = {(uint32_t)kKE, (uint32_t)kKwStripRows, 1, 1, 1};
   uint32_t aes[5] = {1, 1, 1, 1, 1};
-  int rc = h3b_host::encode_tiled(&ma, CU_TENSOR_MAP_DATA_TYPE_UINT8, 5, x, adims, astr, abox, aes,
-                                  CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = h3b_host::encode_tiled(&ma, dt, 5, x, adims, astr, abox, aes, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   uint64_t bdims[2] = {(uint64_t)(taps * C), (uint64_t)O};
-  uint64_t bstr[1] = {(uint64_t)(taps * C)};
-  uint32_t bbox[2] = {(uint32_t)kBK, (uint32_t)BN};
+  uint64_t bstr[1] = {(uint64_t)(taps * C * kElt)};
+  uint32_t bbox[2] = {(uint32_t)kKE, (uint32_t)BN};
   uint32_t es[2] = {1, 1};
-  rc = h3b_host::encode_tiled(&mb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w, bdims, bstr, bbox, es,
-                              CU_TENSOR_MAP_SWIZZLE_128B);
+  rc = h3b_host::encode_tiled(&mb, dt, 2, w, bdims, bstr, bbox, es, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   p.n_tiles = 1;
   p.m_groups = (p.m_tiles + MT - 1) / MT;
   static_assert(Cfg::smem <= 232448, "shared memory budget");
-  auto kern = conv_i8_kw_kernel<BN, MT, AST, BST>;
+  auto kern = conv_kw_kernel<BN, MT, AST, BST, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(Cfg::smem));
   if (e != cudaSuccess) return h3b_host::set_error(H3B_ECUDA, "%s: smem attribute: %s", name, cudaGetErrorString(e));
   const int grid = p.m_groups < h3b_host::num_sms() ? p.m_groups : h3b_host::num_sms();

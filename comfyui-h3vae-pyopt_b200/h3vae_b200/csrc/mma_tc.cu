@@ -1113,13 +1113,12 @@ int conv3d_tc(const ConvArgs& a, int64_t Do, int64_t Ho, int64_t Wo, const char*
     return h3b_host::encode_tiled(&mb, dt, 2, a.w, bdims, bstr, bbox, es, CU_TENSOR_MAP_SWIZZLE_128B);
   };
   const int sms = h3b_host::num_sms();
-  // INT8 3x3x3 stride-1 convs over rows of >= 128 output columns: the kw-strip mainloop
-  if (!F16 && a.kd == 3 && a.kh == 3 && a.kw == 3 && a.sd == 1 && a.sh == 1 && a.sw == 1 && bw == kBM &&
-      C % kBK == 0) {
+  // 3x3x3 stride-1 convs over rows of >= 128 output columns: the kw-strip mainloop
+  if (a.kd == 3 && a.kh == 3 && a.kw == 3 && a.sd == 1 && a.sh == 1 && a.sw == 1 && bw == kBM && C % kKE == 0) {
     if (a.O <= 128 && (p.m_tiles + 1) / 2 >= sms)
-      return launch_conv_kw<128, 2, 3, 6>(a.x, a.x_dims, a.w, a.O, (int)taps, p, a.stream, name);
+      return launch_conv_kw<128, 2, 3, 6, F16>(a.x, a.x_dims, a.w, a.O, (int)taps, p, a.stream, name);
     if (a.O > 128 && a.O <= 256 && p.m_tiles >= sms)
-      return launch_conv_kw<256, 1, 2, 5>(a.x, a.x_dims, a.w, a.O, (int)taps, p, a.stream, name);
+      return launch_conv_kw<256, 1, 2, 5, F16>(a.x, a.x_dims, a.w, a.O, (int)taps, p, a.stream, name);
   }
   if (a.O <= 64) {
     p.n_tiles = 1;

@@ -33,9 +33,27 @@ CASES = [
     ((2, 128, 9, 16, 16), 256, (1, 1, 1), (1, 1, 1)),        # 1x1x1 shortcut
     ((1, 512, 7, 10, 12), 32, (3, 3, 3), (1, 1, 1)),         # encoder conv_out (BN=64 tile)
     ((1, 1024, 7, 10, 10), 512, (3, 3, 3), (1, 1, 1)),       # decoder upsampling conv
-    ((1, 256, 5, 131, 130), 128, (3, 3, 3), (1, 1, 1)),      # two M tiles per CTA, odd tile count
+    ((1, 256, 5, 131, 130), 128, (3, 3, 3), (1, 1, 1)),      # two M tiles per CTA, odd tile count (kw-strip)
     ((1, 128, 5, 9, 200), 192, (3, 3, 3), (1, 1, 1)),        # O not a multiple of the tile, W > 128
+    ((1, 128, 4, 150, 130), 256, (3, 3, 3), (1, 1, 1)),      # kw-strip kernel, 256 output columns
+    ((1, 128, 4, 76, 258), 192, (3, 3, 3), (1, 1, 1)),       # kw-strip, 192 of 256 columns, 2 M tiles per row
 ]
+
+
+def test_conv3d_f16_kw_strip_residual_causal(cuda_lib):
+    """The decoder's 3x3x3 up-conv shape class (128-column rows, enough tiles for the kw-strip
+    mainloop) with the two causal zero frames skipped and a fused residual."""
+    from h3vae_b200 import kernels as K
+    g = torch.Generator().manual_seed(11)
+    x = torch.randn((1, 256, 5, 131, 130), generator=g).half()
+    x[:, :, :2] = 0
+    w = (torch.randn((128, 256, 3, 3, 3), generator=g) / (256 * 27) ** 0.5).half()
+    b = (torch.randn(128, generator=g) * 0.1).half()
+    r = torch.randn((1, 128, 3, 129, 128), generator=g).half()
+    y = K.conv3d_f16(x.cuda().contiguous(memory_format=torch.channels_last_3d), K.pack_conv_weight_f16(w).cuda(),
+                     b.cuda(), (3, 3, 3), (1, 1, 1), causal_zero_frames=2,
+                     residual=r.cuda().contiguous(memory_format=torch.channels_last_3d))
+    _close(y.cpu(), _ref(x, w, b, (1, 1, 1), residual=r))
 
 
 @pytest.mark.parametrize("shape,o,kernel,stride", CASES)
