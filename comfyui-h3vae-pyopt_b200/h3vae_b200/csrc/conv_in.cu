@@ -29,7 +29,36 @@ constexpr int kCinThreads = 32 * (kCinWorkers + 1);
 constexpr uint32_t kCinKBlockBytes = 128 * 128;   // 128 rows x 128 bytes
 constexpr uint32_t kCinATileBytes = 2 * kCinKBlockBytes;
 constexpr uint32_t kCinBTileBytes = 2 * kCinKBlockBytes;
-constexpr uint32_t kCinSmemBytes = 2 * kCinATileBytes + kCinBTileBytes + 1024 + 1024;
+constexpr uint32_t kCinStageBytes = 1024;   // per build/epilogue warp: 16 rows x 64 B of output staging
+constexpr uint32_t kCinSmemBytes = 2 * kCinATileBytes + kCinBTileBytes + 1024 + 1024 + kCinWorkers * kCinStageBytes;
+
+// 32 output rows (lane r = row r) x 32 fp16 channels to dst0 + r * row_stride
+// through this warp's 1 KB staging buffer, 16 rows per pass: the rows' 16-byte
+// chunks are XOR-swizzled so the shared accesses are conflict free, and each
+// global store instruction writes 8 rows x 64 contiguous bytes (instead of 32
+// rows x 16 B).  Warp-collective; rows >= valid_rows are not written.
+__device__ __forceinline__ void cin_store_chunk32(uint32_t stage, const uint4 (&row)[4], __half* dst0,
+                                                  int64_t row_stride, int valid_rows) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int pass = 0; pass < 2; ++pass) {
+    if ((lane >> 4) == pass) {
+      const int rl = lane & 15;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) st_shared_v4(stage + rl * 64 + ((k ^ ((rl >> 1) & 3)) << 4), row[k]);
+    }
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const int rl = (lane >> 2) + 8 * i;
+      const int k = lane & 3;
+      const uint4 v = ld_shared_v4(stage + rl * 64 + ((k ^ ((rl >> 1) & 3)) << 4));
+      const int r = pass * 16 + rl;
+      if (r < valid_rows) *reinterpret_cast<uint4*>(dst0 + r * row_stride + k * 8) = v;
+    }
+    __syncwarp();
+  }
+}
 
 // Byte offset of 16-byte chunk j (0..15) of row r (0..127) in a two-K-block,
 // 128-byte-swizzled K-major tile (the layout TMA SWIZZLE_128B produces).
@@ -170,6 +199,7 @@ __global__ void __launch_bounds__(kCinThreads, 2)
     const int quad = warp & 3;
     const int row = quad * 32 + lane;   // A row == TMEM lane == output pixel of the tile
     const int half = warp >> 2;         // chunks 0..6 / 7..13 while building; columns 0..63 / 64..127 after
+    const uint32_t stage = smem_u32(smem_b + kCinBTileBytes + 2048) + warp * kCinStageBytes;
     auto epilogue = [&](int tile, uint32_t i) -> bool {
       const uint32_t s = i & 1u;
       // tcgen05.ld is warp-collective: leave together if any lane's wait gave up
@@ -180,27 +210,29 @@ __global__ void __launch_bounds__(kCinThreads, 2)
       const int h = t % H; t /= H;
       const int tt = t % T;
       const int b = t / T;
-      const int w = wt * 128 + row;
+      const int w0 = wt * 128 + quad * 32;   // output column of lane 0 of this warp
       const uint32_t t_row = tmem_base + s * kCinO + (static_cast<uint32_t>(quad * 32) << 16) + half * 64;
-      __half* dst = out + ((((static_cast<int64_t>(b) * T + tt) * H + h) * W + w) * kCinO) + half * 64;
+      // the warp's 32 rows are consecutive pixels of one output row; those with w < W are stored
+      __half* dst0 = out + ((((static_cast<int64_t>(b) * T + tt) * H + h) * W + w0) * kCinO) + half * 64;
+      const int valid_rows = W - w0 < 32 ? W - w0 : 32;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t r[32];
         tmem_ld32(t_row + c * 32, r);
         tmem_ld_wait();
-        if (w < W) {
+        uint4 rowv[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            __align__(16) __half2 hv[4];
+        for (int q = 0; q < 4; ++q) {
+          __align__(16) __half2 hv[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int col = half * 64 + c * 32 + q * 8 + 2 * e;
-              hv[e] = __floats2half2_rn(__fadd_rn(__uint_as_float(r[q * 8 + 2 * e]), s_bias[col]),
-                                        __fadd_rn(__uint_as_float(r[q * 8 + 2 * e + 1]), s_bias[col + 1]));
-            }
-            *reinterpret_cast<uint4*>(dst + c * 32 + q * 8) = *reinterpret_cast<const uint4*>(hv);
+          for (int e = 0; e < 4; ++e) {
+            const int col = half * 64 + c * 32 + q * 8 + 2 * e;
+            hv[e] = __floats2half2_rn(__fadd_rn(__uint_as_float(r[q * 8 + 2 * e]), s_bias[col]),
+                                      __fadd_rn(__uint_as_float(r[q * 8 + 2 * e + 1]), s_bias[col + 1]));
           }
+          rowv[q] = *reinterpret_cast<const uint4*>(hv);
         }
+        if (valid_rows > 0) cin_store_chunk32(stage, rowv, dst0 + c * 32, kCinO, valid_rows);
       }
       tc_fence_before();
       mbar_arrive(&t_empty[s]);
