@@ -12,8 +12,11 @@
 //               halves the B traffic per MMA for narrow (BN = 128) outputs.
 //   warps 2..9  epilogue: tcgen05.ld of the finished accumulator (one TMEM
 //               lane = one output row per thread; the two warps of a lane
-//               quadrant take alternate 32-column chunks), dequantize, fused
-//               op, store.
+//               quadrant take alternate 32-column chunks), dequantize with
+//               the tile's column constants staged in shared memory, fused
+//               op, store -- through a per-warp shared staging buffer when
+//               the warp's 32 rows are evenly strided, so each global store
+//               instruction writes 8 rows x 64 contiguous bytes.
 // The double-buffered accumulator lets the epilogue of tile i overlap the
 // mainloop of tile i+1.
 //
