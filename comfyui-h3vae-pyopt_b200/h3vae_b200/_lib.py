@@ -73,6 +73,7 @@ _SIGNATURES = {
     "h3b_attention_f16": (c_int, [c_void_p, _i64p, c_void_p, _i64p, c_void_p, _i64p, c_void_p, _i64p, c_int64,
                                   c_int64, c_int64, c_int64, c_float, c_void_p]),
     "h3b_finalize_pixels": (c_int, [c_void_p, c_int, _i64p, _i64p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "h3b_blend_accumulate": (c_int, [c_void_p, c_int, _i64p, _i64p, c_void_p, c_void_p, _i64p, c_void_p]),
 }
 
 EXPORTED_SYMBOLS = tuple(name for name in _SIGNATURES)

@@ -12,7 +12,8 @@
 //   norm_pack_kernel    GroupNorm affine -> fp16 -> SiLU -> fp16, reflect pad 1
 //                       in H/W and two zero frames in front; modes: absmax of the
 //                       interior, INT8 with the per-tensor scale, or fp16 output.
-//   residual_pack_kernel, quantize kernels, finalize_pixels_kernel.
+//   residual_pack_kernel, quantize kernels, finalize_pixels_kernel,
+//   blend_accumulate_kernel (one tile's weighted term added into the blend canvas).
 #include <mutex>
 
 #include "common.cuh"
@@ -662,6 +663,41 @@ __global__ void finalize_pixels_kernel(const T* __restrict__ x, Strided5 t, int6
   }
 }
 
+// ---------------------------------------------------------------------------
+// Overlap blend: canvas[c, t, y, x] += fp32(tile[c, t, y, x]) * weight[y, x],
+// the product and the sum each rounded once (no FMA), as the host-side
+// `canvas.add_(tile.float() * weight)` rounds them.  One work item is a
+// 128-element piece of one (c, t, y) row, so both tensors are read along their
+// unit-stride x axis and the weight row is shared by every (c, t).
+// ---------------------------------------------------------------------------
+struct Strided4 {
+  int64_t n[4];
+  int64_t s[4];
+};
+
+constexpr int kBlendThreads = 128;
+
+template <typename T>
+__global__ void __launch_bounds__(kBlendThreads) blend_accumulate_kernel(const T* __restrict__ tile, Strided4 ts,
+                                                                       const float* __restrict__ weight,
+                                                                       float* __restrict__ canvas, Strided4 cs,
+                                                                       int64_t pieces, int pieces_per_row) {
+  for (int64_t p = blockIdx.x; p < pieces; p += gridDim.x) {
+    const int64_t row = p / pieces_per_row;
+    const int64_t x = (p - row * pieces_per_row) * kBlendThreads + threadIdx.x;
+    if (x >= ts.n[3]) continue;
+    const int64_t y = row % ts.n[2];
+    const int64_t ct = row / ts.n[2];
+    const int64_t t = ct % ts.n[1];
+    const int64_t c = ct / ts.n[1];
+    float v;
+    if constexpr (sizeof(T) == 2) v = __half2float(tile[c * ts.s[0] + t * ts.s[1] + y * ts.s[2] + x * ts.s[3]]);
+    else v = tile[c * ts.s[0] + t * ts.s[1] + y * ts.s[2] + x * ts.s[3]];
+    float* dst = canvas + c * cs.s[0] + t * cs.s[1] + y * cs.s[2] + x * cs.s[3];
+    *dst = __fadd_rn(*dst, __fmul_rn(v, __ldg(weight + y * ts.n[3] + x)));
+  }
+}
+
 }  // namespace h3b
 
 // ===========================================================================
@@ -1019,6 +1055,34 @@ int h3b_finalize_pixels(const void* x, int x_is_fp16, const int64_t* dims5, cons
   else
     finalize_pixels_kernel<float><<<grid_for(total, 256), 256, 0, st>>>(static_cast<const float*>(x), t, total, std3,
                                                                          mean3, out, contiguous);
+  return h3b_host::check_launch(name);
+}
+
+int h3b_blend_accumulate(const void* tile, int tile_is_fp16, const int64_t* dims4, const int64_t* tile_strides4,
+                         const float* weight, float* canvas, const int64_t* canvas_strides4, h3b_stream_t stream) {
+  const char* name = "h3b_blend_accumulate";
+  if (!tile || !dims4 || !tile_strides4 || !weight || !canvas || !canvas_strides4)
+    return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  Strided4 ts{}, cs{};
+  for (int i = 0; i < 4; ++i) {
+    if (dims4[i] <= 0) return h3b_host::set_error(H3B_EINVAL, "%s: nonempty C,T,H,W tile required", name);
+    if (tile_strides4[i] < 0 || canvas_strides4[i] < 0)
+      return h3b_host::set_error(H3B_EINVAL, "%s: negative strides are not supported", name);
+    ts.n[i] = cs.n[i] = dims4[i];
+    ts.s[i] = tile_strides4[i];
+    cs.s[i] = canvas_strides4[i];
+  }
+  const int pieces_per_row = static_cast<int>((dims4[3] + kBlendThreads - 1) / kBlendThreads);
+  const int64_t pieces = dims4[0] * dims4[1] * dims4[2] * pieces_per_row;
+  const int64_t cap = static_cast<int64_t>(h3b_host::num_sms()) * 16;
+  const int grid = static_cast<int>(pieces < cap ? pieces : cap);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (tile_is_fp16)
+    blend_accumulate_kernel<__half><<<grid, kBlendThreads, 0, st>>>(static_cast<const __half*>(tile), ts, weight,
+                                                                     canvas, cs, pieces, pieces_per_row);
+  else
+    blend_accumulate_kernel<float><<<grid, kBlendThreads, 0, st>>>(static_cast<const float*>(tile), ts, weight,
+                                                                    canvas, cs, pieces, pieces_per_row);
   return h3b_host::check_launch(name);
 }
 

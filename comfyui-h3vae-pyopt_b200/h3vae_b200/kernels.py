@@ -385,6 +385,24 @@ def finalize_pixels(x: torch.Tensor, std: torch.Tensor, mean: torch.Tensor,
     return out
 
 
+def blend_accumulate(canvas: torch.Tensor, tile: torch.Tensor, weight: torch.Tensor) -> None:
+    """canvas += tile.float() * weight in place; canvas is a [C,T,H,W] FP32 window (any strides) of
+    the blend canvas, tile FP16/FP32 [C,T,H,W], weight FP32 [H,W] contiguous (the tile's weight map).
+    ref: h3vae_runtime.py:623-639 (the blend and trim these weights restate)."""
+    dev = _require_cuda(canvas, tile, weight)
+    if canvas.ndim != 4 or tile.shape != canvas.shape or canvas.numel() == 0:
+        raise ValueError("nonempty C,T,H,W tile matching the canvas window required")
+    if canvas.dtype != F32 or tile.dtype not in (F16, F32):
+        raise ValueError("FP32 canvas and FP16/FP32 tile required")
+    if weight.dtype != F32 or weight.shape != canvas.shape[2:] or not weight.is_contiguous():
+        raise ValueError("contiguous FP32 [H,W] weight map required")
+    _lib.check(_lib.load().h3b_blend_accumulate(tile.data_ptr(), 1 if tile.dtype == F16 else 0,
+                                                _lib.i64_array(tile.shape), _lib.i64_array(tile.stride()),
+                                                weight.data_ptr(), canvas.data_ptr(),
+                                                _lib.i64_array(canvas.stride()), _stream(dev)))
+    _count(1)
+
+
 # ---------------------------------------------------------------------------
 # Decoder
 # ---------------------------------------------------------------------------

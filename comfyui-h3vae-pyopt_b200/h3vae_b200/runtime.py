@@ -345,8 +345,8 @@ class H3VAEPyOptRuntime(torch.nn.Module):
             wmap = self._weights(lplan, i, j)
             for n, (bi, c) in enumerate((bi, c) for bi in range(b) for c in cs):
                 ly, lx = lplan.ys[i], lplan.xs[j]
-                lat[bi, :, c * tpc:(c + 1) * tpc, ly:ly + lplan.hs[i], lx:lx + lplan.ws[j]].add_(
-                    mean[n].float() * wmap)
+                K.blend_accumulate(lat[bi, :, c * tpc:(c + 1) * tpc, ly:ly + lplan.hs[i], lx:lx + lplan.ws[j]],
+                                   mean[n], wmap)
         self._reduce_to_rank0(lat)
         self._log_call("encode", t0)
         if self.rank != 0:
@@ -388,8 +388,8 @@ class H3VAEPyOptRuntime(torch.nn.Module):
             pix = self.decoder(lat)
             for n, (bi, c, i, j) in enumerate(group):
                 y0, x0 = pplan.ys[i], pplan.xs[j]
-                canvas[bi, :, c * fpc:(c + 1) * fpc, y0:y0 + pplan.hs[i], x0:x0 + pplan.ws[j]].add_(
-                    pix[n].float() * self._weights(pplan, i, j))
+                K.blend_accumulate(canvas[bi, :, c * fpc:(c + 1) * fpc, y0:y0 + pplan.hs[i], x0:x0 + pplan.ws[j]],
+                                   pix[n], self._weights(pplan, i, j))
         self._reduce_to_rank0(canvas)
         if self.rank != 0:
             self._log_call("decode", t0)

@@ -317,6 +317,19 @@ int h3b_attention_f16(const void* q, const int64_t* q_strides, const void* k, co
 int h3b_finalize_pixels(const void* x, int x_is_fp16, const int64_t* dims5, const int64_t* strides5,
                         const float* std3, const float* mean3, float* out, h3b_stream_t stream);
 
+/* ---- (a8, a15) overlap blend ------------------------------------------- */
+
+/* canvas[c,t,y,x] += fp32(tile[c,t,y,x]) * weight[y,x], product and sum each
+ * rounded once in fp32 (no FMA).  tile: fp16 (tile_is_fp16=1) or fp32 of
+ * logical shape dims4 = {C,T,H,W} with element strides; weight: fp32 [H,W]
+ * contiguous; canvas: fp32 window of the same logical shape with element
+ * strides (a view into the blend canvas).  Each tile's weight map makes the
+ * sum over tiles equal the reference's sequential ramp-blend and trim.
+ * ref: h3vae_runtime.py:623-639 (_encode_spatial_tiled blend / trim),
+ *      h3vae_runtime.py:457-477 (decoder tile tasks). */
+int h3b_blend_accumulate(const void* tile, int tile_is_fp16, const int64_t* dims4, const int64_t* tile_strides4,
+                         const float* weight, float* canvas, const int64_t* canvas_strides4, h3b_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,10 @@ def _cpu_finalize(x, std, mean, out=None):
     return y
 
 
+def _cpu_blend(canvas, tile, weight):
+    canvas.add_(tile.float() * weight)
+
+
 def _inputs():
     g = torch.Generator().manual_seed(11)
     video = (torch.rand((1, 3, 30, 96, 160), generator=g) * 2 - 1).half()
@@ -90,6 +94,7 @@ def _free_port():
 def _worker(rank, world, port, mode, queue):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     rt.K.finalize_pixels = _cpu_finalize
+    rt.K.blend_accumulate = _cpu_blend
     try:
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
         run = _make_runtime(dist.group.WORLD)
@@ -129,6 +134,7 @@ def _run(world, mode):
 
 def test_two_rank_encode_decode_equals_single_process():
     rt.K.finalize_pixels = _cpu_finalize
+    rt.K.blend_accumulate = _cpu_blend
     single = _make_runtime(None)
     video, lat = _inputs()
     enc_ref = single.encode(video)

@@ -245,3 +245,46 @@ def test_attention(cuda_lib, b, h, sq, skv):
     out = K.attention_f16(q.cuda(), k.cuda(), v.cuda(), 0.125)
     ref = O.attention(q.numpy(), k.numpy(), v.numpy(), 0.125)
     _close(out.cpu().numpy(), ref, atol=4e-3, rtol=4e-3)
+
+
+@pytest.mark.parametrize("h,w,tile,ov,tile_dtype", [(96, 200, 64, 16, torch.float16), (40, 300, 256, 32, torch.float32),
+                                                    (130, 130, 64, 8, torch.float16), (50, 200, 200, 16, torch.float16)])
+def test_blend_accumulate(cuda_lib, h, w, tile, ov, tile_dtype):
+    """Every tile of a split accumulated on the GPU equals the CPU weighted accumulation bit for
+    bit and the reference's sequential blend-and-trim restatement within fp32 rounding; the
+    canvas windows are strided views, the tiles strided channel slices of a larger tensor and the
+    widths ragged against the kernel's 128-wide pieces."""
+    from h3vae_b200 import kernels as K
+    from h3vae_b200 import tiling
+    plan = tiling.TilePlan.build(h, w, tile, ov, 1)
+    g = torch.Generator().manual_seed(h * w)
+    c, t = 3, 5
+    tiles, dev_tiles = {}, {}
+    for (i, j) in plan.tiles():
+        moments = (torch.randn(2 * c, t, plan.hs[i], plan.ws[j], generator=g) * 2).to(tile_dtype)
+        tiles[(i, j)] = moments[::2]
+        dev_tiles[(i, j)] = moments.cuda()[::2]   # strided: every other channel
+    ref = torch.zeros(2, c, t, plan.height, plan.width)
+    for (i, j), v in tiles.items():
+        tiling.accumulate_tile(ref[1], v, plan, i, j)
+    canvas = torch.zeros(2, c, t, plan.height, plan.width, device="cuda")
+    for (i, j), v in tiles.items():
+        y, x = plan.ys[i], plan.xs[j]
+        wmap = tiling.tile_weight_map(plan, i, j, torch.float32, "cuda")
+        K.blend_accumulate(canvas[1, :, :, y:y + plan.hs[i], x:x + plan.ws[j]], dev_tiles[(i, j)], wmap)
+    got = canvas.cpu()
+    assert torch.equal(got[0], torch.zeros_like(got[0]))
+    assert torch.equal(got[1], ref[1])
+    seq = tiling.blend_sequential({k: v.double() for k, v in tiles.items()}, plan)
+    assert torch.allclose(got[1].double(), seq, atol=1e-5, rtol=1e-5)
+
+
+def test_blend_accumulate_rejects_bad_arguments(cuda_lib):
+    from h3vae_b200 import kernels as K
+    canvas = torch.zeros(3, 2, 8, 8, device="cuda")
+    with pytest.raises(ValueError):
+        K.blend_accumulate(canvas, torch.zeros(3, 2, 8, 7, device="cuda"), torch.ones(8, 8, device="cuda"))
+    with pytest.raises(ValueError):
+        K.blend_accumulate(canvas, torch.zeros(3, 2, 8, 8, device="cuda"), torch.ones(8, 16, device="cuda")[:, ::2])
+    with pytest.raises(ValueError):
+        K.blend_accumulate(canvas.half(), torch.zeros(3, 2, 8, 8, device="cuda"), torch.ones(8, 8, device="cuda"))
