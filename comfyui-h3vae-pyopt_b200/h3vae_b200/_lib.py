@@ -57,6 +57,8 @@ _SIGNATURES = {
                             c_void_p, c_int64, c_void_p, c_void_p]),
     "h3b_gemm_i8_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                    c_void_p, c_void_p]),
+    "h3b_gemm_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
+    "h3b_gemm_f16_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "h3b_gemm_i8_qkv_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                      c_int64, c_void_p, c_void_p, c_int64, c_float, c_void_p, c_void_p, c_void_p,
                                      c_void_p]),

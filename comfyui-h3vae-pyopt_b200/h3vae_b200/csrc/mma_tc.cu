@@ -1,5 +1,5 @@
 // tcgen05 mainloop shared by the implicit-GEMM causal conv3d (INT8 and fp16
-// operands) and the decoder INT8 linears.
+// operands) and the decoder linears (INT8; fp16 for the fp16 decoder profile).
 //
 // Structure (one persistent CTA per SM, 10 warps):
 //   warp 0      TMA producer: MT A tiles (128 rows x 128 bytes of K each) and
@@ -270,7 +270,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const MmaParams p) {
   static_assert(MT == 1 || MT == 2, "one or two M tiles per CTA tile");
   static_assert(MT == 1 || EP == Epi::kConv || EP == Epi::kLinear, "paired M tiles: conv / linear epilogues only");
-  static_assert(!F16 || EP == Epi::kConv, "fp16 operands: conv epilogue only");
+  static_assert(!F16 || EP != Epi::kQkvRope, "fp16 operands: conv, linear and SwiGLU epilogues");
   constexpr int kKE = F16 ? 64 : 128;   // K elements per 128-byte k-block
   constexpr uint32_t kBTileBytes = BN * kBK;
   constexpr uint32_t kAStageBytes = MT * kATileBytes;
@@ -504,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t m_pre = 0;
       if constexpr (EP == Epi::kLinear || EP == Epi::kSwiGLU || EP == Epi::kQkvRope) {
         m_pre = static_cast<int64_t>(m_group * MT) * kBM + row;
-        if (MT == 1 && m_pre < p.M) sx_pre = __ldg(p.a_scale + m_pre);
+        if (!F16 && MT == 1 && m_pre < p.M) sx_pre = __ldg(p.a_scale + m_pre);
       }
       // tcgen05.ld is warp-collective and the barrier spans all epilogue warps:
       // they leave together if any thread's bounded wait gave up.
@@ -519,7 +519,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t t_row = t_acc + i * BN;
           const int64_t m = static_cast<int64_t>(m_group * MT + i) * kBM + row;
           const bool valid = m < p.M;
-          const float sx = MT == 1 ? sx_pre : (valid ? p.a_scale[m] : 0.0f);
+          const float sx = (F16 || MT == 1) ? sx_pre : (valid ? p.a_scale[m] : 0.0f);
           const bool vec_ok = (p.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0;
           const int64_t m_warp = m - lane;
           const int valid_rows = static_cast<int>(p.M - m_warp < 32 ? p.M - m_warp : 32);
@@ -532,16 +532,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int valid_cols = p.N - n0;
             if (valid_cols >= 32 && vec_ok && valid_rows > 0) {
               float v[32];
-              dequant_chunk<false>(r, sx, cw + c * 32, cb + c * 32, v);
+              dequant_chunk<F16>(r, sx, cw + c * 32, cb + c * 32, v);
               uint4 row[4];
               pack_row32(v, row);
               store_chunk32_staged(stage, row, p.out + m_warp * p.ldo + n0, p.ldo, valid_rows);
-              if (valid && p.acc_out != nullptr) store_acc_chunk(p.acc_out + m * p.N + n0, r, valid_cols);
+              if (!F16 && valid && p.acc_out != nullptr) store_acc_chunk(p.acc_out + m * p.N + n0, r, valid_cols);
             } else if (valid && valid_cols > 0) {
               float v[32];
-              dequant_chunk<false>(r, sx, cw + c * 32, cb + c * 32, v);
+              dequant_chunk<F16>(r, sx, cw + c * 32, cb + c * 32, v);
               store_row_chunk(p.out + m * p.ldo + n0, v, valid_cols, vec_ok);
-              if (p.acc_out != nullptr) store_acc_chunk(p.acc_out + m * p.N + n0, r, valid_cols);
+              if (!F16 && p.acc_out != nullptr) store_acc_chunk(p.acc_out + m * p.N + n0, r, valid_cols);
             }
           }
         }
@@ -614,8 +614,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const bool staged = valid_cols >= 32 && vec_ok && valid_rows > 0;
           if (staged || (valid && valid_cols > 0)) {
             float g[32], u[32];
-            dequant_chunk<false>(rg, sx, cw + c * 32, cb + c * 32, g);
-            dequant_chunk<false>(ru, sx, cw + BN / 2 + c * 32, cb + BN / 2 + c * 32, u);
+            dequant_chunk<F16>(rg, sx, cw + c * 32, cb + c * 32, g);
+            dequant_chunk<F16>(ru, sx, cw + BN / 2 + c * 32, cb + BN / 2 + c * 32, u);
 #pragma unroll
             for (int j = 0; j < 32; j += 2) {
               // gate and up rounded to fp16 (the linear's fp16 output), then
@@ -1014,6 +1014,36 @@ int make_gemm_maps(CUtensorMap* ma, CUtensorMap* mb, const int8_t* qa, int64_t M
                                 CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// fp16 operands: K elements of 2 bytes, the same 128-byte k-block boxes.
+int make_gemm_maps_f16(CUtensorMap* ma, CUtensorMap* mb, const void* a, int64_t M, int64_t K, const void* w,
+                       int64_t w_rows, int b_box_rows) {
+  uint64_t adims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(M)};
+  uint64_t astr[1] = {static_cast<uint64_t>(K) * 2};
+  uint32_t abox[2] = {kBK / 2, kBM};
+  uint32_t es[2] = {1, 1};
+  int rc = h3b_host::encode_tiled(ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a, adims, astr, abox, es,
+                                  CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  uint64_t bdims[2] = {static_cast<uint64_t>(K), static_cast<uint64_t>(w_rows)};
+  uint64_t bstr[1] = {static_cast<uint64_t>(K) * 2};
+  uint32_t bbox[2] = {kBK / 2, static_cast<uint32_t>(b_box_rows)};
+  return h3b_host::encode_tiled(mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, w, bdims, bstr, bbox, es,
+                                CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int check_gemm_f16(const void* a, const void* w, int64_t M, int64_t N, int64_t K, const char* name) {
+  if (!a || !w) return h3b_host::set_error(H3B_EINVAL, "%s: NULL operand", name);
+  if (M <= 0 || N <= 0 || K <= 0)
+    return h3b_host::set_error(H3B_EINVAL, "%s: empty problem M=%lld N=%lld K=%lld", name, (long long)M,
+                               (long long)N, (long long)K);
+  if (K % 8 != 0) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: K=%lld must be a multiple of 8", name, (long long)K);
+  if ((reinterpret_cast<uintptr_t>(a) & 15u) || (reinterpret_cast<uintptr_t>(w) & 15u))
+    return h3b_host::set_error(H3B_EINVAL, "%s: operands must be 16-byte aligned", name);
+  if (M > (int64_t(1) << 30) || N > (int64_t(1) << 30) || K > (int64_t(1) << 24))
+    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: problem too large for 32-bit tile indexing", name);
+  return H3B_OK;
+}
+
 int check_gemm_common(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale, int64_t M,
                       int64_t N, int64_t K, const char* name) {
   if (!qa || !a_scale || !qw || !w_scale) return h3b_host::set_error(H3B_EINVAL, "%s: NULL operand", name);
@@ -1305,6 +1335,55 @@ int h3b_gemm_i8_swiglu(const int8_t* qa, const float* a_scale, const int8_t* qw,
   rc = make_gemm_maps(&ma, &mb, qa, M, K, qw, 2 * F, 128);
   if (rc) return rc;
   return launch_mma<256, 4, AMode::kGemm2D, Epi::kSwiGLU>(ma, mb, p, reinterpret_cast<cudaStream_t>(stream), name);
+}
+
+int h3b_gemm_f16(const void* a, const void* w, const void* bias, int64_t M, int64_t N, int64_t K, void* out,
+                 int64_t ldo, h3b_stream_t stream) {
+  const char* name = "h3b_gemm_f16";
+  int rc = check_gemm_f16(a, w, M, N, K, name);
+  if (rc) return rc;
+  if (!out || ldo < N) return h3b_host::set_error(H3B_EINVAL, "%s: bad output", name);
+  MmaParams p{};
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.k_blocks = (int)((K + kBK / 2 - 1) / (kBK / 2));
+  p.m_tiles = (int)((M + kBM - 1) / kBM);
+  p.m_groups = p.m_tiles;
+  p.bias = static_cast<const __half*>(bias);
+  p.out = static_cast<__half*>(out); p.ldo = ldo;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  CUtensorMap ma, mb;
+  const int64_t tiles256 = p.m_tiles * ((N + 255) / 256);
+  if (N > 128 && tiles256 >= h3b_host::num_sms()) {
+    p.n_tiles = (int)((N + 255) / 256);
+    rc = make_gemm_maps_f16(&ma, &mb, a, M, K, w, N, 256);
+    if (rc) return rc;
+    return launch_mma<256, 4, AMode::kGemm2D, Epi::kLinear, 1, true>(ma, mb, p, st, name);
+  }
+  p.n_tiles = (int)((N + 127) / 128);
+  rc = make_gemm_maps_f16(&ma, &mb, a, M, K, w, N, 128);
+  if (rc) return rc;
+  return launch_mma<128, 6, AMode::kGemm2D, Epi::kLinear, 1, true>(ma, mb, p, st, name);
+}
+
+int h3b_gemm_f16_swiglu(const void* a, const void* w, const void* bias, int64_t M, int64_t F, int64_t K, void* act,
+                        h3b_stream_t stream) {
+  const char* name = "h3b_gemm_f16_swiglu";
+  int rc = check_gemm_f16(a, w, M, 2 * F, K, name);
+  if (rc) return rc;
+  if (!act) return h3b_host::set_error(H3B_EINVAL, "%s: NULL output", name);
+  MmaParams p{};
+  p.M = (int)M; p.N = (int)(2 * F); p.K = (int)K; p.F = (int)F;
+  p.k_blocks = (int)((K + kBK / 2 - 1) / (kBK / 2));
+  p.m_tiles = (int)((M + kBM - 1) / kBM);
+  p.m_groups = p.m_tiles;
+  p.n_tiles = (int)((F + 127) / 128);
+  p.bias = static_cast<const __half*>(bias);
+  p.out = static_cast<__half*>(act);
+  CUtensorMap ma, mb;
+  rc = make_gemm_maps_f16(&ma, &mb, a, M, K, w, 2 * F, 128);
+  if (rc) return rc;
+  return launch_mma<256, 4, AMode::kGemm2D, Epi::kSwiGLU, 1, true>(ma, mb, p, reinterpret_cast<cudaStream_t>(stream),
+                                                                   name);
 }
 
 int h3b_gemm_i8_qkv_rope(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale,

@@ -464,6 +464,51 @@ def gemm_i8_swiglu(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, 
     return act
 
 
+def _f16_operands(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None, rows: int) -> None:
+    _require(a, F16, "a")
+    _require(w, F16, "w")
+    _require(bias, F16, "bias")
+    if a.ndim != 2 or w.ndim != 2 or a.shape[1] != w.shape[1]:
+        raise ValueError("FP16 matrix dimensions do not match")
+    if a.shape[1] % 8 or a.data_ptr() % 16 or w.data_ptr() % 16:
+        raise ValueError("K must be a multiple of 8 and the operands 16-byte aligned")
+    if bias is not None and bias.numel() != rows:
+        raise ValueError("FP16 bias matching output channels required")
+
+
+def gemm_f16(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None, *,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """out[M,N] = fp16(a[M,K] @ w[N,K]^T + bias) with an fp32 accumulator (fp16 decoder profile linear)."""
+    dev = _require_cuda(a, w, bias, out)
+    _f16_operands(a, w, bias, w.shape[0])
+    m, k = a.shape
+    n = w.shape[0]
+    if out is None:
+        out = torch.empty((m, n), device=dev, dtype=F16)
+    elif out.dtype != F16 or out.shape != (m, n) or out.stride(1) != 1:
+        raise ValueError("out must be fp16 [M,N] with unit column stride")
+    _lib.check(_lib.load().h3b_gemm_f16(a.data_ptr(), w.data_ptr(), _ptr(bias), m, n, k, out.data_ptr(),
+                                        out.stride(0), _stream(dev)))
+    _count(1)
+    return out
+
+
+def gemm_f16_swiglu(a: torch.Tensor, w: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
+    """FFN-up fp16 GEMM with the SwiGLU epilogue: fp16 act [M, F] for a [2F, K] weight.
+    ref: opt/fp16_swiglu_gemm.py:66-80 (fused_w1_swiglu)."""
+    dev = _require_cuda(a, w, bias)
+    _f16_operands(a, w, bias, w.shape[0])
+    if w.shape[0] % 2:
+        raise ValueError("expected matching K and paired gate/up output rows")
+    m, k = a.shape
+    f = w.shape[0] // 2
+    act = torch.empty((m, f), device=dev, dtype=F16)
+    _lib.check(_lib.load().h3b_gemm_f16_swiglu(a.data_ptr(), w.data_ptr(), _ptr(bias), m, f, k, act.data_ptr(),
+                                               _stream(dev)))
+    _count(1)
+    return act
+
+
 def gemm_i8_qkv_rope(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, weight_scale: torch.Tensor,
                      bias: torch.Tensor | None, batch: int, tokens: int, heads: int, cos: torch.Tensor,
                      sin: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:

@@ -322,8 +322,9 @@ class _DecoderBlock:
 
 class H3Decoder:
     """Synthetic H3-structured decoder (random init, seeded).  int8=True runs the fused INT8 block
-    chain (the int8_decode + decode_fusions profile); int8=False runs the fp16 profile: cuBLAS fp16
-    linears and PyTorch SDPA around the fused QK RMSNorm + RoPE and RMSNorm kernels."""
+    chain (the int8_decode + decode_fusions profile); int8=False runs the fp16 profile: fp16
+    tcgen05 linears (the FFN-up with the fused SwiGLU epilogue of opt/fp16_swiglu_gemm.py), the
+    tcgen05 attention, and the fused QK RMSNorm + RoPE and RMSNorm kernels."""
 
     def __init__(self, cfg: DecoderConfig | None = None, device="cuda", seed: int = 1, int8: bool = True):
         self.cfg = cfg = cfg or DecoderConfig()
@@ -380,26 +381,23 @@ class H3Decoder:
                 sin.view(1, n, 1, -1).expand(b, n, 1, sin.shape[-1]).contiguous())
 
     def transformer_fp16(self, x: torch.Tensor, grid: tuple[int, int, int]) -> torch.Tensor:
-        """fp16 profile of the block chain (ref: opt/int8_norm_quant.py:106-124 block structure with
-        the fp16 linears of the default decoder)."""
+        """fp16 profile of the block chain (ref: opt/int8_norm_quant.py:106-124 block structure;
+        FFN-up + SwiGLU fused as opt/fp16_swiglu_gemm.py:94-110 FusedFP16FFN)."""
         cfg = self.cfg
         b, n, d = x.shape
         cos, sin = self._rope(b, *grid)
         x = x.reshape(b * n, d).contiguous()
         for blk in self.blocks:
             n1 = K.rms_norm_f16(x, blk.norm1_w, cfg.eps)
-            qkv = F.linear(n1, blk.qkv_w, blk.qkv_b).view(b, n, 3 * d)
+            qkv = K.gemm_f16(n1, blk.qkv_w, blk.qkv_b).view(b, n, 3 * d)
             q, k = K.qk_rope(qkv, cos, sin, cfg.heads, cfg.qk_eps)
             v = qkv.view(b, n, cfg.heads, 192)[..., 128:]
-            y = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2),
-                                               scale=1.0 / 8.0)
-            a = F.linear(y.transpose(1, 2).reshape(b * n, d), blk.out_w, blk.out_b)
+            y = K.attention_f16(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), 1.0 / 8.0)
+            a = K.gemm_f16(y.transpose(1, 2).reshape(b * n, d), blk.out_w, blk.out_b)
             h = torch.addcmul(x.float(), a.float(), blk.scale1.float()).half()
             n2 = K.rms_norm_f16(h, blk.norm2_w, cfg.eps)
-            ff = F.linear(n2, blk.up_w, blk.up_b).float()
-            g, u = ff[:, : cfg.ffn], ff[:, cfg.ffn:]
-            act = (g.half().float() * torch.sigmoid(g.half().float()) * u.half().float()).half()
-            out = F.linear(act, blk.down_w, blk.down_b)
+            act = K.gemm_f16_swiglu(n2, blk.up_w, blk.up_b)
+            out = K.gemm_f16(act, blk.down_w, blk.down_b)
             x = torch.addcmul(h.float(), out.float(), blk.scale2.float()).half()
         y = F.layer_norm(x.float(), (d,), self.ln_w.float(), self.ln_b.float(), cfg.eps).half()
         return y.view(b, n, d)

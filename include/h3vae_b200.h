@@ -244,6 +244,22 @@ int h3b_gemm_i8(const int8_t* qa, const float* a_scale, const int8_t* qw, const 
 int h3b_gemm_i8_swiglu(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale,
                        const void* bias, int64_t M, int64_t F, int64_t K, void* act, h3b_stream_t stream);
 
+/* fp16 decoder profile (decode_fusions without int8_decode): the same tcgen05
+ * GEMM with fp16 operands (kind::f16, fp32 accumulate).
+ *   h3b_gemm_f16:        out[m, n] = fp16(acc[m,n] + bias[n])
+ *   h3b_gemm_f16_swiglu: g = fp16(acc_g + b[j]), u = fp16(acc_u + b[F+j]),
+ *                        act[m, j] = fp16( g / (1 + exp(-g)) * u ) in fp32
+ * a fp16 [M,K] (row stride K), w fp16 [N,K] (SwiGLU: [2F,K], rows 0..F-1 gate,
+ * F..2F-1 up), bias fp16 or NULL, out fp16 with row stride ldo (SwiGLU: F).
+ * K % 8 == 0, a and w 16-byte aligned.
+ * ref: opt/fp16_swiglu_gemm.py:20-47 (w1_swiglu kernel: fp32 accumulate, bias,
+ *      fp16 rounding of gate/up, fp32 SwiGLU); the plain fp16 linears of the
+ *      same profile are the model's nn.Linear layers. */
+int h3b_gemm_f16(const void* a, const void* w, const void* bias, int64_t M, int64_t N, int64_t K, void* out,
+                 int64_t ldo, h3b_stream_t stream);
+int h3b_gemm_f16_swiglu(const void* a, const void* w, const void* bias, int64_t M, int64_t F, int64_t K, void* act,
+                        h3b_stream_t stream);
+
 /* QKV GEMM with the fused per-head QK RMSNorm + rotary epilogue.  qw rows are
  * laid out per head as [q(64) | k(64) | v(64)] (N = heads*192).  For each
  * token m = b*tokens + t and head h:

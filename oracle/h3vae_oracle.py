@@ -371,6 +371,24 @@ def ffn_up_swiglu(q, s, qweight, w_scale, bias=None) -> np.ndarray:
     return swiglu_act(lin[:, :f], lin[:, f:]).astype(F16)
 
 
+def linear_f16(a, w, bias=None) -> np.ndarray:
+    """fp16 linear with an fp32 accumulator: fp16(acc + bias[n]).  The dot product is taken in
+    float64 and rounded once to fp32 (a GPU's fp32 accumulation order differs by rounding only).
+    ref: opt/fp16_swiglu_gemm.py:35-41 (fp32 acc, fp32 bias add) for the fp16 profile's linears."""
+    acc = (np.asarray(a, np.float64) @ np.asarray(w, np.float64).T).astype(F32)
+    if bias is not None:
+        acc = acc + np.asarray(bias, F32).reshape(1, -1)
+    return acc.astype(F16)
+
+
+def ffn_up_swiglu_f16(a, w, bias=None) -> np.ndarray:
+    """fp16 FFN-up GEMM + SwiGLU: gate/up columns fp16(acc + bias), then fp32 silu(gate) * up rounded
+    once to fp16.  ref: opt/fp16_swiglu_gemm.py:35-47 (w1_swiglu kernel)."""
+    lin = linear_f16(a, w, bias).astype(F32)
+    f = lin.shape[1] // 2
+    return swiglu_act(lin[:, :f], lin[:, f:]).astype(F16)
+
+
 def residual_rms_quant(x, a, g, w, eps, round_stats=False):
     """raw = fma(a,g,x); h = fp16(raw); inv = rsqrt(sum(stat^2) * (1/K) + eps); act = fp16(h*inv*w);
     row quantization.  ref: opt/int8_norm_quant.py:23-44 (and opt/int8_norm1_producer.py:29-61)."""

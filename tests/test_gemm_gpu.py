@@ -1,5 +1,6 @@
-"""INT8 decoder GEMM family on the B200 vs the CPU oracle (CK contract restated from
-opt/int8_ffn_up_fused.py:76-90 and opt/decoder_fused_qk_rope.py:13-35).  int32 accumulators are
+"""Decoder GEMM family on the B200 vs the CPU oracle: INT8 (CK contract restated from
+opt/int8_ffn_up_fused.py:76-90 and opt/decoder_fused_qk_rope.py:13-35) and the fp16 profile
+(opt/fp16_swiglu_gemm.py:20-47).  int32 accumulators are
 bit-exact; fp16 outputs within max-abs 1e-2 / rel 1e-3."""
 import numpy as np
 import pytest
@@ -76,3 +77,51 @@ def test_qkv_rope(cuda_lib, batch, tokens, heads, k, r):
     _close(qo.permute(0, 2, 1, 3).cpu().numpy(), rq, atol=1e-2)
     _close(ko.permute(0, 2, 1, 3).cpu().numpy(), rk, atol=1e-2)
     _close(vo.permute(0, 2, 1, 3).cpu().numpy(), rv, atol=1e-2)
+
+
+def _f16_operands(rng, m, n, k):
+    a = rng.standard_normal((m, k)).astype(np.float16)
+    w = (rng.standard_normal((n, k)) / np.sqrt(k)).astype(np.float16)
+    b = (rng.standard_normal(n) * 0.5).astype(np.float16)
+    return a, w, b
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 1024, 1024), (17, 3072, 1024), (129, 2048, 2048), (300, 136, 256),
+                                   (4096, 1024, 4096), (200, 1000, 1000), (2048, 3072, 1024)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_gemm_f16(cuda_lib, m, n, k, with_bias):
+    """fp16 decoder-profile linear: fp16 outputs within max-abs 1e-2 / rel 1e-3 of the oracle (the
+    fp32 accumulation order differs); K and N ragged against the 64-element k-blocks and tiles."""
+    from h3vae_b200 import kernels as K
+    rng = np.random.default_rng(m * 7 + n + k)
+    a, w, b = _f16_operands(rng, m, n, k)
+    bias = b if with_bias else None
+    out = K.gemm_f16(torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda(),
+                     None if bias is None else torch.from_numpy(bias).cuda())
+    _close(out.cpu().numpy(), O.linear_f16(a, w, bias))
+
+
+@pytest.mark.parametrize("m,f,k", [(1, 4096, 1024), (129, 8192, 2048), (4096, 4096, 1024), (200, 136, 256),
+                                   (33, 200, 1000)])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_ffn_up_swiglu_f16(cuda_lib, m, f, k, with_bias):
+    from h3vae_b200 import kernels as K
+    rng = np.random.default_rng(m + f * 3 + k)
+    a, w, b = _f16_operands(rng, m, 2 * f, k)
+    bias = b if with_bias else None
+    act = K.gemm_f16_swiglu(torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda(),
+                            None if bias is None else torch.from_numpy(bias).cuda())
+    _close(act.cpu().numpy(), O.ffn_up_swiglu_f16(a, w, bias), atol=2e-2)
+
+
+def test_gemm_f16_rejects_bad_arguments(cuda_lib):
+    from h3vae_b200 import kernels as K
+    a = torch.zeros(4, 36, dtype=torch.float16, device="cuda")
+    with pytest.raises(ValueError):   # K not a multiple of 8
+        K.gemm_f16(a, torch.zeros(8, 36, dtype=torch.float16, device="cuda"))
+    with pytest.raises(ValueError):   # odd number of gate/up rows
+        K.gemm_f16_swiglu(torch.zeros(4, 64, dtype=torch.float16, device="cuda"),
+                          torch.zeros(7, 64, dtype=torch.float16, device="cuda"))
+    with pytest.raises(ValueError):   # int8 operand
+        K.gemm_f16(torch.zeros(4, 64, dtype=torch.int8, device="cuda"),
+                   torch.zeros(8, 64, dtype=torch.float16, device="cuda"))
