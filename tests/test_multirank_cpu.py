@@ -132,9 +132,10 @@ def _run(world, mode):
     return results
 
 
-def test_two_rank_encode_decode_equals_single_process():
-    rt.K.finalize_pixels = _cpu_finalize
-    rt.K.blend_accumulate = _cpu_blend
+def test_two_rank_encode_decode_equals_single_process(monkeypatch):
+    # CPU stand-ins for this test only (the spawned ranks set their own)
+    monkeypatch.setattr(rt.K, "finalize_pixels", _cpu_finalize)
+    monkeypatch.setattr(rt.K, "blend_accumulate", _cpu_blend)
     single = _make_runtime(None)
     video, lat = _inputs()
     enc_ref = single.encode(video)
