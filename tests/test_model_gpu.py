@@ -1,6 +1,7 @@
 """End-to-end runtime on the B200: a small H3-structured encoder/decoder, tiled encode/decode round
 trip through the public first_stage_model API, and the INT8 path against the fp16 path of the same
-weights (quality criterion: PSNR of INT8 vs fp16)."""
+weights (quality criterion: PSNR of INT8 vs fp16), and the fp16 profile's block chain against the
+oracle composition."""
 import math
 
 import pytest
@@ -58,3 +59,48 @@ def test_tiled_equals_untiled_blend_weights_sum_to_one():
     for i, j in plan.tiles():
         tiling.accumulate_tile(canvas, torch.ones(plan.hs[i], plan.ws[j], dtype=torch.float64), plan, i, j)
     assert torch.allclose(canvas, torch.ones_like(canvas))
+
+
+def _oracle_fp16_chain(dec, x, grid):
+    """The fp16 block chain composed from the oracle's restatements (rms_norm_f16, linear_f16,
+    qk_rope, attention, ffn_up_swiglu_f16), with the model's fp32 residual adds and final LayerNorm."""
+    import numpy as np
+    from oracle import h3vae_oracle as O
+    cfg = dec.cfg
+    b, n, d = x.shape
+    cos, sin = (t.cpu().numpy() for t in dec._rope(b, *grid))
+    npy = lambda t: t.detach().cpu().numpy()  # noqa: E731
+    xs = x.reshape(b * n, d).numpy()
+    for blk in dec.blocks:
+        n1 = O.rms_norm_f16(xs, npy(blk.norm1_w), cfg.eps)
+        qkv = O.linear_f16(n1, npy(blk.qkv_w), npy(blk.qkv_b)).reshape(b, n, 3 * d)
+        q, k, v = O.qk_rope(qkv, cos, sin, cfg.heads, cfg.qk_eps)
+        att = O.attention(q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3), 1.0 / 8.0)
+        y = att.transpose(0, 2, 1, 3).reshape(b * n, d).astype(np.float16)
+        a = O.linear_f16(y, npy(blk.out_w), npy(blk.out_b))
+        h = (xs.astype(np.float32) + a.astype(np.float32) * npy(blk.scale1).astype(np.float32)).astype(np.float16)
+        n2 = O.rms_norm_f16(h, npy(blk.norm2_w), cfg.eps)
+        act = O.ffn_up_swiglu_f16(n2, npy(blk.up_w), npy(blk.up_b))
+        o = O.linear_f16(act, npy(blk.down_w), npy(blk.down_b))
+        xs = (h.astype(np.float32) + o.astype(np.float32) * npy(blk.scale2).astype(np.float32)).astype(np.float16)
+    xf = xs.astype(np.float64)
+    mean, var = xf.mean(-1, keepdims=True), xf.var(-1, keepdims=True)
+    ln = (xf - mean) / np.sqrt(var + cfg.eps) * npy(dec.ln_w).astype(np.float64) + npy(dec.ln_b).astype(np.float64)
+    return ln.reshape(b, n, d)
+
+
+def test_fp16_block_chain_matches_oracle():
+    """The fp16 decoder profile's block chain (tcgen05 fp16 linears, fused FFN-up + SwiGLU, QK-norm +
+    RoPE, tcgen05 attention) against the oracle composition: relative L2 error below 1e-2 after two
+    blocks and the final LayerNorm (fp16 rounding points differ only by accumulation order)."""
+    from h3vae_b200.model import DecoderConfig, H3Decoder
+    cfg = DecoderConfig(hidden=256, heads=4, blocks=2, ffn=512, up_channels=(128,), up_spatial=(True,),
+                        up_temporal=(True,))
+    dec = H3Decoder(cfg, device="cuda", seed=3, int8=False)
+    grid = (2, 8, 16)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(2, 2 * 8 * 16, cfg.hidden, generator=g).half()
+    got = dec.transformer(x.cuda(), grid).double().cpu()
+    ref = torch.from_numpy(_oracle_fp16_chain(dec, x, grid))
+    rel = ((got - ref).norm() / ref.norm()).item()
+    assert rel < 1e-2, rel
