@@ -398,9 +398,8 @@ def main():
             t1 = torch.cuda.Event(enable_timing=True)
             t0.record(stream)
             lat = runtime.encode(host_video)
-            pix = runtime.decode(fp16(lat))
-            if rank == 0:
-                host_out.copy_(pix, non_blocking=True)
+            # the ComfyUI chunked-IO call: pixels land in the caller's pinned host buffer
+            runtime.decode(fp16(lat), output_buffer=host_out)
             t1.record(stream)
             torch.cuda.synchronize()
             e2e_ms.append(t0.elapsed_time(t1))

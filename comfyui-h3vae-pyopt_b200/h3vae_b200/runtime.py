@@ -381,6 +381,18 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         tasks = [(bi, c, i, j) for bi in range(b) for c in range(chunks) for (i, j) in lplan.tiles()]
         per_call = max(1, self.tile_batch)
         groups = tiling.batches(tasks, per_call)
+        frames = self._frames_from_tokens(t)
+        # A pinned host output buffer on one GPU: each temporal chunk is finalized and copied to the
+        # host on a side stream as soon as its last tile is blended (tasks run chunk by chunk), so the
+        # device->host transfer overlaps the decoding of the later chunks.
+        streamed = (output_buffer is not None and self.world == 1 and output_buffer.device.type == "cpu"
+                    and output_buffer.is_pinned() and output_buffer.dtype == torch.float32
+                    and output_buffer.is_contiguous()
+                    and tuple(output_buffer.shape) == (b, 3, frames, pplan.height, pplan.width))
+        copy_stream = torch.cuda.Stream(self.dev) if streamed else None
+        pending = {}
+        for (bi, c, _, _) in tasks:
+            pending[(bi, c)] = pending.get((bi, c), 0) + 1
         for k in tiling.shard_range(len(groups), self.world, self.rank):
             group = groups[k]
             lat = torch.cat([zn[bi:bi + 1, :, c * tpc:(c + 1) * tpc, lplan.ys[i]:lplan.ys[i] + lplan.hs[i],
@@ -390,11 +402,17 @@ class H3VAEPyOptRuntime(torch.nn.Module):
                 y0, x0 = pplan.ys[i], pplan.xs[j]
                 K.blend_accumulate(canvas[bi, :, c * fpc:(c + 1) * fpc, y0:y0 + pplan.hs[i], x0:x0 + pplan.ws[j]],
                                    pix[n], self._weights(pplan, i, j))
+                pending[(bi, c)] -= 1
+                if streamed and pending[(bi, c)] == 0:
+                    self._emit_chunk(canvas, bi, c * fpc, min((c + 1) * fpc, frames), output_buffer, copy_stream)
+        if streamed:
+            copy_stream.synchronize()
+            self._log_call("decode", t0)
+            return output_buffer
         self._reduce_to_rank0(canvas)
         if self.rank != 0:
             self._log_call("decode", t0)
             return None
-        frames = self._frames_from_tokens(t)
         dec = canvas[:, :, :frames]
         direct = (output_buffer is not None and output_buffer.shape == dec.shape
                   and output_buffer.dtype == torch.float32 and output_buffer.device == dec.device
@@ -409,6 +427,20 @@ class H3VAEPyOptRuntime(torch.nn.Module):
             out = pixels
         self._log_call("decode", t0)
         return out
+
+    def _emit_chunk(self, canvas, bi, f0, f1, host_out, copy_stream):
+        """Finalize frames [f0, f1) of batch entry bi into a device staging tensor and copy them to the
+        pinned host output on copy_stream (one contiguous copy per channel plane)."""
+        if f0 >= f1:
+            return
+        stage = K.finalize_pixels(canvas[bi:bi + 1, :, f0:f1], self._img_std.reshape(3), self._img_mean.reshape(3))
+        ready = torch.cuda.Event()
+        ready.record()
+        copy_stream.wait_event(ready)
+        with torch.cuda.stream(copy_stream):
+            for ch in range(3):
+                host_out[bi, ch, f0:f1].copy_(stage[0, ch], non_blocking=True)
+        stage.record_stream(copy_stream)
 
     def decode_tiled(self, z, **kwargs):
         return self.decode(z)

@@ -104,3 +104,16 @@ def test_fp16_block_chain_matches_oracle():
     ref = torch.from_numpy(_oracle_fp16_chain(dec, x, grid))
     rel = ((got - ref).norm() / ref.norm()).item()
     assert rel < 1e-2, rel
+
+
+def test_decode_into_pinned_host_buffer_streams_chunks():
+    """decode(output_buffer=<pinned host tensor>) finalizes and copies each temporal chunk on a side
+    stream while later chunks decode; the result equals the device-side decode bit for bit."""
+    torch.manual_seed(1)
+    rt = _small_runtime(True)
+    lat = torch.randn(1, 16, 2 * 9, 40, 72).half()   # 2 temporal chunks x 2x3 tiles, 3 tiles per call
+    ref = rt.decode(lat.cuda()).cpu()
+    buf = torch.empty(ref.shape, dtype=torch.float32).pin_memory()
+    res = rt.decode(lat, output_buffer=buf)
+    assert res is buf
+    assert torch.equal(buf, ref)
