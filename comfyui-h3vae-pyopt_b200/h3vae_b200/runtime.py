@@ -9,7 +9,7 @@ comfy.sd.VAE exactly like the reference (h3vae_runtime.py:720-806).
 B200 additions: the hot kernels are the sm_100a library (there is no torch.compile; the
 compile_* options are accepted and ignored), and the tile work can be sharded over the GPUs of
 one node: with a torch.distributed process group (one process per GPU) every rank runs the same
-encode/decode call, takes a contiguous block of the (tile, clip) batches, accumulates its tiles'
+encode/decode call, takes a contiguous block of the (clip batch, tile) work items, accumulates its tiles'
 blend contributions into a canvas, and one NCCL reduce sums the canvases on rank 0, which
 returns the result (other ranks return None).
 
@@ -302,10 +302,13 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         t0 = time.monotonic()
         if self.int8_encode and x is not None and x.dtype != torch.float16:
             raise RuntimeError("int8_encode requires FP16 pixel input; use the FP16 VAE dtype")
-        if self.rank == 0:
+        if self.rank == 0 and x.ndim == 4:
+            x = x.unsqueeze(2)
+        # A pinned host video on one GPU is uploaded clip batch by clip batch on a side stream, and
+        # the work items run clip-major, so the host->device copy overlaps the encoding.
+        streamed = (self.world == 1 and x.device.type == "cpu" and x.is_pinned() and x.is_contiguous())
+        if self.rank == 0 and not streamed:
             x = x.to(device=self.dev)
-            if x.ndim == 4:
-                x = x.unsqueeze(2)
         x = self._share_input(x)
         b, _, t, h, w = x.shape
         tile = tiling.select_encoder_tile(self.encoder_tile_size, h, w)
@@ -319,13 +322,19 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         tpc = self.tokens_per_clip
         lat = torch.zeros((b, self.latent_channels, clips * tpc, lplan.height, lplan.width), dtype=torch.float32,
                           device=self.dev)
-        # work items: (tile, group of clips), staged batch of clips per encoder call
-        items = []
-        for (i, j) in plan.tiles():
-            for cs in tiling.batches(list(range(clips)), self.encoder_staged_batch):
-                items.append((i, j, cs))
+        # work items: (staged batch of clips, tile), clip-major; the clip batches write disjoint
+        # latent frames, so each latent value still receives its tiles in row-major tile order
+        cbatches = tiling.batches(list(range(clips)), self.encoder_staged_batch)
+        items = [(g, i, j) for g in range(len(cbatches)) for (i, j) in plan.tiles()]
+        arrived = None
+        if streamed:
+            x, arrived = self._upload_clip_batches(x, cbatches, t)
         for k in tiling.shard_range(len(items), self.world, self.rank):
-            i, j, cs = items[k]
+            g, i, j = items[k]
+            cs = cbatches[g]
+            if arrived is not None and arrived[g] is not None:
+                torch.cuda.current_stream(self.dev).wait_event(arrived[g])
+                arrived[g] = None
             tile_px = x[..., plan.ys[i]:plan.ys[i] + plan.hs[i], plan.xs[j]:plan.xs[j] + plan.ws[j]]
             batch = []
             for bi in range(b):
@@ -352,6 +361,24 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         if self.rank != 0:
             return None
         return (lat - self.latents_mean.float()) / self.latents_std.float()
+
+    def _upload_clip_batches(self, x_host, cbatches, t):
+        """Issue the host->device copy of each clip batch's frames on a side stream (one contiguous
+        copy per (batch entry, channel) plane).  Returns the device video and one event per clip batch."""
+        x_dev = torch.empty(x_host.shape, dtype=x_host.dtype, device=self.dev)
+        copy_stream = torch.cuda.Stream(self.dev)
+        copy_stream.wait_stream(torch.cuda.current_stream(self.dev))
+        events = []
+        with torch.cuda.stream(copy_stream):
+            for cs in cbatches:
+                f0, f1 = cs[0] * CLIP_LENGTH, min((cs[-1] + 1) * CLIP_LENGTH, t)
+                for bi in range(x_host.shape[0]):
+                    for ch in range(x_host.shape[1]):
+                        x_dev[bi, ch, f0:f1].copy_(x_host[bi, ch, f0:f1], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(copy_stream)
+                events.append(ev)
+        return x_dev, events
 
     # -- decode ----------------------------------------------------------------
     @torch.no_grad()

@@ -117,3 +117,14 @@ def test_decode_into_pinned_host_buffer_streams_chunks():
     res = rt.decode(lat, output_buffer=buf)
     assert res is buf
     assert torch.equal(buf, ref)
+
+
+def test_encode_from_pinned_host_video_streams_clip_batches():
+    """encode(<pinned host video>) uploads clip batch by clip batch on a side stream while earlier
+    batches encode; the latents equal the encode of the same video already on the device."""
+    torch.manual_seed(2)
+    rt = _small_runtime(True, encoder_staged_batch=1)
+    video = (torch.rand(1, 3, 40, 96, 160) * 2 - 1).half()   # 3 clips, the last one padded
+    ref = rt.encode(video.cuda())
+    got = rt.encode(video.pin_memory())
+    assert torch.equal(got, ref)
