@@ -201,3 +201,52 @@ def test_oracle_per_token_quantization_known_answer():
     a = O.conv3d_per_token(qa, sc, qw, ws, (3, 3, 3)).astype(np.float32)
     b = O.conv_epilogue(O.conv3d_int_acc(qa, qw, (3, 3, 3)), np.float32(0.02), ws, None).astype(np.float32)
     assert np.allclose(a, b, atol=2e-3, rtol=2e-3)
+
+
+def _gated_decoder():
+    ff = torch.nn.Module()
+    ff.use_gated, ff.act_fn = True, torch.nn.SiLU()
+    ff.w1 = torch.nn.Linear(4, 16, dtype=torch.float16)
+    ff.w2 = torch.nn.Linear(8, 4, dtype=torch.float16)
+    block = torch.nn.Module()
+    block.ff, block.attn = ff, torch.nn.Identity()
+    raw = torch.nn.Module()
+    raw.transformer_blocks = torch.nn.ModuleList([block])
+    return raw.eval()
+
+
+def test_fp16_swiglu_mirror_module_swap():
+    """ref: tests/test_fp16_swiglu_gemm.py:15-27 (clone keeps the original and shares the weights;
+    training mode and non-SiLU FFNs are refused)."""
+    from h3vae_b200.opt.fp16_swiglu_gemm import FusedFP16FFN, clone_fp16_decoder
+    raw = _gated_decoder()
+    cand = clone_fp16_decoder(raw, (128, 64, 64, 4, 2))
+    assert not isinstance(raw.transformer_blocks[0].ff, FusedFP16FFN)
+    assert isinstance(cand.transformer_blocks[0].ff, FusedFP16FFN)
+    assert cand.transformer_blocks[0].ff.w1 is not raw.transformer_blocks[0].ff.w1
+    assert cand.transformer_blocks[0].ff.w1.weight is raw.transformer_blocks[0].ff.w1.weight
+    assert set(cand.state_dict()) == set(raw.state_dict())
+    raw.train()
+    with pytest.raises(ValueError):
+        clone_fp16_decoder(raw, (128, 64, 64, 4, 2))
+    raw.eval()
+    raw.transformer_blocks[0].ff.act_fn = torch.nn.GELU()
+    with pytest.raises(ValueError):
+        clone_fp16_decoder(raw, (128, 64, 64, 4, 2))
+
+
+def test_fp16_swiglu_mirror_guards():
+    """ref: tests/test_fp16_swiglu_gemm.py:29-42 (CPU tensors and every shape / dtype / config
+    violation raise ValueError before any launch)."""
+    from h3vae_b200.opt.fp16_swiglu_gemm import fused_w1_swiglu, validate
+    x = torch.ones(2, 4, dtype=torch.float16)
+    w = torch.ones(8, 4, dtype=x.dtype)
+    validate(x, w, None, (64, 64, 64, 4, 3))
+    with pytest.raises(ValueError, match="CUDA"):
+        fused_w1_swiglu(x, w)
+    for a, b, bias, c in [(x.float(), w, None, (64, 64, 64, 4, 3)), (x, w[:7], None, (64, 64, 64, 4, 3)),
+                          (x, w, torch.zeros(7, dtype=x.dtype), (64, 64, 64, 4, 3)),
+                          (x, w, None, (64, 64, 64, 1, 3)), (x, w, None, (64, 64, 64, 4)),
+                          (x[:0], w, None, (64, 64, 64, 4, 3))]:
+        with pytest.raises(ValueError):
+            validate(a, b, bias, c)
