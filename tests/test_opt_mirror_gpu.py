@@ -163,3 +163,29 @@ def test_finalize_pixels_mirror(cuda_lib):
         y = finalize_pixels(x.cuda(), std.cuda(), mean.cuda())
     ref = O.finalize_pixels(x.numpy(), std.numpy(), mean.numpy())
     np.testing.assert_array_equal(y.cpu().numpy(), ref)
+
+
+def test_fp16_swiglu_gemm_mirror(cuda_lib):
+    """torch.ops.h3vae_b200_fp16_exp.w1_swiglu (ref: opt/fp16_swiglu_gemm.py:83-86) on a 3-D
+    activation with a ragged F, and the FusedFP16FFN module swap (fused w1 + SwiGLU, the model's own
+    w2) against the oracle composition."""
+    from h3vae_b200.opt import fp16_swiglu_gemm as M
+    g = _gen(12)
+    x = torch.randn(3, 40, 256, generator=g).half()
+    w = (torch.randn(2 * 192, 256, generator=g) / 16).half()
+    b = (torch.randn(2 * 192, generator=g) * 0.5).half()
+    y = torch.ops.h3vae_b200_fp16_exp.w1_swiglu(x.cuda(), w.cuda(), b.cuda(), 64, 64, 64, 4, 3)
+    assert tuple(y.shape) == (3, 40, 192)
+    ref = O.ffn_up_swiglu_f16(x.reshape(-1, 256).numpy(), w.numpy(), b.numpy())
+    _close(y.reshape(-1, 192).cpu().numpy(), ref, atol=2e-2)
+    ff = torch.nn.Module()
+    ff.use_gated, ff.act_fn = True, torch.nn.SiLU()
+    ff.w1 = torch.nn.Linear(256, 384).half()
+    ff.w2 = torch.nn.Linear(192, 256).half()
+    fused = M.FusedFP16FFN(ff.eval(), (64, 64, 64, 4, 3)).cuda()
+    out = fused(x.cuda()).float().cpu()
+    act = O.ffn_up_swiglu_f16(x.reshape(-1, 256).numpy(), ff.w1.weight.detach().cpu().numpy(),
+                              ff.w1.bias.detach().cpu().numpy())
+    ref2 = torch.from_numpy(O.linear_f16(act, ff.w2.weight.detach().cpu().numpy(),
+                                         ff.w2.bias.detach().cpu().numpy()).astype(np.float32)).reshape(3, 40, 256)
+    assert ((out - ref2).norm() / ref2.norm()).item() < 1e-2
