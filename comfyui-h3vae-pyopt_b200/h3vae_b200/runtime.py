@@ -378,6 +378,9 @@ class H3VAEPyOptRuntime(torch.nn.Module):
                 ev = torch.cuda.Event()
                 ev.record(copy_stream)
                 events.append(ev)
+        # the allocator must not hand the block out again before the side-stream copies finish,
+        # also when an exception ends the encode before every event was waited on
+        x_dev.record_stream(copy_stream)
         return x_dev, events
 
     # -- decode ----------------------------------------------------------------
