@@ -118,12 +118,19 @@ def tile_weight_map(plan: TilePlan, i: int, j: int, dtype=torch.float32, device=
     m = torch.zeros(h, w, dtype=dtype, device=device)
     # own region: the vertical ramp, then the horizontal ramp over the blended tile
     m[:own_h, :own_w] = wy[:own_h, None] * wx[None, :own_w]
+    # A band reaches only as far as the neighbour's own trimmed part: when an overlap is larger
+    # than that part, the rest of the overlap is trimmed from the neighbour and belongs to the
+    # tile after it, which blends with the neighbour's raw tile, not with this one.
     # band below: this tile is the raw "upper" tile of (i+1, j)
     if o_down:
-        m[own_h:, :own_w] = (1 - _ramp(o_down, dtype, device))[:, None] * wx[None, :own_w]
+        next_h = plan.hs[i + 1] - (plan.oys[i + 1] if i + 1 < plan.rows - 1 else 0)
+        nd = min(o_down, next_h)
+        m[own_h:own_h + nd, :own_w] = (1 - _ramp(o_down, dtype, device))[:nd, None] * wx[None, :own_w]
     # band right: this tile is the raw "left" tile of (i, j+1), over that tile's whole trimmed height
     if o_right:
-        m[:own_h, own_w:] = (1 - _ramp(o_right, dtype, device))[None, :]
+        next_w = plan.ws[j + 1] - (plan.oxs[j + 1] if j + 1 < plan.cols - 1 else 0)
+        nr = min(o_right, next_w)
+        m[:own_h, own_w:own_w + nr] = (1 - _ramp(o_right, dtype, device))[None, :nr]
     return m
 
 

@@ -60,3 +60,30 @@ def test_shard_range_partitions(n, world):
         sizes.append(len(rr))
     assert seen == list(range(n))
     assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("seed", range(40))
+def test_random_plans_partition_unity_and_match_sequential_blend(seed):
+    """Randomized plans (tile, overlap, ratio, ragged sizes): the per-tile weights sum to one on every
+    canvas pixel and the weighted accumulation equals the reference's sequential blend-and-trim."""
+    rng = torch.Generator().manual_seed(1000 + seed)
+    ratio = [1, 2, 4, 8][int(torch.randint(0, 4, (1,), generator=rng))]
+    tile = ratio * int(torch.randint(8, 40, (1,), generator=rng))
+    ov = ratio * int(torch.randint(1, tile // ratio // 2 + 1, (1,), generator=rng))
+    h = ratio * int(torch.randint(1, 3 * tile // ratio, (1,), generator=rng))
+    w = ratio * int(torch.randint(1, 3 * tile // ratio, (1,), generator=rng))
+    if tile <= ov:
+        pytest.skip("tile must exceed the overlap")
+    plan = tiling.TilePlan.build(h, w, tile, ov, ratio) if (h > tile or w > tile) else \
+        tiling.TilePlan((0,), (h,), (), (0,), (w,), ())
+    assert plan.height == h and plan.width == w
+    ones = torch.zeros(h, w, dtype=torch.float64)
+    tiles = {}
+    for i, j in plan.tiles():
+        tiling.accumulate_tile(ones, torch.ones(plan.hs[i], plan.ws[j], dtype=torch.float64), plan, i, j)
+        tiles[(i, j)] = torch.randn(plan.hs[i], plan.ws[j], generator=rng, dtype=torch.float64)
+    assert torch.allclose(ones, torch.ones_like(ones), atol=1e-12)
+    canvas = torch.zeros(h, w, dtype=torch.float64)
+    for (i, j), t in tiles.items():
+        tiling.accumulate_tile(canvas, t, plan, i, j)
+    assert torch.allclose(canvas, tiling.blend_sequential(tiles, plan), atol=1e-12)
