@@ -502,3 +502,27 @@ def blend_linear(a: np.ndarray, b: np.ndarray, overlap: int, axis: int) -> np.nd
     sl_b[axis] = slice(0, overlap)
     b[tuple(sl_b)] = (a[tuple(sl_a)] * (1 - w) + b[tuple(sl_b)] * w).astype(b.dtype)
     return b
+
+
+def blend_tiles_sequential(tiles, y_overlaps, x_overlaps) -> np.ndarray:
+    """The reference's blend + trim + concatenate of a tile grid: tiles[i][j] raw [..., h, w];
+    each tile is blended with its RAW upper and left neighbours (linear ramp), then trimmed by
+    the overlap with its lower / right neighbour, and the rows are concatenated.
+    ref: h3vae_runtime.py:623-639."""
+    rows = []
+    n_rows, n_cols = len(tiles), len(tiles[0])
+    for i in range(n_rows):
+        row = []
+        for j in range(n_cols):
+            t = np.asarray(tiles[i][j])
+            if i:
+                t = blend_linear(tiles[i - 1][j], t, y_overlaps[i - 1], t.ndim - 2)
+            if j:
+                t = blend_linear(tiles[i][j - 1], t, x_overlaps[j - 1], t.ndim - 1)
+            if i < n_rows - 1:
+                t = t[..., : t.shape[-2] - y_overlaps[i], :]
+            if j < n_cols - 1:
+                t = t[..., : t.shape[-1] - x_overlaps[j]]
+            row.append(t)
+        rows.append(np.concatenate(row, axis=-1))
+    return np.concatenate(rows, axis=-2)

@@ -87,3 +87,27 @@ def test_random_plans_partition_unity_and_match_sequential_blend(seed):
     for (i, j), t in tiles.items():
         tiling.accumulate_tile(canvas, t, plan, i, j)
     assert torch.allclose(canvas, tiling.blend_sequential(tiles, plan), atol=1e-12)
+
+
+@pytest.mark.parametrize("seed", range(20))
+def test_weighted_accumulation_matches_oracle_blend(seed):
+    """The weighted per-tile accumulation (the product's blend, done on the device by
+    h3b_blend_accumulate) against the oracle's restatement of the reference's blend + trim on
+    random splits from the oracle's split_tiles."""
+    import numpy as np
+    from oracle import h3vae_oracle as O
+    rng = np.random.default_rng(seed)
+    tile = int(rng.integers(8, 96))
+    ov = int(rng.integers(1, tile))
+    h, w = int(rng.integers(tile + 1, 4 * tile)), int(rng.integers(1, 4 * tile))
+    ys, hs, oys = O.split_tiles(h, tile, ov, 1)
+    xs, ws, oxs = O.split_tiles(w, tile, ov, 1) if w > tile else ([0], [w], [])
+    assert [list(ys), list(hs), list(oys)] == [list(v) for v in tiling.split_tiles(h, tile, ov, 1)]
+    plan = tiling.TilePlan(tuple(ys), tuple(hs), tuple(oys), tuple(xs), tuple(ws), tuple(oxs))
+    raw = [[rng.standard_normal((2, hs[i], ws[j])) for j in range(len(xs))] for i in range(len(ys))]
+    ref = O.blend_tiles_sequential(raw, oys, oxs)
+    canvas = torch.zeros(2, plan.height, plan.width, dtype=torch.float64)
+    for i, j in plan.tiles():
+        tiling.accumulate_tile(canvas, torch.from_numpy(raw[i][j]), plan, i, j)
+    assert ref.shape == tuple(canvas.shape)
+    assert np.allclose(canvas.numpy(), ref, atol=1e-12)
