@@ -250,3 +250,45 @@ def test_fp16_swiglu_mirror_guards():
                           (x[:0], w, None, (64, 64, 64, 4, 3))]:
         with pytest.raises(ValueError):
             validate(a, b, bias, c)
+
+
+def test_oracle_fp16_block_chain_against_independent_fp32_torch():
+    """Pins the oracle composition that the fp16 block-chain GPU test compares against: the same
+    two blocks written independently in fp32 PyTorch (no fp16 rounding points) agree within 1e-3
+    relative L2."""
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parent))
+    from test_model_gpu import _oracle_fp16_chain
+
+    from h3vae_b200.model import DecoderConfig, H3Decoder
+    cfg = DecoderConfig(hidden=256, heads=4, blocks=2, ffn=512, up_channels=(128,), up_spatial=(True,),
+                        up_temporal=(True,))
+    dec = H3Decoder(cfg, device="cpu", seed=3, int8=False)
+    grid = (2, 8, 16)
+    x = torch.randn(2, 256, 256, generator=torch.Generator().manual_seed(9)).half()
+    ref = torch.from_numpy(_oracle_fp16_chain(dec, x, grid))
+    b, n, d = x.shape
+    cos, sin = (t.float() for t in dec._rope(b, *grid))
+    r = cos.shape[-1]
+    xs = x.float().reshape(b * n, d)
+
+    def rms(t, w):
+        return t * torch.rsqrt((t * t).mean(-1, keepdim=True) + cfg.eps) * w.float()
+
+    def norm_rope(v):
+        v = v * torch.rsqrt((v * v).mean(-1, keepdim=True) + cfg.qk_eps)
+        rot = torch.cat([-v[..., r // 2:r], v[..., : r // 2]], -1)
+        return torch.cat([v[..., :r] * cos + rot * sin, v[..., r:]], -1)
+
+    for blk in dec.blocks:
+        qkv = (rms(xs, blk.norm1_w) @ blk.qkv_w.float().T + blk.qkv_b.float()).view(b, n, cfg.heads, 3, 64)
+        q, k, v = norm_rope(qkv[:, :, :, 0]), norm_rope(qkv[:, :, :, 1]), qkv[:, :, :, 2]
+        p = torch.softmax(q.transpose(1, 2) @ k.transpose(1, 2).transpose(-1, -2) / 8, -1)
+        att = (p @ v.transpose(1, 2)).transpose(1, 2).reshape(b * n, d)
+        h = xs + (att @ blk.out_w.float().T + blk.out_b.float()) * blk.scale1.float()
+        ff = rms(h, blk.norm2_w) @ blk.up_w.float().T + blk.up_b.float()
+        g, u = ff[:, : cfg.ffn], ff[:, cfg.ffn:]
+        xs = h + ((g * torch.sigmoid(g) * u) @ blk.down_w.float().T + blk.down_b.float()) * blk.scale2.float()
+    y = torch.nn.functional.layer_norm(xs, (d,), dec.ln_w.float(), dec.ln_b.float(), cfg.eps).view(b, n, d)
+    assert ((y.double() - ref).norm() / ref.norm()).item() < 1e-3
