@@ -9,12 +9,11 @@ values so existing callers and saved prompts keep working; the sm_100a kernel pi
 """
 from __future__ import annotations
 
-import copy
-
 import torch
 from torch import nn
 
 from .. import kernels as K
+from ._containers import clone_containers
 
 _BM = (32, 64, 128, 256)
 _BN = (32, 64, 128)
@@ -88,22 +87,12 @@ class FusedFP16FFN(nn.Module):
         return self.w2(w1_swiglu(x, self.w1.weight, self.w1.bias, *self.config))
 
 
-def _share_tree(module: nn.Module) -> nn.Module:
-    """A new module tree of shallow copies: own parameter / buffer / child tables, same tensors."""
-    twin = copy.copy(module)
-    twin._parameters = type(module._parameters)(module._parameters)
-    twin._buffers = type(module._buffers)(module._buffers)
-    twin._modules = type(module._modules)(
-        (name, None if child is None else _share_tree(child)) for name, child in module._modules.items())
-    return twin
-
-
 def clone_fp16_decoder(raw, config):
     """The decoder with every transformer block's FFN replaced by FusedFP16FFN; the original module
     tree is left untouched and the weights are shared, not copied.  ref: opt/fp16_swiglu_gemm.py:113-124."""
     if raw.training:
         raise ValueError("eval decoder required")
-    result = _share_tree(raw)
+    result = clone_containers(raw)
     for block in result.transformer_blocks:
         block.ff = FusedFP16FFN(block.ff, config)
     return result

@@ -1,7 +1,10 @@
 """Residual + RMSNorm + rowwise INT8 (mirror of the reference's opt/int8_norm_quant.py)."""
 from __future__ import annotations
 
+import os
+
 import torch
+from torch import nn
 
 from .. import kernels as K
 from .int8_swiglu_fused import prequantized_linear
@@ -44,4 +47,66 @@ def _(x, a, g, w, qw, ws, bias, eps, warps):
     return torch.empty_like(x), x.new_empty((*x.shape[:-1], qw.shape[0]))
 
 
-__all__ = ["residual_quant", "residual_rms_linear", "validate"]
+class NormQuantBlock(nn.Module):
+    """A scaled residual decoder block whose residual add, RMSNorm and FFN run through the INT8
+    producers: h = fp16(fma(attn, scale1, x)), out = FFN(RMSNorm(h)), x' = h + out * scale2.  The
+    attention module is the block's own, called as attn(norm1(x), rotary_pos_emb, pack_info).
+    ref: opt/int8_norm_quant.py:87-124."""
+
+    def __init__(self, block, warps=8):
+        super().__init__()
+        if not isinstance(block.norm2, nn.RMSNorm) or not block.use_scale:
+            raise ValueError("scaled residual block with RMSNorm required")
+        if tuple(block.norm2.normalized_shape) != (2048,) or block.norm2.weight is None:
+            raise ValueError("affine RMSNorm width 2048 required")
+        self.norm1, self.norm2 = block.norm1, block.norm2
+        self.attn, self.ff = block.attn, block.ff
+        self.scale1, self.scale2 = block.scale1, block.scale2
+        self.warps = warps
+        self.fuse_ffn_up = self._fused_ffn_available()
+        self.train(block.training)
+
+    def _fused_ffn_available(self) -> bool:
+        from .int8_ffn_up_fused import supports_fused_ffn_up
+        return supports_fused_ffn_up(self.scale1.device)
+
+    def _apply(self, fn, recurse=True):
+        result = super()._apply(fn, recurse=recurse)
+        self.fuse_ffn_up = self._fused_ffn_available()
+        return result
+
+    def forward(self, hidden_states, rotary_pos_emb=None, pack_info=None):
+        if self.training or torch.is_grad_enabled():
+            raise RuntimeError("eval + inference/no_grad required")
+        pack_info = {} if pack_info is None else pack_info
+        normed = self.norm1(hidden_states.float()).to(hidden_states.dtype)
+        attn = self.attn(normed, rotary_pos_emb, pack_info)
+        w1, w2 = self.ff.w1, self.ff.w2
+        if self.fuse_ffn_up:
+            from .int8_ffn_up_fused import fused_residual_ffn
+            h, out = fused_residual_ffn(hidden_states, attn, self.scale1, self.norm2.weight, w1.qweight,
+                                        w1.weight_scale, w1.bias, w2.qweight, w2.weight_scale, w2.bias,
+                                        self.norm2.eps, self.warps)
+        else:
+            from .int8_swiglu_fused import swiglu_int8_linear
+            h, hidden = residual_rms_linear(hidden_states, attn, self.scale1, self.norm2.weight, w1.qweight,
+                                            w1.weight_scale, w1.bias, self.norm2.eps, self.warps)
+            out = swiglu_int8_linear(hidden, w2.qweight, w2.weight_scale, w2.bias, 16)
+        return h + out * self.scale2
+
+
+def clone_norm_quant_decoder(raw, warps=8):
+    """Container clone of an INT8both decoder with fused FFNs and every block a NormQuantBlock.
+    ref: opt/int8_norm_quant.py:127-136."""
+    if os.environ.get("MINIMAX_H3_VAE_DECODER_VIT_FP32_NORM", "1").lower() not in ("1", "true", "yes", "on"):
+        raise ValueError("experimental fusion requires FP32 norm enabled")
+    if warps not in (4, 8, 16):
+        raise ValueError("unsupported warp count")
+    from .int8_swiglu_fused import clone_fused_decoder
+    result = clone_fused_decoder(raw, 16)
+    result.transformer_blocks = nn.ModuleList(
+        [NormQuantBlock(block, warps).eval() for block in result.transformer_blocks])
+    return result
+
+
+__all__ = ["NormQuantBlock", "clone_norm_quant_decoder", "residual_quant", "residual_rms_linear", "validate"]

@@ -3,6 +3,7 @@ opt/int8_swiglu_fused.py; the CK cutlass_int8_dequant call becomes the tcgen05 G
 from __future__ import annotations
 
 import torch
+from torch import nn
 
 from .. import kernels as K
 
@@ -52,4 +53,36 @@ def _(x, weight, weight_scale, bias, warps):
     return x.new_empty((*x.shape[:-1], weight.shape[0]))
 
 
-__all__ = ["quantize_swiglu", "prequantized_linear", "swiglu_int8_linear", "validate_input"]
+class FusedFFN(nn.Module):
+    """An INT8both FFN whose SwiGLU, activation quantization and w2 GEMM run as one op after w1.
+    ref: opt/int8_swiglu_fused.py:124-138."""
+
+    def __init__(self, original, warps=8):
+        super().__init__()
+        if getattr(original, "mode", None) != "INT8both":
+            raise ValueError("requires an existing INT8both FFN")
+        self.w1, self.w2 = original.w1, original.w2
+        self.warps = warps
+        self.train(original.training)
+
+    def forward(self, x):
+        if self.training or torch.is_grad_enabled():
+            raise RuntimeError("eval + no_grad/inference_mode required")
+        return swiglu_int8_linear(self.w1(x), self.w2.qweight, self.w2.weight_scale, self.w2.bias, self.warps)
+
+
+def clone_fused_decoder(raw, warps=8):
+    """A container clone of `raw` (weights shared) with every block's FFN wrapped in FusedFFN.
+    ref: opt/int8_swiglu_fused.py:141-155."""
+    from ._containers import clone_containers, require_backend
+    require_backend()
+    if raw.training:
+        raise ValueError("decoder.eval() required")
+    result = clone_containers(raw)
+    for block in result.transformer_blocks:
+        block.ff = FusedFFN(block.ff, warps).eval()
+    return result
+
+
+__all__ = ["FusedFFN", "clone_fused_decoder", "quantize_swiglu", "prequantized_linear", "swiglu_int8_linear",
+           "validate_input"]

@@ -59,6 +59,7 @@ class KitchenInt8Linear(nn.Module):
         self.bias = original.bias
         self.in_features, self.out_features = original.in_features, original.out_features
         self.source_dtype = original.weight.dtype
+        self.extra_weight_bytes = q.numel() * q.element_size() + s.numel() * s.element_size()
         self.train(original.training)
 
     def _apply(self, fn, recurse=True):
@@ -79,4 +80,63 @@ class KitchenInt8Linear(nn.Module):
         return int8_linear(x, self.qweight, self.weight_scale, self.bias)
 
 
-__all__ = ["KitchenInt8Linear", "int8_linear", "quantize_static_weight"]
+class KitchenInt8FFN(nn.Module):
+    """Gated SiLU FFN with w1 and/or w2 as static-weight INT8 linears (modes INT8both, INT8w1,
+    INT8w2); the branch not selected keeps the source linear.  ref: opt/kitchen_int8.py:222-280."""
+
+    MODES = frozenset(("INT8both", "INT8w1", "INT8w2"))
+
+    def __init__(self, original: nn.Module, mode: str = "INT8both", *, quantize_fn=None,
+                 require_cuda: bool = False):
+        super().__init__()
+        if mode not in self.MODES:
+            raise ValueError(f"unsupported INT8 FFN mode: {mode}")
+        if not bool(getattr(original, "use_gated", False)):
+            raise ValueError("kitchen INT8 experiment requires a gated FFN")
+        if not isinstance(getattr(original, "act_fn", None), nn.SiLU):
+            raise ValueError("kitchen INT8 experiment requires a SiLU FFN")
+        for name in ("w1", "w2"):
+            if not isinstance(getattr(original, name, None), nn.Linear):
+                raise ValueError(f"kitchen INT8 FFN requires an nn.Linear {name}")
+
+        def convert(linear, selected):
+            if not selected:
+                return linear
+            return KitchenInt8Linear(linear, quantize_fn=quantize_fn, require_cuda=require_cuda)
+
+        self.mode = mode
+        self.use_gated = True
+        self.act_fn = original.act_fn
+        self.w1 = convert(original.w1, mode in ("INT8both", "INT8w1"))
+        self.w2 = convert(original.w2, mode in ("INT8both", "INT8w2"))
+        self.train(original.training)
+
+    @property
+    def extra_weight_bytes(self) -> int:
+        return sum(getattr(m, "extra_weight_bytes", 0) for m in (self.w1, self.w2))
+
+    def forward(self, hidden_states: torch.Tensor) -> torch.Tensor:
+        gate, up = self.w1(hidden_states).chunk(2, dim=-1)
+        return self.w2(self.act_fn(gate) * up)
+
+
+def install_kitchen_int8_ffn(decoder: nn.Module, mode: str = "INT8both", *, require_cuda: bool = True) -> int:
+    """Replace every transformer block's FFN of `decoder` in place (the caller owns any clone);
+    all blocks are converted before the first assignment, so a block that fails validation leaves
+    the decoder unchanged.  Returns the number of FFNs replaced.  ref: opt/kitchen_int8.py:283-310."""
+    if decoder.training:
+        raise ValueError("kitchen INT8 candidate requires decoder.eval()")
+    blocks = getattr(decoder, "transformer_blocks", None)
+    if blocks is None:
+        raise ValueError("decoder has no transformer_blocks")
+    from ._containers import require_backend
+    require_backend()
+    replacements = [KitchenInt8FFN(block.ff, mode, require_cuda=require_cuda) for block in blocks]
+    for block, replacement in zip(blocks, replacements):
+        block.ff = replacement
+    decoder._h3vae_kitchen_int8_ffn_mode = mode
+    return len(replacements)
+
+
+__all__ = ["KitchenInt8FFN", "KitchenInt8Linear", "install_kitchen_int8_ffn", "int8_linear",
+           "quantize_static_weight"]

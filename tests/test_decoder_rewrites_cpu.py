@@ -1,0 +1,188 @@
+"""CPU contracts of the decoder-rewrite helpers in h3vae_b200.opt (INT8 FFN install, fused FFN,
+norm-quant blocks, INT8 QKV and attention-out projections, container cloning), following the
+reference's tests/test_int8_swiglu_fused.py, test_int8_norm_quant.py, test_int8_qkv.py,
+test_int8_attention_out.py and test_kitchen_int8.py:105-127.  The rewritten modules' forward passes
+run the ops that the GPU tests cover."""
+import copy
+from unittest.mock import patch
+
+import pytest
+import torch
+
+from h3vae_b200.opt import int8_attention_out, int8_norm_quant, int8_qkv, int8_swiglu_fused, kitchen_int8
+from h3vae_b200.opt._containers import clone_containers, selected_indices
+
+
+def _attn_block(width=2048):
+    block = torch.nn.Module()
+    block.attn = torch.nn.Module()
+    block.attn.original = torch.nn.Module()
+    block.attn.original.to_qkv = torch.nn.Linear(width, width * 3, device="meta")
+    block.attn.original.to_out = torch.nn.Linear(width, width, device="meta")
+    return block.eval()
+
+
+def _int8both_ff():
+    ff = torch.nn.Module()
+    ff.mode = "INT8both"
+    ff.w1 = torch.nn.Linear(4, 8)
+    ff.w2 = torch.nn.Linear(4, 4)
+    return ff
+
+
+def test_selected_indices():
+    """ref: tests/test_int8_qkv.py:10-14."""
+    assert selected_indices(36) == tuple(range(36))
+    assert selected_indices(36, [3, 7]) == (3, 7)
+    for bad in ([], [1, 1], [-1], [36], [True], [1.0]):
+        with pytest.raises(ValueError):
+            selected_indices(36, bad)
+
+
+def test_fused_ffn_requires_quantized_ffn_and_clone_isolates():
+    """ref: tests/test_int8_swiglu_fused.py:20-40."""
+    with pytest.raises(ValueError):
+        int8_swiglu_fused.FusedFFN(torch.nn.Linear(4, 4))
+    raw = torch.nn.Module()
+    block = torch.nn.Module()
+    ff = _int8both_ff()
+    block.ff = ff
+    block.register_module("absent", None)
+    raw.transformer_blocks = torch.nn.ModuleList([block])
+    raw.eval()
+    clone = int8_swiglu_fused.clone_fused_decoder(raw)
+    assert raw.transformer_blocks[0].ff is ff
+    assert clone.transformer_blocks[0] is not block
+    assert clone.transformer_blocks[0].ff.w1.weight is ff.w1.weight
+    assert clone.transformer_blocks[0].absent is None
+    with pytest.raises(RuntimeError):   # grad mode is on: inference only
+        clone.transformer_blocks[0].ff(torch.zeros(2, 4))
+    raw.train()
+    with pytest.raises(ValueError):
+        int8_swiglu_fused.clone_fused_decoder(raw)
+
+
+def test_norm_quant_clone_contracts(monkeypatch):
+    """ref: tests/test_int8_norm_quant.py:29-59."""
+    monkeypatch.setenv("MINIMAX_H3_VAE_DECODER_VIT_FP32_NORM", "0")
+    with pytest.raises(ValueError):
+        int8_norm_quant.clone_norm_quant_decoder(torch.nn.Module().eval())
+    monkeypatch.setenv("MINIMAX_H3_VAE_DECODER_VIT_FP32_NORM", "1")
+    with pytest.raises(ValueError):
+        int8_norm_quant.clone_norm_quant_decoder(torch.nn.Module().eval(), 3)
+    raw = torch.nn.Module()
+    block = torch.nn.Module()
+    block.use_scale = True
+    block.norm1 = torch.nn.RMSNorm(2048).half()
+    block.norm2 = torch.nn.RMSNorm(2048, eps=1e-5).half()
+    block.attn = torch.nn.Identity()
+    block.scale1 = torch.nn.Parameter(torch.ones(2048, dtype=torch.float16))
+    block.scale2 = torch.nn.Parameter(torch.ones(2048, dtype=torch.float16))
+    ff = _int8both_ff()
+    block.ff = ff
+    raw.transformer_blocks = torch.nn.ModuleList([block])
+    raw.eval()
+    result = int8_norm_quant.clone_norm_quant_decoder(raw)
+    assert raw.transformer_blocks[0] is block
+    assert isinstance(result.transformer_blocks[0], int8_norm_quant.NormQuantBlock)
+    assert result.transformer_blocks[0].scale1 is block.scale1
+    assert result.transformer_blocks[0].ff.w1.weight is ff.w1.weight
+    assert result.transformer_blocks[0].fuse_ffn_up is False   # CPU parameters
+    with pytest.raises(RuntimeError):
+        result.transformer_blocks[0](torch.zeros(2, 2048))
+    block.norm2 = torch.nn.RMSNorm(1024, eps=1e-5).half()
+    with pytest.raises(ValueError):
+        int8_norm_quant.NormQuantBlock(block)
+
+
+def test_qkv_linear_validation_and_replacement_scope():
+    """ref: tests/test_int8_qkv.py:16-49."""
+    block = _attn_block()
+    assert int8_qkv.qkv_linear(block)[1] is block.attn.original.to_qkv
+    block.train()
+    with pytest.raises(ValueError):
+        int8_qkv.qkv_linear(block)
+    with pytest.raises(ValueError):
+        int8_qkv.qkv_linear(_attn_block(128))
+    raw = torch.nn.Module()
+    raw.transformer_blocks = torch.nn.ModuleList([_attn_block(), _attn_block()])
+    raw.eval()
+    clone = copy.deepcopy(raw)
+    replacement = torch.nn.Identity()
+    with patch.object(int8_qkv, "clone_norm_quant_decoder", return_value=clone), \
+            patch.object(int8_qkv, "KitchenInt8Linear", return_value=replacement) as factory:
+        result = int8_qkv.clone_qkv_int8_decoder(raw, indices=[1])
+    assert isinstance(raw.transformer_blocks[1].attn.original.to_qkv, torch.nn.Linear)
+    assert isinstance(result.transformer_blocks[0].attn.original.to_qkv, torch.nn.Linear)
+    assert result.transformer_blocks[1].attn.original.to_qkv is replacement
+    assert factory.call_count == 1 and factory.call_args.kwargs["require_cuda"]
+
+
+def test_attention_out_validation_containers_and_scope():
+    """ref: tests/test_int8_attention_out.py:18-60."""
+    block = _attn_block()
+    assert int8_attention_out.out_linear(block)[1] is block.attn.original.to_out
+    block.train()
+    with pytest.raises(ValueError):
+        int8_attention_out.out_linear(block)
+    with pytest.raises(ValueError):
+        int8_attention_out.out_linear(_attn_block(128))
+    block = _attn_block()
+    block.attn.original.to_out = torch.nn.Identity()
+    with pytest.raises(ValueError):
+        int8_attention_out.out_linear(block)
+    raw = _attn_block()
+    raw.alias = raw.attn
+    raw.register_buffer("probe", torch.ones(2))
+    clone = clone_containers(raw)
+    assert clone.attn is not raw.attn and clone.alias is clone.attn
+    assert clone.probe is raw.probe
+    assert clone.attn.original.to_out.weight is raw.attn.original.to_out.weight
+    clone.probe = torch.zeros(2)
+    assert torch.equal(raw.probe, torch.ones(2))
+    raw = torch.nn.Module()
+    raw.transformer_blocks = torch.nn.ModuleList([_attn_block(), _attn_block()])
+    raw.eval()
+    replacement = torch.nn.Identity()
+    with patch.object(int8_attention_out, "KitchenInt8Linear", return_value=replacement) as factory:
+        result = int8_attention_out.clone_attention_out_decoder(raw, indices=[1])
+    for i in range(2):
+        assert isinstance(raw.transformer_blocks[i].attn.original.to_out, torch.nn.Linear)
+        assert (result.transformer_blocks[i].attn.original.to_qkv.weight
+                is raw.transformer_blocks[i].attn.original.to_qkv.weight)
+    assert isinstance(result.transformer_blocks[0].attn.original.to_out, torch.nn.Linear)
+    assert result.transformer_blocks[1].attn.original.to_out is replacement
+    assert factory.call_count == 1 and factory.call_args.kwargs["require_cuda"]
+
+
+def test_kitchen_int8_ffn_modes_and_install():
+    """ref: tests/test_kitchen_int8.py:105-127 (only the selected branch is replaced; inference only)
+    and opt/kitchen_int8.py:283-310 (install validates every block before assigning)."""
+    def gated():
+        ff = torch.nn.Module()
+        ff.use_gated, ff.act_fn = True, torch.nn.SiLU()
+        ff.w1 = torch.nn.Linear(64, 128).half()
+        ff.w2 = torch.nn.Linear(64, 64).half()
+        return ff.eval()
+    source = gated()
+    cand = kitchen_int8.KitchenInt8FFN(source, "INT8w1").eval()
+    assert isinstance(cand.w1, kitchen_int8.KitchenInt8Linear) and cand.w2 is source.w2
+    assert cand.extra_weight_bytes == 128 * 64 + 128 * 4
+    cand = kitchen_int8.KitchenInt8FFN(source, "INT8w2").eval()
+    assert cand.w1 is source.w1 and isinstance(cand.w2, kitchen_int8.KitchenInt8Linear)
+    with pytest.raises(ValueError):
+        kitchen_int8.KitchenInt8FFN(source, "INT4")
+    with pytest.raises(RuntimeError):
+        kitchen_int8.KitchenInt8FFN(source).eval()(torch.zeros(2, 64, dtype=torch.float16))
+    decoder = torch.nn.Module()
+    blocks = [torch.nn.Module(), torch.nn.Module()]
+    blocks[0].ff, blocks[1].ff = gated(), torch.nn.Linear(4, 4)   # the second block is not a gated FFN
+    decoder.transformer_blocks = torch.nn.ModuleList(blocks)
+    decoder.eval()
+    original = decoder.transformer_blocks[0].ff
+    with pytest.raises(ValueError):
+        kitchen_int8.install_kitchen_int8_ffn(decoder, require_cuda=False)
+    assert decoder.transformer_blocks[0].ff is original     # nothing assigned
+    decoder.transformer_blocks[1].ff = gated()
+    assert kitchen_int8.install_kitchen_int8_ffn(decoder, require_cuda=False) == 2
+    assert all(isinstance(b.ff, kitchen_int8.KitchenInt8FFN) for b in decoder.transformer_blocks)
