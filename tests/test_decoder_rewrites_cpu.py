@@ -186,3 +186,53 @@ def test_kitchen_int8_ffn_modes_and_install():
     decoder.transformer_blocks[1].ff = gated()
     assert kitchen_int8.install_kitchen_int8_ffn(decoder, require_cuda=False) == 2
     assert all(isinstance(b.ff, kitchen_int8.KitchenInt8FFN) for b in decoder.transformer_blocks)
+
+
+def _qk_attention(**overrides):
+    attn = torch.nn.Module()
+    attn.spatial_parallel = False
+    attn.norm_q = torch.nn.RMSNorm(64, eps=1e-6, elementwise_affine=False)
+    attn.norm_k = torch.nn.RMSNorm(64, eps=1e-6, elementwise_affine=False)
+    attn.dim_head, attn.heads = 64, 2
+    attn.to_qkv = torch.nn.Linear(128, 384)
+    attn.to_out = torch.nn.Linear(128, 128)
+    for k, v in overrides.items():
+        setattr(attn, k, v)
+    return attn.eval()
+
+
+def test_qk_fusion_validation_delegation_and_clone(monkeypatch):
+    """The fused-QK attention accepts only single-device, unaffined equal-eps RMSNorm QK norms with
+    64-wide heads; without rotary tables it runs the original module; the clone leaves the caller's
+    blocks untouched (ref: opt/decoder_fused_qk_rope.py:55-89)."""
+    from h3vae_b200.opt.decoder_fused_qk_rope import FusedQKAttention, clone_with_qk_fusion
+    for bad in (dict(spatial_parallel=True), dict(norm_q=torch.nn.LayerNorm(64)), dict(dim_head=128),
+                dict(norm_k=torch.nn.RMSNorm(64, eps=1e-5, elementwise_affine=False)),
+                dict(norm_q=torch.nn.RMSNorm(64, eps=1e-6))):
+        with pytest.raises(ValueError):
+            FusedQKAttention(_qk_attention(**bad))
+    calls = []
+
+    class Recording(torch.nn.Module):
+        def forward(self, x, rotary, pack_info):
+            calls.append((rotary, pack_info))
+            return x
+
+    attn = _qk_attention()
+    attn.forward = Recording().forward
+    fused = FusedQKAttention(attn)
+    x = torch.zeros(1, 3, 128)
+    assert fused(x) is x and calls == [(None, {})]
+    raw = torch.nn.Module()
+    block = torch.nn.Module()
+    block.attn = _qk_attention()
+    raw.transformer_blocks = torch.nn.ModuleList([block])
+    raw.eval()
+    result = clone_with_qk_fusion(raw)
+    assert raw.transformer_blocks[0] is block and isinstance(block.attn, torch.nn.Module)
+    assert not isinstance(block.attn, FusedQKAttention)
+    assert isinstance(result.transformer_blocks[0].attn, FusedQKAttention)
+    assert result.transformer_blocks[0].attn.original is block.attn
+    monkeypatch.setenv("MINIMAX_H3_VAE_DECODER_VIT_FP32_NORM", "0")
+    with pytest.raises(ValueError):
+        clone_with_qk_fusion(raw)
