@@ -236,3 +236,77 @@ def test_qk_fusion_validation_delegation_and_clone(monkeypatch):
     monkeypatch.setenv("MINIMAX_H3_VAE_DECODER_VIT_FP32_NORM", "0")
     with pytest.raises(ValueError):
         clone_with_qk_fusion(raw)
+
+
+def test_final_norm_adapter_shares_parameters_and_keeps_tensor_path():
+    """ref: tests/test_int8_norm1_quant.py:33-64."""
+    from h3vae_b200.opt import int8_norm1_quant as norm1
+    source = torch.nn.LayerNorm(2048, eps=1e-5, dtype=torch.float16).eval()
+    adapter = norm1._FinalNormAdapter(source).eval()
+    assert set(adapter.state_dict()) == set(source.state_dict())
+    assert adapter.weight is source.weight and adapter.bias is source.bias
+    with torch.inference_mode():
+        x = torch.randn(2, 7, 2048, dtype=torch.float16)
+        assert torch.equal(adapter(x), source(x))
+        adapter.to(dtype=torch.float32)
+        assert adapter.weight is source.weight
+        assert torch.equal(adapter(x.float()), source(x.float()))
+    adapter = norm1._FinalNormAdapter(torch.nn.LayerNorm(2048, eps=1e-5, dtype=torch.float16).eval()).eval()
+    old = torch.__future__.get_overwrite_module_params_on_conversion()
+    try:
+        torch.__future__.set_overwrite_module_params_on_conversion(True)
+        adapter.to(dtype=torch.float32)
+    finally:
+        torch.__future__.set_overwrite_module_params_on_conversion(old)
+    with torch.inference_mode():
+        y = adapter(torch.randn(2, 7, 2048))
+    assert y.dtype == torch.float32 and bool(torch.isfinite(y).all())
+
+
+def test_carry_safe_unpad():
+    """ref: tests/test_int8_norm1_quant.py:77-93."""
+    from unittest.mock import Mock
+
+    from h3vae_b200.opt import int8_norm1_quant as norm1
+    original = Mock(side_effect=lambda states, pad: states)
+    unpad = norm1._carry_safe_unpad(original)
+    carry = (object(), object(), object())
+    assert unpad(carry, 0) is carry
+    original.reset_mock()
+    with pytest.raises(RuntimeError, match="zero sequence padding"):
+        unpad(carry, 1)
+    original.assert_not_called()
+    tensor = torch.empty(2, 5, 3)
+    assert unpad(tensor, 1) is tensor
+    original.assert_called_once_with(tensor, 1)
+    with pytest.raises(RuntimeError, match="preserve final residual carry"):
+        norm1._carry_safe_unpad(lambda s, p: tuple(list(s)))((object(), object(), object()), 0)
+
+
+def test_norm1_device_gate_and_clone_guards():
+    """The chain runs on sm_100 only (ref: tests/test_int8_norm1_quant.py:95-103, with this build's
+    gate); the clone refuses training decoders and wrong block counts and, disabled, returns a plain
+    container clone (ref: opt/int8_norm1_quant.py:282-296)."""
+    from h3vae_b200.opt import int8_norm1_quant as norm1
+    assert norm1.supports_norm1_quant("cpu") is False
+    for capability, expected in (((10, 0), True), ((12, 0), False), ((9, 0), False)):
+        norm1._device_supports_norm1_quant.cache_clear()
+        with patch.object(torch.cuda, "is_available", return_value=True), \
+                patch.object(torch.cuda, "get_device_capability", return_value=capability):
+            assert norm1.supports_norm1_quant("cuda:0") is expected
+    norm1._device_supports_norm1_quant.cache_clear()
+    raw = torch.nn.Module()
+    raw.transformer_blocks = torch.nn.ModuleList([torch.nn.Linear(2, 2) for _ in range(36)])
+    raw.train()
+    with pytest.raises(ValueError):
+        norm1.clone_norm1_quant_decoder(raw)
+    raw.eval()
+    result = norm1.clone_norm1_quant_decoder(raw)
+    assert result._h3vae_norm1_quant_enabled is False
+    assert result is not raw and result.transformer_blocks[0] is not raw.transformer_blocks[0]
+    assert result.transformer_blocks[0].weight is raw.transformer_blocks[0].weight
+    with pytest.raises(RuntimeError):   # enabling needs an sm_100 device
+        norm1.clone_norm1_quant_decoder(raw, enabled=True)
+    raw.transformer_blocks = torch.nn.ModuleList([torch.nn.Linear(2, 2) for _ in range(35)])
+    with pytest.raises(ValueError):
+        norm1.clone_norm1_quant_decoder(raw)
