@@ -1,5 +1,6 @@
-"""CPU contracts of the decoder-rewrite helpers in h3vae_b200.opt (INT8 FFN install, fused FFN,
-norm-quant blocks, INT8 QKV and attention-out projections, container cloning), following the
+"""CPU contracts of the model-rewrite helpers in h3vae_b200.opt (INT8 FFN install, fused FFN,
+norm-quant blocks, the norm1 carry chain, INT8 QKV and attention-out projections, QK fusion,
+container cloning, the encoder's staged clip batching), following the
 reference's tests/test_int8_swiglu_fused.py, test_int8_norm_quant.py, test_int8_qkv.py,
 test_int8_attention_out.py and test_kitchen_int8.py:105-127.  The rewritten modules' forward passes
 run the ops that the GPU tests cover."""
@@ -310,3 +311,53 @@ def test_norm1_device_gate_and_clone_guards():
     raw.transformer_blocks = torch.nn.ModuleList([torch.nn.Linear(2, 2) for _ in range(35)])
     with pytest.raises(ValueError):
         norm1.clone_norm1_quant_decoder(raw)
+
+
+def _fake_encoder():
+    torch.manual_seed(0)
+    enc = torch.nn.Module()
+    enc.gradient_checkpointing, enc.use_fused_norm = False, False
+    enc.conv_in = torch.nn.Conv3d(3, 8, 1)
+    stages = []
+    for down in (True, True, False):
+        stage = torch.nn.Module()
+        stage.block = torch.nn.ModuleList([torch.nn.Conv3d(8, 8, (1, 3, 3), padding=(0, 1, 1))])
+        if down:
+            stage.downsample = torch.nn.Conv3d(8, 8, (1, 2, 2), stride=(1, 2, 2))
+        stages.append(stage)
+    enc.down = torch.nn.ModuleList(stages)
+    enc.norm_out = torch.nn.GroupNorm(2, 8)
+    enc.conv_out = torch.nn.Conv3d(8, 4, 1)
+    return enc.eval(), torch.nn.Conv3d(4, 4, 1).eval()
+
+
+@pytest.mark.parametrize("cut,batch,token_drop", [(1, 1, 0), (2, 2, 0), (2, 4, 3), (1, 2, 1)])
+def test_encode_staged_equals_per_clip_encoding(cut, batch, token_drop):
+    """Staged clip batching (ref: opt/encoder_staged_batch.py:39-57) equals encoding each padded
+    17-frame clip on its own and concatenating in time, then dropping token_drop latent frames."""
+    from h3vae_b200.opt.encoder_staged_batch import EncoderPrefix, EncoderSuffix, encode_staged
+    enc, quant = _fake_encoder()
+    prefix, suffix = EncoderPrefix(enc, cut), EncoderSuffix(enc, quant, cut)
+    video = torch.randn(1, 3, 40, 16, 16, generator=torch.Generator().manual_seed(1))
+    with torch.no_grad():
+        got = encode_staged(video, prefix, suffix, clip_length=17, token_drop=token_drop, batch_size=batch, cut=cut)
+        padded = torch.cat([video, video[:, :, -1:].repeat(1, 1, 11, 1, 1)], dim=2)
+        ref = torch.cat([suffix(prefix(padded[:, :, t:t + 17])) for t in (0, 17, 34)], dim=2)
+    ref = ref[:, :, :-token_drop] if token_drop else ref
+    assert got.shape == ref.shape
+    assert torch.allclose(got, ref, atol=1e-5, rtol=1e-5)
+
+
+def test_encode_staged_guards():
+    from h3vae_b200.opt.encoder_staged_batch import EncoderPrefix, EncoderSuffix, encode_staged
+    enc, quant = _fake_encoder()
+    prefix, suffix = EncoderPrefix(enc, 2), EncoderSuffix(enc, quant, 2)
+    with pytest.raises(ValueError):
+        EncoderPrefix(enc, 3)
+    enc.use_fused_norm = True
+    with pytest.raises(ValueError):
+        EncoderPrefix(enc, 1)
+    with pytest.raises(ValueError):   # batch-one videos only
+        encode_staged(torch.zeros(2, 3, 17, 8, 8), prefix, suffix, clip_length=17, token_drop=0, batch_size=1, cut=2)
+    with pytest.raises(ValueError):   # unvalidated (cut, batch) pair
+        encode_staged(torch.zeros(1, 3, 17, 8, 8), prefix, suffix, clip_length=17, token_drop=0, batch_size=4, cut=1)
