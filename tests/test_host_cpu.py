@@ -4,6 +4,7 @@ the runtime, the ComfyUI node surface, and the argument checks of the reference-
 from __future__ import annotations
 
 import re
+import sys
 
 import numpy as np
 import pytest
@@ -292,3 +293,59 @@ def test_oracle_fp16_block_chain_against_independent_fp32_torch():
         xs = h + ((g * torch.sigmoid(g) * u) @ blk.down_w.float().T + blk.down_b.float()) * blk.scale2.float()
     y = torch.nn.functional.layer_norm(xs, (d,), dec.ln_w.float(), dec.ln_b.float(), cfg.eps).view(b, n, d)
     assert ((y.double() - ref).norm() / ref.norm()).item() < 1e-3
+
+
+def test_build_comfy_vae_with_a_stand_in_comfy(monkeypatch):
+    """The comfy.sd.VAE wrapper (ref: h3vae_runtime.py:720-806) against stand-in comfy modules: the
+    latent / pixel ratios follow the runtime's clip geometry, input pixels map [0,1] -> [-1,1], the
+    runtime is the patched first-stage model, and a non-FP16 VAE dtype is refused."""
+    import types
+
+    from h3vae_b200.model import DecoderConfig, EncoderConfig
+    from h3vae_b200.runtime import H3VAEPyOptRuntime, build_comfy_vae
+
+    mm = types.ModuleType("comfy.model_management")
+    mm.vae_device = lambda: torch.device("cpu")
+    mm.vae_offload_device = lambda: torch.device("cpu")
+    mm.vae_dtype = lambda device, dtypes: dtypes[0]
+    mm.intermediate_device = lambda: torch.device("cpu")
+    mm.dtype_size = lambda dtype: 2
+    mp = types.ModuleType("comfy.model_patcher")
+
+    class CoreModelPatcher:
+        def __init__(self, model, load_device, offload_device):
+            self.model, self.load_device, self.offload_device = model, load_device, offload_device
+
+    mp.CoreModelPatcher = CoreModelPatcher
+    sd = types.ModuleType("comfy.sd")
+
+    class VAE:
+        def model_size(self):
+            self.size = 1234
+            return self.size
+
+    sd.VAE = VAE
+    comfy = types.ModuleType("comfy")
+    comfy.model_management, comfy.model_patcher, comfy.sd = mm, mp, sd
+    for name, module in (("comfy", comfy), ("comfy.model_management", mm), ("comfy.model_patcher", mp),
+                         ("comfy.sd", sd)):
+        monkeypatch.setitem(sys.modules, name, module)
+
+    runtime = H3VAEPyOptRuntime(device="cpu", log_calls=False, compile_decoder=False, compile_encoder=False,
+                                encoder_config=EncoderConfig(channels=(32, 32, 32, 32), blocks_per_stage=1,
+                                                             int8_stages=()),
+                                decoder_config=DecoderConfig(hidden=64, heads=1, blocks=1, ffn=128,
+                                                             up_channels=(32, 32, 32)))
+    vae = build_comfy_vae(runtime)
+    tpc, ratio = runtime.tokens_per_clip, runtime.decoder.spatial_ratio
+    assert isinstance(vae, VAE) and vae.patcher.model is runtime and vae.size == 1234
+    assert vae.latent_channels == runtime.latent_channels and vae.handles_tiling
+    assert vae.upscale_ratio[0](tpc) == 17 and vae.upscale_ratio[0](2 * tpc) == 34 and vae.upscale_ratio[1:] == (ratio, ratio)
+    assert vae.downscale_ratio[0](17) == tpc and vae.downscale_ratio[0](18) == 2 * tpc
+    x = torch.rand(1, 3, 2, 4, 4)
+    assert torch.equal(vae.process_input(x), x * 2.0 - 1.0) and vae.process_output(x) is x
+    assert vae.memory_used_decode((1, 16, tpc, 8, 8), torch.float16) > vae.memory_used_decode((1, 16, tpc, 4, 4),
+                                                                                            torch.float16)
+    mm.vae_dtype = lambda device, dtypes: torch.float32
+    with pytest.raises(RuntimeError, match="FP16"):
+        build_comfy_vae(runtime)
