@@ -9,9 +9,12 @@ comfy.sd.VAE exactly like the reference (h3vae_runtime.py:720-806).
 B200 additions: the hot kernels are the sm_100a library (there is no torch.compile; the
 compile_* options are accepted and ignored), and the tile work can be sharded over the GPUs of
 one node: with a torch.distributed process group (one process per GPU) every rank runs the same
-encode/decode call, takes a contiguous block of the (clip batch, tile) work items, accumulates its tiles'
-blend contributions into a canvas, and one NCCL reduce sums the canvases on rank 0, which
-returns the result (other ranks return None).
+encode/decode call and takes a contiguous block of the (clip batch, tile) work items.  Rank 0 holds
+the request; it sends every other rank only the pixel window its encoder items read (point to
+point, NCCL over NVLink; a decode request is the small latent tensor and is broadcast).  Each rank
+accumulates its tiles' blend contributions into the slab of the canvas its items cover (frame range
+x row band x column band), and rank 0 receives every slab and adds it into its canvas, then
+finalizes and returns the result (other ranks return None).  No full-size canvas is reduced.
 
 The real klvae model code and weights are not distributed with the reference; without them the
 runtime builds the H3-structured synthetic model of h3vae_b200.model with seeded random weights.
@@ -21,6 +24,7 @@ from __future__ import annotations
 import logging
 import os
 import time
+from contextlib import nullcontext as _nullcontext
 
 import torch
 
@@ -34,6 +38,7 @@ DEFAULT_MODEL_CODE_DIR = os.environ.get("H3_VAE_MODEL_CODE_DIR", "")
 DEFAULT_WEIGHTS_FALLBACK = os.environ.get("H3_VAE_WEIGHTS_PATH", "")
 
 CLIP_LENGTH = 17          # frames per causal encoder clip (ref: opt/encoder_staged_batch.py:39-57)
+TAIL_FRAMES = 5           # frames 17k+5 <-> tokens 5k+2 (ref: h3vae_runtime.py:483-491, :739-742)
 IMG_MEAN = (0.485, 0.456, 0.406)
 IMG_STD = (0.229, 0.224, 0.225)
 
@@ -171,8 +176,13 @@ class H3VAEPyOptRuntime(torch.nn.Module):
                 "leave model_code_dir and weights_path empty to run the H3-structured synthetic model")
         if compile_decoder or compile_encoder:
             logger.info("[H3VAE-B200] compile_* options ignored: kernels are precompiled sm_100a code")
-        if dtype != torch.float16:
-            raise RuntimeError("the B200 path runs fp16 activations (dtype=fp16)")
+        if dtype not in (torch.float16, torch.float32):
+            raise RuntimeError("dtype must be fp16 or fp32")
+        if dtype == torch.float32:
+            # the reference allows an fp32 VAE outside the INT8 / fused modes (h3vae_runtime.py:743-748);
+            # here fp32 pixels and latents are accepted and returned, the arithmetic runs on the fp16
+            # tensor-core path with fp32 accumulation
+            logger.info("[H3VAE-B200] dtype=fp32: fp32 inputs accepted, activations computed in fp16")
         if act_scale_mode not in ("tensor", "token"):
             raise ValueError("act_scale_mode must be 'tensor' (per-tensor, the reference's scheme) or 'token'")
 
@@ -222,44 +232,120 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         import torch.distributed as dist
         return dist.get_rank(self.process_group)
 
-    def _reduce_to_rank0(self, canvas: torch.Tensor) -> None:
-        if self.world > 1:
-            import torch.distributed as dist
-            dist.reduce(canvas, dst=dist.get_global_rank(self.process_group, 0), op=dist.ReduceOp.SUM,
-                        group=self.process_group)
+    def _src(self) -> int:
+        import torch.distributed as dist
+        return dist.get_global_rank(self.process_group, 0)
 
-    def _share_input(self, t: torch.Tensor | None) -> torch.Tensor:
-        """Rank 0 owns the request tensor; the other ranks receive it (shape, then fp16 data)."""
+    _DTYPES = (torch.float16, torch.float32, torch.bfloat16)
+
+    def _share_meta(self, t: torch.Tensor | None) -> tuple[tuple[int, ...], torch.dtype]:
+        """Rank 0 owns the request tensor; every rank learns its shape and dtype (one broadcast)."""
+        if self.world == 1:
+            return tuple(t.shape), t.dtype
+        import torch.distributed as dist
+        meta = torch.zeros(7, dtype=torch.int64, device=self.dev)
+        if self.rank == 0:
+            if t.dtype not in self._DTYPES:
+                raise ValueError(f"unsupported request dtype {t.dtype}")
+            meta[0], meta[1] = t.ndim, self._DTYPES.index(t.dtype)
+            meta[2:2 + t.ndim] = torch.tensor(list(t.shape), dtype=torch.int64)
+        dist.broadcast(meta, src=self._src(), group=self.process_group)
+        m = [int(v) for v in meta.tolist()]
+        return tuple(m[2:2 + m[0]]), self._DTYPES[m[1]]
+
+    def _broadcast_tensor(self, t: torch.Tensor | None, shape, dtype) -> torch.Tensor:
+        """The whole (small) request tensor on every rank: the latents of a decode call."""
         if self.world == 1:
             return t
         import torch.distributed as dist
-        src = dist.get_global_rank(self.process_group, 0)
-        shape = torch.tensor(list(t.shape) if self.rank == 0 else [0] * 5, dtype=torch.int64, device=self.dev)
-        dist.broadcast(shape, src=src, group=self.process_group)
         if self.rank == 0:
-            t = t.to(torch.float16).contiguous()
+            t = t.to(device=self.dev).contiguous()
         else:
-            t = torch.empty(tuple(int(v) for v in shape.tolist()), dtype=torch.float16, device=self.dev)
-        dist.broadcast(t, src=src, group=self.process_group)
+            t = torch.empty(shape, dtype=dtype, device=self.dev)
+        dist.broadcast(t, src=self._src(), group=self.process_group)
         return t
+
+    @staticmethod
+    def _frame_major(shape5, device, dtype=torch.float32):
+        """A zeroed blend canvas with frames outermost after the batch ([B, T, C, H, W] storage),
+        returned as its logical [B, C, T, H, W] view: one rank's frame range is then one contiguous
+        block, and a slab of frames, rows and columns ships as one buffer."""
+        b, c, t, h, w = shape5
+        return torch.zeros((b, t, c, h, w), dtype=dtype, device=device).permute(0, 2, 1, 3, 4)
+
+    def _gather_slabs(self, canvas, slab, boxes, on_slab=None) -> list:
+        """Bring every rank's blend slab to rank 0.  Rank r > 0 accumulated its work items into
+        `slab`, the zero-initialised box boxes[r] = (t0, t1, y0, y1, x0, x1) of the canvas; rank 0
+        accumulated its own items straight into `canvas`.  Rank 0 receives the other slabs (one
+        point-to-point receive per rank, posted together) and adds each into its box, calling
+        on_slab(r) after each add.  Returns the pending send works on ranks > 0."""
+        if self.world == 1:
+            return []
+        import torch.distributed as dist
+        src = self._src()
+        if self.rank != 0:
+            # frame-major contiguous storage of the slab is what crosses the link
+            return [dist.isend(slab.permute(0, 2, 1, 3, 4).contiguous(), dst=src, group=self.process_group)]
+        ops, bufs = [], {}
+        for r in range(1, self.world):
+            t0, t1, y0, y1, x0, x1 = boxes[r]
+            if t1 <= t0:
+                continue
+            buf = torch.empty((canvas.shape[0], t1 - t0, canvas.shape[1], y1 - y0, x1 - x0), dtype=canvas.dtype,
+                              device=canvas.device)
+            bufs[r] = buf
+            ops.append(dist.P2POp(dist.irecv, buf, dist.get_global_rank(self.process_group, r), self.process_group))
+        works = dist.batch_isend_irecv(ops) if ops else []
+        for w in works:
+            w.wait()
+        for r, buf in bufs.items():
+            t0, t1, y0, y1, x0, x1 = boxes[r]
+            canvas[:, :, t0:t1, y0:y1, x0:x1].add_(buf.permute(0, 2, 1, 3, 4))
+            if on_slab is not None:
+                on_slab(r)
+        return []
 
     # -- shapes ----------------------------------------------------------------
     def _device(self):
         return self.dev
 
     def _frames_from_tokens(self, t: int) -> int:
-        return max(1, -(-t // self.tokens_per_clip) * CLIP_LENGTH)
+        """Frame count of a decoded latent of t tokens: 17k+5 frames for 5k+2 tokens, one frame for
+        one token (ref: h3vae_runtime.py:483-486).  For an encoder whose temporal ratio is not 4 the
+        same rule holds with its own clip and tail token counts."""
+        if t <= 1:
+            return 1
+        return max(1, (t - self.tail_tokens) // self.tokens_per_clip * CLIP_LENGTH + TAIL_FRAMES)
 
     def _tokens_from_frames(self, frames: int) -> int:
-        return -(-frames // CLIP_LENGTH) * self.tokens_per_clip
+        """ref: h3vae_runtime.py:488-491."""
+        if frames <= 1:
+            return 1
+        return max(1, (frames - TAIL_FRAMES) // CLIP_LENGTH * self.tokens_per_clip + self.tail_tokens)
 
-    @property
-    def tokens_per_clip(self) -> int:
-        t = CLIP_LENGTH
-        for down in self.encoder.cfg.temporal_down:
+    @staticmethod
+    def _causal_tokens(frames: int, temporal_down) -> int:
+        t = frames
+        for down in temporal_down:
             if down:
                 t = (t - 1) // 2 + 1
         return t
+
+    @property
+    def tokens_per_clip(self) -> int:
+        """Tokens of one 17-frame clip (5 for the H3 temporal ratio 4)."""
+        return self._causal_tokens(CLIP_LENGTH, self.encoder.cfg.temporal_down)
+
+    @property
+    def tail_tokens(self) -> int:
+        """Tokens of the first 5 frames of a clip (2 for the H3 temporal ratio 4)."""
+        return self._causal_tokens(TAIL_FRAMES, self.encoder.cfg.temporal_down)
+
+    @property
+    def token_drop(self) -> int:
+        """Tokens dropped from the end of a staged encode (3 for H3: each clip gives 5 tokens, the
+        trailing 3 belong to the repeated padding frames; ref: opt/encoder_staged_batch.py:57)."""
+        return self.tokens_per_clip - self.tail_tokens
 
     def decode_output_shape(self, input_shape):
         b, c, t, h, w = input_shape
@@ -296,21 +382,32 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         x01 = (x.float() + 1.0) * 0.5
         return ((x01 - self._img_mean) / self._img_std).to(torch.float16)
 
+    @staticmethod
+    def _box(boxes):
+        """Bounding box (t0, t1, y0, y1, x0, x1) of several boxes; an empty list gives an empty box."""
+        if not boxes:
+            return (0, 0, 0, 0, 0, 0)
+        return (min(b[0] for b in boxes), max(b[1] for b in boxes), min(b[2] for b in boxes),
+                max(b[3] for b in boxes), min(b[4] for b in boxes), max(b[5] for b in boxes))
+
     @torch.no_grad()
     def encode(self, x, device=None):
-        """x: [B,3,T,H,W] (or [B,3,H,W]) in [-1,1] -> fp32 latents [B, C, t, H/r, W/r] (rank 0)."""
-        t0 = time.monotonic()
-        if self.int8_encode and x is not None and x.dtype != torch.float16:
-            raise RuntimeError("int8_encode requires FP16 pixel input; use the FP16 VAE dtype")
-        if self.rank == 0 and x.ndim == 4:
-            x = x.unsqueeze(2)
-        # A pinned host video on one GPU is uploaded clip batch by clip batch on a side stream, and
-        # the work items run clip-major, so the host->device copy overlaps the encoding.
-        streamed = (self.world == 1 and x.device.type == "cpu" and x.is_pinned() and x.is_contiguous())
-        if self.rank == 0 and not streamed:
-            x = x.to(device=self.dev)
-        x = self._share_input(x)
-        b, _, t, h, w = x.shape
+        """x: [B,3,T,H,W] (or [B,3,H,W]) in [-1,1] -> fp32 latents [B, C, t, H/r, W/r] (rank 0).
+
+        T frames are cut into causal 17-frame clips (the last one padded by repeating its final
+        frame), each clip gives tokens_per_clip tokens, and the trailing token_drop tokens are
+        dropped: 17k+5 frames -> 5k+2 tokens.  A single frame is encoded on its own and gives one
+        token.  ref: h3vae_runtime.py:572-582, 641-661; opt/encoder_staged_batch.py:39-57."""
+        t_start = time.monotonic()
+        if self.rank == 0:
+            if self.int8_encode and x.dtype != torch.float16:
+                raise RuntimeError("int8_encode requires FP16 pixel input; use the FP16 VAE dtype")
+            if x.ndim == 4:
+                x = x.unsqueeze(2)
+            if x.ndim != 5 or x.shape[1] != 3:
+                raise ValueError("encode expects [B,3,T,H,W] or [B,3,H,W] pixels")
+        shape, dtype = self._share_meta(x)
+        b, _, t, h, w = shape
         tile = tiling.select_encoder_tile(self.encoder_tile_size, h, w)
         r = self.encoder.cfg.spatial_ratio
         if h > tile or w > tile:
@@ -318,51 +415,130 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         else:
             plan = tiling.TilePlan((0,), (h,), (), (0,), (w,), ())
         lplan = plan.scaled(r)
-        clips = -(-t // CLIP_LENGTH)
-        tpc = self.tokens_per_clip
-        lat = torch.zeros((b, self.latent_channels, clips * tpc, lplan.height, lplan.width), dtype=torch.float32,
-                          device=self.dev)
+        clip_len = 1 if t == 1 else CLIP_LENGTH
+        tpc = 1 if t == 1 else self.tokens_per_clip
+        clips = -(-t // clip_len)
         # work items: (staged batch of clips, tile), clip-major; the clip batches write disjoint
         # latent frames, so each latent value still receives its tiles in row-major tile order
         cbatches = tiling.batches(list(range(clips)), self.encoder_staged_batch)
         items = [(g, i, j) for g in range(len(cbatches)) for (i, j) in plan.tiles()]
-        arrived = None
-        if streamed:
-            x, arrived = self._upload_clip_batches(x, cbatches, t)
-        for k in tiling.shard_range(len(items), self.world, self.rank):
+
+        def px_box(k):
+            g, i, j = items[k]
+            cs = cbatches[g]
+            return (cs[0] * clip_len, min((cs[-1] + 1) * clip_len, t), plan.ys[i], plan.ys[i] + plan.hs[i],
+                    plan.xs[j], plan.xs[j] + plan.ws[j])
+
+        def lat_box(k):
+            g, i, j = items[k]
+            cs = cbatches[g]
+            return (cs[0] * tpc, (cs[-1] + 1) * tpc, lplan.ys[i], lplan.ys[i] + lplan.hs[i],
+                    lplan.xs[j], lplan.xs[j] + lplan.ws[j])
+
+        shards = [tiling.shard_range(len(items), self.world, q) for q in range(self.world)]
+        px_boxes = [self._box([px_box(k) for k in sh]) for sh in shards]
+        lat_boxes = [self._box([lat_box(k) for k in sh]) for sh in shards]
+        mine = shards[self.rank]
+        # -- input: rank 0 holds the video; every other rank receives only its pixel window
+        xv, origin, arrived, sends = self._scatter_video(x, shape, dtype, cbatches, clip_len, px_boxes)
+        # -- latent canvas (rank 0: all tokens; other ranks: their latent slab)
+        lshape = (b, self.latent_channels, clips * tpc, lplan.height, lplan.width)
+        if self.rank == 0:
+            canvas = self._frame_major(lshape, self.dev)
+            lorigin = (0, 0, 0)
+        else:
+            t0, t1, y0, y1, x0, x1 = lat_boxes[self.rank]
+            canvas = self._frame_major((b, self.latent_channels, t1 - t0, y1 - y0, x1 - x0), self.dev)
+            lorigin = (t0, y0, x0)
+        for k in mine:
             g, i, j = items[k]
             cs = cbatches[g]
             if arrived is not None and arrived[g] is not None:
                 torch.cuda.current_stream(self.dev).wait_event(arrived[g])
                 arrived[g] = None
-            tile_px = x[..., plan.ys[i]:plan.ys[i] + plan.hs[i], plan.xs[j]:plan.xs[j] + plan.ws[j]]
+            py, px = plan.ys[i] - origin[1], plan.xs[j] - origin[2]
+            tile_px = xv[..., py:py + plan.hs[i], px:px + plan.ws[j]]
             batch = []
             for bi in range(b):
                 for c in cs:
-                    clip = tile_px[bi:bi + 1, :, c * CLIP_LENGTH:(c + 1) * CLIP_LENGTH]
-                    if clip.shape[2] < CLIP_LENGTH:   # pad the last clip by repeating its last frame
-                        rep = clip[:, :, -1:].expand(-1, -1, CLIP_LENGTH - clip.shape[2], -1, -1)
+                    f0 = c * clip_len - origin[0]
+                    clip = tile_px[bi:bi + 1, :, f0:f0 + clip_len]
+                    if clip.shape[2] < clip_len:   # pad the last clip by repeating its last frame
+                        rep = clip[:, :, -1:].expand(-1, -1, clip_len - clip.shape[2], -1, -1)
                         clip = torch.cat([clip, rep], dim=2)
                     batch.append(clip)
-            clips = torch.cat(batch, 0)
-            if clips.dtype == torch.float16:
+            clip_batch = torch.cat(batch, 0)
+            if clip_batch.dtype == torch.float16:
                 # normalization fused into the encoder's input conv
-                moments = self.encoder(clips, norm=(self._img_mean, self._img_std))
+                moments = self.encoder(clip_batch, norm=(self._img_mean, self._img_std))
             else:
-                moments = self.encoder(self._normalize_pixels(clips))
+                moments = self.encoder(self._normalize_pixels(clip_batch))
             mean = moments[:, : self.latent_channels]
             wmap = self._weights(lplan, i, j)
+            ly, lx = lplan.ys[i] - lorigin[1], lplan.xs[j] - lorigin[2]
             for n, (bi, c) in enumerate((bi, c) for bi in range(b) for c in cs):
-                ly, lx = lplan.ys[i], lplan.xs[j]
-                K.blend_accumulate(lat[bi, :, c * tpc:(c + 1) * tpc, ly:ly + lplan.hs[i], lx:lx + lplan.ws[j]],
+                c0 = c * tpc - lorigin[0]
+                K.blend_accumulate(canvas[bi, :, c0:c0 + tpc, ly:ly + lplan.hs[i], lx:lx + lplan.ws[j]],
                                    mean[n], wmap)
-        self._reduce_to_rank0(lat)
-        self._log_call("encode", t0)
+        sends += self._gather_slabs(canvas, canvas, lat_boxes)
+        for work in sends:
+            work.wait()
+        self._log_call("encode", t_start)
         if self.rank != 0:
             return None
-        return (lat - self.latents_mean.float()) / self.latents_std.float()
+        tokens = clips * tpc - (self.token_drop if t > 1 else 0)
+        lat = canvas[:, :, :tokens]
+        return ((lat - self.latents_mean.float()) / self.latents_std.float()).contiguous()
 
-    def _upload_clip_batches(self, x_host, cbatches, t):
+    def _scatter_video(self, x, shape, dtype, cbatches, clip_len, px_boxes):
+        """Place the request video for this rank's work items.
+
+        Returns (video, origin, arrived, sends): `video` holds this rank's pixel window, whose
+        (frame, row, column) origin in the full video is `origin`; `arrived` is one CUDA event per
+        clip batch when the frames are still being uploaded (else None); `sends` are rank 0's
+        pending sends.  A pinned host video on rank 0 is uploaded clip batch by clip batch on a
+        side stream, so the host->device copy overlaps the encoding of the earlier batches.  At
+        N > 1 rank 0 cuts every other rank's window out of its copy on that side stream and sends
+        it point to point (NCCL over NVLink); the other ranks receive only their window."""
+        b, c, t = shape[0], shape[1], shape[2]
+        if self.rank == 0:
+            streamed = (x.device.type == "cpu" and x.is_pinned() and x.is_contiguous()
+                        and self.dev.type == "cuda")
+            arrived = None
+            if streamed:
+                x, arrived = self._upload_clip_batches(x, cbatches, t, clip_len)
+            else:
+                x = x.to(device=self.dev)
+            sends = []
+            if self.world > 1:
+                import torch.distributed as dist
+                side = torch.cuda.Stream(self.dev) if self.dev.type == "cuda" else None
+                if side is not None:
+                    side.wait_stream(torch.cuda.current_stream(self.dev))
+                for q in range(1, self.world):
+                    t0, t1, y0, y1, x0, x1 = px_boxes[q]
+                    if t1 <= t0:
+                        continue
+                    ctx = torch.cuda.stream(side) if side is not None else _nullcontext()
+                    with ctx:
+                        if arrived is not None:
+                            for g, cs in enumerate(cbatches):
+                                if cs[0] * clip_len < t1 and min((cs[-1] + 1) * clip_len, t) > t0:
+                                    side.wait_event(arrived[g])
+                        win = x[:, :, t0:t1, y0:y1, x0:x1].contiguous()
+                        sends.append(dist.isend(win, dst=dist.get_global_rank(self.process_group, q),
+                                                group=self.process_group))
+                if side is not None:
+                    x.record_stream(side)
+            return x, (0, 0, 0), arrived, sends
+        import torch.distributed as dist
+        t0, t1, y0, y1, x0, x1 = px_boxes[self.rank]
+        win = torch.empty((b, c, t1 - t0, y1 - y0, x1 - x0), dtype=dtype, device=self.dev)
+        if t1 > t0:
+            dist.irecv(win, src=self._src(), group=self.process_group).wait()
+        return win, (t0, y0, x0), None, []
+
+    def _upload_clip_batches(self, x_host, cbatches, t, clip_len=CLIP_LENGTH):
         """Issue the host->device copy of each clip batch's frames on a side stream (one contiguous
         copy per (batch entry, channel) plane).  Returns the device video and one event per clip batch."""
         x_dev = torch.empty(x_host.shape, dtype=x_host.dtype, device=self.dev)
@@ -371,7 +547,7 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         events = []
         with torch.cuda.stream(copy_stream):
             for cs in cbatches:
-                f0, f1 = cs[0] * CLIP_LENGTH, min((cs[-1] + 1) * CLIP_LENGTH, t)
+                f0, f1 = cs[0] * clip_len, min((cs[-1] + 1) * clip_len, t)
                 for bi in range(x_host.shape[0]):
                     for ch in range(x_host.shape[1]):
                         x_dev[bi, ch, f0:f1].copy_(x_host[bi, ch, f0:f1], non_blocking=True)
@@ -386,14 +562,23 @@ class H3VAEPyOptRuntime(torch.nn.Module):
     # -- decode ----------------------------------------------------------------
     @torch.no_grad()
     def decode(self, z, output_buffer=None, **kwargs):
-        """z: [B, C, t, h, w] normalized latents -> fp32 pixels [B, 3, F, h*r, w*r] in [0, 1] (rank 0)."""
-        t0 = time.monotonic()
-        if self.int8_decode and z is not None and z.dtype != torch.float16:
-            raise RuntimeError("int8_decode requires FP16 latent input; use the FP16 VAE dtype")
-        z = self._share_input(z.to(device=self.dev) if self.rank == 0 else None)
+        """z: [B, C, t, h, w] normalized latents -> fp32 pixels [B, 3, F, h*r, w*r] in [0, 1] (rank 0).
+
+        F = 17k+5 for t = 5k+2 tokens (one frame for one token).  The tokens are decoded in chunks
+        of tokens_per_clip (the last chunk padded by repeating the final token) and the output is
+        trimmed to F frames.  ref: h3vae_runtime.py:524-564."""
+        t_start = time.monotonic()
+        if self.rank == 0:
+            if self.int8_decode and z.dtype != torch.float16:
+                raise RuntimeError("int8_decode requires FP16 latent input; use the FP16 VAE dtype")
+            if z.ndim != 5:
+                raise ValueError("decode expects [B,C,t,h,w] latents")
+            z = z.to(device=self.dev)
+        shape, dtype = self._share_meta(z)
+        z = self._broadcast_tensor(z, shape, dtype)
         zn = (z * self.latents_std + self.latents_mean).to(torch.float16)
         b, _, t, h, w = zn.shape
-        tpc = self.tokens_per_clip
+        tpc = 1 if t == 1 else self.tokens_per_clip
         chunks = -(-t // tpc)
         if chunks * tpc != t:   # too few tokens for the last chunk: repeat the last latent frame
             zn = torch.cat([zn, zn[:, :, -1:].expand(-1, -1, chunks * tpc - t, -1, -1)], dim=2)
@@ -407,42 +592,72 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         pplan = tiling.TilePlan(*(tuple(v * r for v in seq) for seq in
                                   (lplan.ys, lplan.hs, lplan.oys, lplan.xs, lplan.ws, lplan.oxs)))
         fpc = self.decoder.frames_for(tpc)
-        canvas = torch.zeros((b, 3, chunks * fpc, pplan.height, pplan.width), dtype=torch.float32, device=self.dev)
-        tasks = [(bi, c, i, j) for bi in range(b) for c in range(chunks) for (i, j) in lplan.tiles()]
-        per_call = max(1, self.tile_batch)
-        groups = tiling.batches(tasks, per_call)
         frames = self._frames_from_tokens(t)
-        # A pinned host output buffer on one GPU: each temporal chunk is finalized and copied to the
-        # host on a side stream as soon as its last tile is blended (tasks run chunk by chunk), so the
-        # device->host transfer overlaps the decoding of the later chunks.
-        streamed = (output_buffer is not None and self.world == 1 and output_buffer.device.type == "cpu"
-                    and output_buffer.is_pinned() and output_buffer.dtype == torch.float32
-                    and output_buffer.is_contiguous()
+        tasks = [(bi, c, i, j) for bi in range(b) for c in range(chunks) for (i, j) in lplan.tiles()]
+        groups = tiling.batches(tasks, max(1, self.tile_batch))
+        shards = [tiling.shard_range(len(groups), self.world, q) for q in range(self.world)]
+
+        def px_box(task):
+            _, c, i, j = task
+            return (c * fpc, (c + 1) * fpc, pplan.ys[i], pplan.ys[i] + pplan.hs[i], pplan.xs[j],
+                    pplan.xs[j] + pplan.ws[j])
+
+        boxes = [self._box([px_box(tk) for k in sh for tk in groups[k]]) for sh in shards]
+        if self.rank == 0:
+            canvas = self._frame_major((b, 3, chunks * fpc, pplan.height, pplan.width), self.dev)
+            origin = (0, 0, 0)
+        else:
+            t0, t1, y0, y1, x0, x1 = boxes[self.rank]
+            canvas = self._frame_major((b, 3, t1 - t0, y1 - y0, x1 - x0), self.dev)
+            origin = (t0, y0, x0)
+        # A pinned host output buffer on rank 0: each temporal chunk is finalized and copied to the
+        # host on a side stream as soon as its last tile is blended (tasks run chunk by chunk, and
+        # another rank's tiles count once its slab has been added), so the device->host transfer
+        # overlaps the decoding of the later chunks.
+        streamed = (self.rank == 0 and output_buffer is not None and output_buffer.device.type == "cpu"
+                    and self.dev.type == "cuda" and output_buffer.is_pinned()
+                    and output_buffer.dtype == torch.float32 and output_buffer.is_contiguous()
                     and tuple(output_buffer.shape) == (b, 3, frames, pplan.height, pplan.width))
         copy_stream = torch.cuda.Stream(self.dev) if streamed else None
         pending = {}
         for (bi, c, _, _) in tasks:
             pending[(bi, c)] = pending.get((bi, c), 0) + 1
-        for k in tiling.shard_range(len(groups), self.world, self.rank):
+
+        def done(bi, c, n=1):
+            pending[(bi, c)] -= n
+            if streamed and pending[(bi, c)] == 0:
+                self._emit_chunk(canvas, bi, c * fpc, min((c + 1) * fpc, frames), output_buffer, copy_stream)
+
+        for k in shards[self.rank]:
             group = groups[k]
             lat = torch.cat([zn[bi:bi + 1, :, c * tpc:(c + 1) * tpc, lplan.ys[i]:lplan.ys[i] + lplan.hs[i],
                                 lplan.xs[j]:lplan.xs[j] + lplan.ws[j]] for (bi, c, i, j) in group], 0)
             pix = self.decoder(lat)
             for n, (bi, c, i, j) in enumerate(group):
-                y0, x0 = pplan.ys[i], pplan.xs[j]
-                K.blend_accumulate(canvas[bi, :, c * fpc:(c + 1) * fpc, y0:y0 + pplan.hs[i], x0:x0 + pplan.ws[j]],
+                f0, y0, x0 = c * fpc - origin[0], pplan.ys[i] - origin[1], pplan.xs[j] - origin[2]
+                K.blend_accumulate(canvas[bi, :, f0:f0 + fpc, y0:y0 + pplan.hs[i], x0:x0 + pplan.ws[j]],
                                    pix[n], self._weights(pplan, i, j))
-                pending[(bi, c)] -= 1
-                if streamed and pending[(bi, c)] == 0:
-                    self._emit_chunk(canvas, bi, c * fpc, min((c + 1) * fpc, frames), output_buffer, copy_stream)
+                if self.rank == 0:
+                    done(bi, c)
+
+        def slab_added(q):
+            counts = {}
+            for k in shards[q]:
+                for (bi, c, _, _) in groups[k]:
+                    counts[(bi, c)] = counts.get((bi, c), 0) + 1
+            for key, n in counts.items():
+                done(*key, n=n)
+
+        sends = self._gather_slabs(canvas, canvas, boxes, on_slab=slab_added)
+        for work in sends:
+            work.wait()
+        if self.rank != 0:
+            self._log_call("decode", t_start)
+            return None
         if streamed:
             copy_stream.synchronize()
-            self._log_call("decode", t0)
+            self._log_call("decode", t_start)
             return output_buffer
-        self._reduce_to_rank0(canvas)
-        if self.rank != 0:
-            self._log_call("decode", t0)
-            return None
         dec = canvas[:, :, :frames]
         direct = (output_buffer is not None and output_buffer.shape == dec.shape
                   and output_buffer.dtype == torch.float32 and output_buffer.device == dec.device
@@ -455,7 +670,7 @@ class H3VAEPyOptRuntime(torch.nn.Module):
             out = output_buffer
         else:
             out = pixels
-        self._log_call("decode", t0)
+        self._log_call("decode", t_start)
         return out
 
     def _emit_chunk(self, canvas, bi, f0, f1, host_out, copy_stream):
@@ -512,7 +727,7 @@ def build_comfy_vae(runtime: H3VAEPyOptRuntime, dtype=None):
     import comfy.model_patcher
     import comfy.sd
 
-    tpc, ratio = runtime.tokens_per_clip, runtime.decoder.spatial_ratio
+    ratio = runtime.decoder.spatial_ratio
 
     class H3VAEPyOptVAE(comfy.sd.VAE):
         def __init__(self, first_stage_model, device=None, dtype=None):
@@ -520,11 +735,13 @@ def build_comfy_vae(runtime: H3VAEPyOptRuntime, dtype=None):
             self.latent_channels = runtime.latent_channels
             self.latent_dim = 3
             self.output_channels = 3
-            self.upscale_ratio = (lambda a: max(1, -(-a // tpc) * CLIP_LENGTH), ratio, ratio)
-            self.upscale_index_formula = (CLIP_LENGTH // tpc, ratio, ratio)
-            self.downscale_ratio = (lambda a: max(1, -(-a // CLIP_LENGTH) * tpc), ratio, ratio)
-            self.downscale_index_formula = (CLIP_LENGTH // tpc, ratio, ratio)
-            self.working_dtypes = [torch.float16]
+            # frames 17k+5 <-> latents 5k+2 (ref: h3vae_runtime.py:739-742)
+            self.upscale_ratio = (lambda a: runtime._frames_from_tokens(a), ratio, ratio)
+            self.upscale_index_formula = (4, ratio, ratio)
+            self.downscale_ratio = (lambda a: runtime._tokens_from_frames(a), ratio, ratio)
+            self.downscale_index_formula = (4, ratio, ratio)
+            self.working_dtypes = ([torch.float16] if runtime.int8_decode or runtime.int8_encode
+                                   else [torch.float16, torch.float32])
             self.handles_tiling = True
             self.process_output = lambda image: image
             self.process_input = lambda image: image * 2.0 - 1.0
@@ -541,7 +758,7 @@ def build_comfy_vae(runtime: H3VAEPyOptRuntime, dtype=None):
             offload_device = model_management.vae_offload_device()
             if dtype is None:
                 dtype = model_management.vae_dtype(self.device, self.working_dtypes)
-            if dtype != torch.float16:
+            if dtype not in self.working_dtypes:
                 raise RuntimeError("INT8 VAE mode requires ComfyUI to select an FP16 VAE dtype")
             self.vae_dtype = dtype
             self.output_device = model_management.intermediate_device()

@@ -100,7 +100,8 @@ def test_int8_encode_and_fusion_validation_policy():
     (dict(encoder_staged_batch=3), ValueError, "1, 2 or 4"),
     (dict(tile_batch=-1), ValueError, "non-negative"),
     (dict(model_code_dir="/nonexistent"), NotImplementedError, "synthetic"),
-    (dict(dtype=torch.float32), RuntimeError, "fp16"),
+    (dict(dtype=torch.bfloat16), RuntimeError, "fp16 or fp32"),
+    (dict(dtype=torch.float32, decode_fusions=True, device="cpu"), RuntimeError, "fp16"),
     (dict(int8_decode=True, device="cpu"), RuntimeError, "CUDA device"),
     (dict(act_scale_mode="channel"), ValueError, "act_scale_mode"),
 ])
@@ -340,12 +341,22 @@ def test_build_comfy_vae_with_a_stand_in_comfy(monkeypatch):
     tpc, ratio = runtime.tokens_per_clip, runtime.decoder.spatial_ratio
     assert isinstance(vae, VAE) and vae.patcher.model is runtime and vae.size == 1234
     assert vae.latent_channels == runtime.latent_channels and vae.handles_tiling
-    assert vae.upscale_ratio[0](tpc) == 17 and vae.upscale_ratio[0](2 * tpc) == 34 and vae.upscale_ratio[1:] == (ratio, ratio)
-    assert vae.downscale_ratio[0](17) == tpc and vae.downscale_ratio[0](18) == 2 * tpc
+    # the reference's temporal contract: frames 17k+5 <-> latents 5k+2, one frame <-> one latent
+    # (ref: h3vae_runtime.py:739-742)
+    assert tpc == 5 and vae.upscale_ratio[1:] == (ratio, ratio) and vae.downscale_ratio[1:] == (ratio, ratio)
+    assert vae.upscale_ratio[0](37) == 124 and vae.downscale_ratio[0](124) == 37
+    assert vae.upscale_ratio[0](2) == 5 and vae.downscale_ratio[0](5) == 2
+    assert vae.upscale_ratio[0](1) == 1 and vae.downscale_ratio[0](1) == 1
+    for k in range(6):
+        assert vae.upscale_ratio[0](5 * k + 2) == 17 * k + 5 and vae.downscale_ratio[0](17 * k + 5) == 5 * k + 2
+    assert vae.upscale_index_formula == (4, ratio, ratio) and vae.downscale_index_formula == (4, ratio, ratio)
+    assert vae.working_dtypes == [torch.float16, torch.float32]
     x = torch.rand(1, 3, 2, 4, 4)
     assert torch.equal(vae.process_input(x), x * 2.0 - 1.0) and vae.process_output(x) is x
     assert vae.memory_used_decode((1, 16, tpc, 8, 8), torch.float16) > vae.memory_used_decode((1, 16, tpc, 4, 4),
                                                                                             torch.float16)
     mm.vae_dtype = lambda device, dtypes: torch.float32
+    assert build_comfy_vae(runtime).vae_dtype == torch.float32   # fp32 is allowed outside the INT8 modes
+    mm.vae_dtype = lambda device, dtypes: torch.bfloat16
     with pytest.raises(RuntimeError, match="FP16"):
         build_comfy_vae(runtime)

@@ -132,7 +132,11 @@ def _run(world, mode):
     return results
 
 
-def test_two_rank_encode_decode_equals_single_process(monkeypatch):
+@pytest.mark.parametrize("world", [2, 3])
+def test_multi_rank_encode_decode_equals_single_process(monkeypatch, world):
+    """Rank 0 sends each rank only its pixel window and adds the ranks' canvas slabs; with 3 ranks
+    the shard boundaries fall inside clip batches and temporal chunks, so slabs overlap and are
+    summed."""
     # CPU stand-ins for this test only (the spawned ranks set their own)
     monkeypatch.setattr(rt.K, "finalize_pixels", _cpu_finalize)
     monkeypatch.setattr(rt.K, "blend_accumulate", _cpu_blend)
@@ -140,9 +144,10 @@ def test_two_rank_encode_decode_equals_single_process(monkeypatch):
     video, lat = _inputs()
     enc_ref = single.encode(video)
     dec_ref = single.decode(lat)
-    results = _run(2, "ok")
+    results = _run(world, "ok")
     assert results[0][0] == "ok", results[0][1]
-    assert results[1] == ("ok", None)           # non-zero ranks return None
+    for r in range(1, world):
+        assert results[r] == ("ok", None)       # non-zero ranks return None
     enc, dec = (torch.from_numpy(a) for a in results[0][1])
     assert enc.shape == enc_ref.shape and dec.shape == dec_ref.shape
     torch.testing.assert_close(enc, enc_ref, rtol=0, atol=1e-5)
@@ -153,3 +158,30 @@ def test_rank_failure_surfaces_as_error_on_peer():
     results = _run(2, "fail")
     assert results[1][0] == "error" and "planted failure" in results[1][1]
     assert results[0][0] == "error", "rank 0 must not wait forever for a rank that died"
+
+
+def test_temporal_contract_matches_reference(monkeypatch):
+    """Frames 17k+5 <-> latents 5k+2 and one frame <-> one latent, through encode and decode
+    (ref: h3vae_runtime.py:483-491, 572-582, 524-537; opt/encoder_staged_batch.py:39-57)."""
+    monkeypatch.setattr(rt.K, "finalize_pixels", _cpu_finalize)
+    monkeypatch.setattr(rt.K, "blend_accumulate", _cpu_blend)
+    run = _make_runtime(None)
+    g = torch.Generator().manual_seed(5)
+    video = (torch.rand((1, 3, 124, 64, 64), generator=g) * 2 - 1).half()
+    lat = run.encode(video)
+    assert lat.shape == (1, 16, 37, 8, 8)
+    out = run.decode(lat.half())
+    assert out.shape == run.decode_output_shape(lat.shape) == (1, 3, 124, 64, 64)
+    # the kept tokens are the first 37 of the 8 clips' 40 (the dropped 3 encode padding frames)
+    clips = torch.cat([video[:, :, :119], video[:, :, -1:].expand(-1, -1, 17, -1, -1)], dim=2)
+    full = run.encode(clips)
+    assert full.shape[2] == 8 * 5 - 3
+    for k in range(4):
+        v = video[:, :, :17 * k + 5]
+        z = run.encode(v)
+        assert z.shape[2] == 5 * k + 2 == run._tokens_from_frames(17 * k + 5)
+        assert run.decode(z.half()).shape[2] == 17 * k + 5 == run._frames_from_tokens(5 * k + 2)
+    img = video[:, :, 0]                      # a single image [B,3,H,W]
+    z1 = run.encode(img)
+    assert z1.shape == (1, 16, 1, 8, 8)
+    assert run.decode(z1.half()).shape == (1, 3, 1, 64, 64)
