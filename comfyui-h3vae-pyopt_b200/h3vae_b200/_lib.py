@@ -27,6 +27,7 @@ _SIGNATURES = {
     "h3b_last_error": (c_char_p, []),
     "h3b_abi_version": (c_int, []),
     "h3b_device_error": (c_int, [POINTER(c_uint), c_int]),
+    "h3b_probe_wait_timeout": (c_int, [c_uint, c_void_p]),
     "h3b_conv3d_i8": (c_int, [c_void_p, _i64p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,
                               c_void_p, c_void_p, c_void_p, c_void_p, _i64p, c_void_p, c_void_p, c_int, c_void_p]),
     "h3b_conv3d_f16": (c_int, [c_void_p, _i64p, c_void_p, c_int64, c_int, c_int, c_int, c_int, c_int, c_int,

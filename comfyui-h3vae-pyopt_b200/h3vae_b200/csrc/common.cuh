@@ -168,16 +168,23 @@ __device__ __forceinline__ bool mbar_poll(uint64_t* bar, uint32_t parity, volati
   return false;
 }
 
-// Bounded wait on a phase parity.  Returns false (and records the error) if
-// the phase never completes or if another role already aborted the CTA.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
-  for (uint32_t i = 0; i < kSpinLimit; ++i) {
+// Bounded wait on a phase parity with an explicit poll limit.  Returns false
+// (and records the error) if the phase does not complete within `limit` polls
+// or if another role already aborted the CTA.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                                uint32_t limit) {
+  for (uint32_t i = 0; i < limit; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((i & 1023u) == 1023u && abort_flag != nullptr && *abort_flag) return false;
   }
   record_error(kErrBarrierTimeout);
   if (abort_flag != nullptr) *abort_flag = 1;
   return false;
+}
+
+// The kernels' wait: the same loop with the library-wide bound.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  return mbar_wait_limit(bar, parity, abort_flag, kSpinLimit);
 }
 
 // ---------------------------------------------------------------------------

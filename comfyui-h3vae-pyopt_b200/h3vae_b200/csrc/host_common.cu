@@ -76,7 +76,47 @@ int num_sms() {
 
 }  // namespace h3b_host
 
+namespace h3b {
+
+// One warp waits on an mbarrier that nothing arrives at, through the same
+// bounded wait the kernels use, with a caller-chosen poll limit.  The wait
+// runs out, records kErrBarrierTimeout in the device error word and returns.
+__global__ void __launch_bounds__(32) wait_timeout_probe_kernel(uint32_t poll_limit) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncwarp();
+  mbar_wait_limit(&bar, 0, &abort_flag, poll_limit);
+  __syncwarp();
+}
+
+}  // namespace h3b
+
 extern "C" {
+
+int h3b_probe_wait_timeout(uint32_t poll_limit, h3b_stream_t stream) {
+  const char* name = "h3b_probe_wait_timeout";
+  if (poll_limit == 0 || poll_limit > (1u << 20))
+    return h3b_host::set_error(H3B_EINVAL, "%s: poll_limit must be in [1, 2^20], got %u", name, poll_limit);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  h3b::wait_timeout_probe_kernel<<<1, 32, 0, st>>>(poll_limit);
+  int rc = h3b_host::check_launch(name);
+  if (rc != H3B_OK) return rc;
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return h3b_host::set_error(H3B_ECUDA, "%s: %s", name, cudaGetErrorString(e));
+  unsigned int v = 0;
+  e = cudaMemcpyFromSymbol(&v, h3b::g_device_error, sizeof(v));
+  if (e != cudaSuccess) return h3b_host::set_error(H3B_ECUDA, "%s: read of device error word failed: %s", name,
+                                                   cudaGetErrorString(e));
+  if (v & h3b::kErrBarrierTimeout)
+    return h3b_host::set_error(H3B_EDEVICE, "%s: bounded wait expired after %u polls (device error bits 0x%x)",
+                               name, poll_limit, v);
+  return H3B_OK;
+}
 
 const char* h3b_last_error(void) { return h3b_host::g_last_error; }
 

@@ -45,6 +45,16 @@ int h3b_abi_version(void);
  * timeout or invariant failure. */
 int h3b_device_error(unsigned int* bits, int clear);
 
+/* Failure-detection probe (diagnostic; no counterpart in the reference).
+ * Launches one warp that waits on an mbarrier nothing arrives at, through the
+ * same bounded wait every kernel of this library uses, with the given poll
+ * limit (1 .. 2^20) instead of the library-wide one.  The wait runs out, ORs
+ * the barrier-timeout bit (1) into the device error word and the kernel
+ * returns; the call synchronizes `stream` and returns H3B_EDEVICE when the bit
+ * is set.  Nothing traps and nothing waits without a bound; the context stays
+ * usable.  The bit stays set until h3b_device_error(&bits, 1) clears it. */
+int h3b_probe_wait_timeout(uint32_t poll_limit, h3b_stream_t stream);
+
 /* ---- (a4) INT8 implicit-GEMM 3-D convolution ---------------------------- */
 
 /* Valid (unpadded) 3-D convolution of an already padded, already quantized

@@ -1,0 +1,187 @@
+"""Parity at the configurations the benchmark runs, on the B200.
+
+* Config 2: one INT8 decoder block (4 tiles x 1024 tokens, hidden 1024, 16 heads x 64, rotary 48 over a
+  4x16x16 token grid, FFN 2 x 4096) and a two-block chain (the (h, out, scale2) carry and the in-place
+  residual of ref opt/int8_norm1_quant.py:185-252) against the oracle's composition of the same steps
+  (row_quant_ck / prequantized_linear / qk_rope / attention / residual_rms_quant / ffn_up_swiglu /
+  final_residual_layernorm).  INT8 re-quantization between the GEMMs turns the attention's fp16-vs-
+  float64 rounding into occasional +-1 code flips, so the block output is compared by relative L2 error
+  and by max-abs error relative to the output's range.
+* Stage-1 INT8 conv at its full size [4,128,19,258,258] -> [4,128,17,256,256] (the kw-strip kernel with a
+  persistent multi-wave grid, with and without the fused residual): int32 accumulators bit-exact against
+  the oracle on sampled whole output rows (every batch entry, first / middle / last frames and rows).
+* Stage-1 norm producer at its full size [4,128,17,256,256]: the per-tensor scale against the oracle over
+  every frame, the INT8 codes on sampled frames (+-1 on at most 0.1 %).
+* The north_star quality gate: an INT8 encode + decode round trip against the fp16 encode + decode round
+  trip of the same weights (config-3 encoder, config-4 decoder), PSNR >= 45 dB.
+"""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import h3vae_oracle as O
+
+pytestmark = pytest.mark.gpu
+CL3 = torch.channels_last_3d
+
+
+def _npy(t):
+    return t.detach().cpu().numpy()
+
+
+def _oracle_int8_chain(dec, x, grid):
+    """The INT8 block chain composed from the oracle's restatements, in the model's order."""
+    cfg = dec.cfg
+    b, n, d = x.shape
+    cos, sin = (_npy(t) for t in dec._rope(b, *grid))
+    xs = x.reshape(b * n, d)
+    h_state, out, prev_scale2 = xs, None, None
+    for i, blk in enumerate(dec.blocks):
+        if i == 0:
+            q1, s1 = O.row_quant_ck(O.rms_norm_f16(xs, _npy(blk.norm1_w), cfg.eps).astype(np.float32))
+        else:
+            h_state, q1, s1, _ = O.residual_rms_quant(h_state, out, _npy(prev_scale2), _npy(blk.norm1_w), cfg.eps)
+            xs = h_state
+        qkv = O.prequantized_linear(q1, s1, _npy(blk.qkv_q), _npy(blk.qkv_s), _npy(blk.qkv_b)).reshape(b, n, 3 * d)
+        q, k, v = O.qk_rope(qkv, cos, sin, cfg.heads, cfg.qk_eps)
+        att = O.attention(q.transpose(0, 2, 1, 3), k.transpose(0, 2, 1, 3), v.transpose(0, 2, 1, 3), 1.0 / 8.0)
+        y = att.transpose(0, 2, 1, 3).reshape(b * n, d).astype(np.float16)
+        qy, sy = O.row_quant_ck(y.astype(np.float32))
+        a = O.prequantized_linear(qy, sy, _npy(blk.out_q), _npy(blk.out_s), _npy(blk.out_b))
+        h_state, q2, s2, _ = O.residual_rms_quant(xs, a, _npy(blk.scale1), _npy(blk.norm2_w), cfg.eps)
+        act = O.ffn_up_swiglu(q2, s2, _npy(blk.up_q), _npy(blk.up_s), _npy(blk.up_b))
+        qf, sf = O.row_quant_ck(act.astype(np.float32))
+        out = O.prequantized_linear(qf, sf, _npy(blk.down_q), _npy(blk.down_s), _npy(blk.down_b))
+        prev_scale2 = blk.scale2
+    y = O.final_residual_layernorm(h_state, out, _npy(prev_scale2), _npy(dec.ln_w), _npy(dec.ln_b), cfg.eps)
+    return y.reshape(b, n, d)
+
+
+@pytest.mark.parametrize("blocks", [1, 2])
+def test_config2_int8_block_chain_matches_oracle(cuda_lib, blocks):
+    from h3vae_b200.model import DecoderConfig, H3Decoder
+    cfg = DecoderConfig(hidden=1024, heads=16, blocks=blocks, ffn=4096, rot_dims=48)
+    dec = H3Decoder(cfg, device="cuda", seed=11, int8=True)
+    grid = (4, 16, 16)
+    g = torch.Generator().manual_seed(2)
+    x = torch.randn(4, 1024, 1024, generator=g).half()
+    got = _npy(dec.transformer(x.cuda(), grid)).astype(np.float64)
+    ref = _oracle_int8_chain(dec, x.numpy(), grid).astype(np.float64)
+    rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    err = np.abs(got - ref)
+    print(f"config 2, {blocks} block(s): rel L2 {rel:.2e}, max abs {err.max():.3e} (|ref| max {np.abs(ref).max():.2f}),"
+          f" elements off by > 1e-2: {np.count_nonzero(err > 1e-2)} of {err.size}")
+    assert rel < 5e-3, rel
+    assert err.max() < 0.05 * np.abs(ref).max()
+
+
+def _stage1_operands(seed):
+    rng = np.random.default_rng(seed)
+    qx = rng.integers(-127, 128, size=(4, 128, 19, 258, 258), dtype=np.int8)
+    qx[:, :, :2] = 0                                         # the producer's two causal zero frames
+    qw = rng.integers(-127, 128, size=(128, 27 * 128), dtype=np.int8)
+    ws = (rng.random(128, dtype=np.float32) * 2e-4 + 2e-5).astype(np.float32)
+    bias = (rng.standard_normal(128) * 0.02).astype(np.float16)
+    return qx, qw, ws, bias
+
+
+SAMPLE_FRAMES = (0, 1, 2, 8, 16)
+SAMPLE_ROWS = (0, 1, 127, 254, 255)
+
+
+def test_stage1_int8_conv_full_size_sampled_rows(cuda_lib):
+    from h3vae_b200 import kernels as K
+    qx, qw, ws, bias = _stage1_operands(7)
+    sx = 0.0123
+    qx_d = torch.from_numpy(qx).cuda().contiguous(memory_format=CL3)
+    acc = torch.empty((4, 128, 17, 256, 256), dtype=torch.int32, device="cuda", memory_format=CL3)
+    out = K.conv3d_i8(qx_d, torch.tensor(sx, device="cuda"), torch.from_numpy(qw).cuda(),
+                      torch.from_numpy(ws).cuda(), torch.from_numpy(bias).cuda(), (3, 3, 3), causal_zero_frames=2,
+                      acc_out=acc)
+    g = torch.Generator(device="cuda").manual_seed(1)
+    res = (torch.randn((4, 128, 17, 256, 256), generator=g, device="cuda") * 0.5).half().contiguous(memory_format=CL3)
+    out_res = K.conv3d_i8(qx_d, torch.tensor(sx, device="cuda"), torch.from_numpy(qw).cuda(),
+                          torch.from_numpy(ws).cuda(), torch.from_numpy(bias).cuda(), (3, 3, 3), causal_zero_frames=2,
+                          residual=res)
+    torch.cuda.synchronize()
+    for b in range(4):
+        for od in SAMPLE_FRAMES:
+            for oh in SAMPLE_ROWS:
+                ref_acc = O.conv3d_int_acc(qx[b:b + 1, :, od:od + 3, oh:oh + 3, :], qw, (3, 3, 3))[0, :, 0, 0, :]
+                got_acc = _npy(acc[b, :, od, oh, :])
+                assert np.array_equal(got_acc, ref_acc), (b, od, oh, np.count_nonzero(got_acc != ref_acc))
+                ref = O.conv_epilogue(ref_acc[None, :, None, None, :], np.float32(sx), ws, bias)[0, :, 0, 0, :]
+                got = _npy(out[b, :, od, oh, :])
+                diff = np.abs(got.astype(np.float32) - ref.astype(np.float32))
+                assert np.all(diff <= 1e-2 + 1e-3 * np.abs(ref.astype(np.float32))), (b, od, oh, diff.max())
+                ref_r = (ref.astype(np.float32) + _npy(res[b, :, od, oh, :]).astype(np.float32)).astype(np.float16)
+                got_r = _npy(out_res[b, :, od, oh, :]).astype(np.float32)
+                diff = np.abs(got_r - ref_r.astype(np.float32))
+                assert np.all(diff <= 1e-2 + 1e-3 * np.abs(ref_r.astype(np.float32))), (b, od, oh, diff.max())
+
+
+def test_stage1_norm_producer_full_size(cuda_lib):
+    from h3vae_b200 import kernels as K
+    g = torch.Generator().manual_seed(5)
+    b, c, d, h, w = 4, 128, 17, 256, 256
+    x = (torch.randn((b, c, d, h, w), generator=g) * 1.3 + 0.2).half().contiguous(memory_format=CL3)
+    gamma = (1.0 + 0.1 * torch.randn(c, generator=g)).half()
+    beta = (0.1 * torch.randn(c, generator=g)).half()
+    pre = (0.05 * torch.randn(c, generator=g)).half()
+    q, s = K.norm_pad_quant(x.cuda(), gamma.cuda(), beta.cuda(), 1e-6, pre.cuda())
+    xn = x.numpy()
+    amax = 0.0
+    frames = {}
+    for bi in range(b):
+        for t in range(d):
+            z = O.norm_silu(xn[bi:bi + 1, :, t:t + 1], gamma.numpy(), beta.numpy(), 1e-6, pre.numpy())
+            amax = max(amax, float(np.abs(z).max()))
+            if (bi, t) in ((0, 0), (1, 7), (3, 16)):
+                frames[(bi, t)] = z
+    ref_s = O.tensor_scale(amax)
+    assert abs(float(s) - float(ref_s)) <= 1e-3 * float(ref_s), (float(s), float(ref_s))
+    for (bi, t), z in frames.items():
+        ref_q = O.quant_half_away(O.pad_reflect_causal(z)[:, :, 2:], float(s))[0, :, 0]   # [C, H+2, W+2]
+        got = _npy(q[bi, :, t + 2])
+        dq = np.abs(got.astype(np.int32) - ref_q.astype(np.int32))
+        assert dq.max() <= 1 and np.count_nonzero(dq) <= 1e-3 * dq.size, ((bi, t), dq.max(), np.count_nonzero(dq))
+    assert not _npy(q[:, :, :2]).any()                      # the two causal zero frames
+
+
+def _smooth_video(frames, size, seed):
+    g = torch.Generator().manual_seed(seed)
+    v = torch.randn(1, 3, frames, size // 8, size // 8, generator=g)
+    v = torch.nn.functional.interpolate(v, size=(frames, size, size), mode="trilinear", align_corners=False)
+    v = v / v.std()
+    return v.clamp(-1, 1).half()
+
+
+def _psnr(a, b):
+    mse = torch.mean((a.double() - b.double()) ** 2).item()
+    return 10 * math.log10(1.0 / max(mse, 1e-20))
+
+
+def test_int8_round_trip_psnr_against_fp16_round_trip(cuda_lib):
+    """north_star: end-to-end RGB PSNR >= 45 dB of the INT8 path against the fp16 path of the same
+    weights, on config-3 encoder tiles and config-4 decoder tiles (22 frames = two causal clips)."""
+    from h3vae_b200.runtime import H3VAEPyOptRuntime
+    common = dict(compile_decoder=False, compile_encoder=False, log_calls=False, tile_batch=4,
+                  encoder_staged_batch=4, decoder_tile_size=256, encoder_tile_size=256, tile_overlap_min=32)
+    rt8 = H3VAEPyOptRuntime(int8_encode=True, int8_decode=True, decode_fusions=True, **common)
+    rt16 = H3VAEPyOptRuntime(**common)
+    video = _smooth_video(22, 256, 4).cuda()
+    lat8, lat16 = rt8.encode(video), rt16.encode(video)
+    assert lat8.shape == lat16.shape == (1, 16, 7, 32, 32)
+    out8, out16 = rt8.decode(lat8.half()), rt16.decode(lat16.half())
+    assert out8.shape == out16.shape == (1, 3, 22, 256, 256)
+    inside = ((out16 > 0) & (out16 < 1)).float().mean().item()
+    psnr = _psnr(out8, out16)
+    psnr_dec = _psnr(rt8.decode(lat16.half()), out16)
+    lat_rel = ((lat8 - lat16).norm() / lat16.norm()).item()
+    print(f"INT8 vs fp16 round trip PSNR {psnr:.2f} dB (decode only {psnr_dec:.2f} dB), latent rel err "
+          f"{lat_rel:.4f}, unclamped fp16 pixels {inside:.1%}")
+    assert inside > 0.5            # a gate on saturated (clamped) pixels would say nothing
+    assert psnr >= 45.0, psnr
+    assert psnr_dec >= 45.0, psnr_dec

@@ -53,7 +53,7 @@ def test_ffn_up_swiglu(cuda_lib, m, f, k, with_bias):
     bias = b if with_bias else None
     act = K.gemm_i8_swiglu(torch.from_numpy(q).cuda(), torch.from_numpy(s).cuda(), torch.from_numpy(w).cuda(),
                            torch.from_numpy(ws).cuda(), None if bias is None else torch.from_numpy(bias).cuda())
-    _close(act.cpu().numpy(), O.ffn_up_swiglu(q, s, w, ws, bias), atol=2e-2)
+    _close(act.cpu().numpy(), O.ffn_up_swiglu(q, s, w, ws, bias))          # max-abs 1e-2, rel 1e-3
 
 
 @pytest.mark.parametrize("batch,tokens,heads,k,r", [(4, 1024, 16, 1024, 48), (2, 300, 4, 256, 48),
@@ -111,7 +111,10 @@ def test_ffn_up_swiglu_f16(cuda_lib, m, f, k, with_bias):
     bias = b if with_bias else None
     act = K.gemm_f16_swiglu(torch.from_numpy(a).cuda(), torch.from_numpy(w).cuda(),
                             None if bias is None else torch.from_numpy(bias).cuda())
-    _close(act.cpu().numpy(), O.ffn_up_swiglu_f16(a, w, bias), atol=2e-2)
+    # fp32 accumulation order differs from the oracle's float64 dot product, so a gate or up value can
+    # round to the neighbouring fp16 value; through silu(g) * u that moves act by up to ~2.3 fp16 ulps
+    # (2.3 * 2^-10 relative), hence rel 3e-3 here; the INT8 path above has exact sums and meets 1e-3
+    _close(act.cpu().numpy(), O.ffn_up_swiglu_f16(a, w, bias), atol=1e-2, rtol=3e-3)
 
 
 def test_gemm_f16_rejects_bad_arguments(cuda_lib):
