@@ -4,9 +4,11 @@ One step = encode + decode of the synthetic video through H3VAEPyOptRuntime (the
 first_stage_model API): 24 spatial tiles (tile 256, 32-px minimum overlap) x 8 causal 17-frame
 clips, encoded 4 clips per call (config 3 shape [4,3,17,256,256], every 3x3x3 residual conv on the
 INT8 tcgen05 kernel) and decoded 4 tiles per call (config 4 shape [4,16,5,32,32], 6 INT8
-transformer blocks), blended linearly and finalized to fp32 RGB.  With torchrun (one process per
-GPU) the tile batches are sharded over the ranks and the blend canvases are summed on rank 0
-with one NCCL reduce.
+transformer blocks), blended linearly and finalized to fp32 RGB.  124 frames encode to 37 latent
+frames and decode back to 124 (the reference's 17k+5 <-> 5k+2 contract).  With torchrun (one process
+per GPU) the tile batches are sharded over the ranks: rank 0 sends each rank the pixel window its
+encoder items read, and gathers every rank's latent / pixel canvas slab (NCCL point-to-point over
+NVLink).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -54,9 +56,13 @@ def parse_args():
     ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", choices=("video", "tile"), default="video",
+    ap.add_argument("--workload", choices=("video", "tile", "kernels"), default="video",
                     help="video: the config-5 round trip (the bench line); tile: one config-3 encoder call and "
-                         "one config-4 decoder call per step (small enough for ncu captures)")
+                         "one config-4 decoder call per step (small enough for ncu captures); kernels: the "
+                         "decoder GEMMs and attention at the real H3 shapes and the encoder conv calls the "
+                         "reference publishes, each timed alone with CUDA events")
+    ap.add_argument("--no-quality", action="store_true",
+                    help="skip the INT8-vs-fp16 round-trip PSNR measured after the timed region (N=1)")
     ap.add_argument("--tile-batch", type=int, default=4,
                     help="tile workload: clips per encoder call and tiles per decoder call (4 = configs 3/4)")
     ap.add_argument("--tile-part", choices=("both", "encoder", "decoder"), default="both",
@@ -188,29 +194,70 @@ def int8_ops_per_round_trip(cfg=None, dcfg=None) -> tuple[float, float]:
     return enc + per_tile * dec_tasks, attn * dec_tasks
 
 
-def cpu_conv_sample(seconds_budget: float = 15.0) -> dict:
-    """Time the oracle's INT8 conv (per-tensor quantization + exact integer conv + epilogue) on the
-    config-1 tensor [1,128,9,64,64] with all host threads; returns INT8 ops/s."""
-    import numpy as np
-    from oracle import h3vae_oracle as O
+def cpu_model_name() -> str:
+    try:
+        for line in subprocess.run(["lscpu"], capture_output=True, text=True, timeout=10).stdout.splitlines():
+            if line.lower().startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except (OSError, subprocess.SubprocessError):
+        pass
+    return "unknown"
+
+
+ENC_CROP = 64      # encoder work item sampled on a 64x64 window of its 256x256 tile (area ratio 16)
+DEC_CROP = 16      # decoder tile task sampled on a 16x16 window of its 32x32 latent tile (area ratio 4)
+
+
+def cpu_round_trip_sample(enc, dec, tiles: int, clips: int, dec_tasks: int, seed: int = 0) -> dict:
+    """The CPU restatement of the path (oracle.cpu_model: the reference's CPU arithmetic -- dequantized
+    fp32 INT8 convs as its CPU oracle computes them, the producers with their fp16 rounding points, fp32
+    convs rounded to fp16, the INT8 decoder block chain, torch SDPA on the CPU) on the host cores, per
+    the CPU-baseline plan: one encoder work item (one tile x one 17-frame clip) and one decoder tile task
+    (one tile x one 5-token chunk), each timed on a spatial crop and scaled to the full item by op count
+    (work linear in the positions x area ratio, attention x area ratio squared), then multiplied by the
+    item counts of the round trip.  Labelled "extrapolated"."""
+    from oracle import cpu_model as C
     torch.set_num_threads(os.cpu_count() or 1)
-    g = torch.Generator().manual_seed(0)
-    x = torch.randn(1, 128, 11, 66, 66, generator=g).half().numpy()
-    w = torch.randn(128, 128, 3, 3, 3, generator=g) / 3456 ** 0.5
-    qw, ws = O.prepare_int8_weight(w)
-    qwn, wsn = qw.numpy(), ws.numpy()
-    ops = 2 * 9 * 64 * 64 * 128 * 128 * 27
-    times = []
-    t_end = time.perf_counter() + seconds_budget
-    while time.perf_counter() < t_end or not times:
-        t0 = time.perf_counter()
-        O.int8_valid_conv3d(x, qwn, wsn, (3, 3, 3), bias=None)
-        times.append(time.perf_counter() - t0)
-        if len(times) >= 20:
-            break
-    best = float(np.median(times))
-    return {"ops_per_s": ops / best, "seconds_per_sample": best, "samples": len(times),
-            "cores": torch.get_num_threads()}
+    mean = torch.tensor([0.485, 0.456, 0.406])
+    std = torch.tensor([0.229, 0.224, 0.225])
+    t0 = time.perf_counter()
+    enc_s, enc_info = C.encoder_item_seconds(enc, 17, ENC_CROP, TILE, mean, std, seed)
+    dec_s, dec_info = C.decoder_task_seconds(dec, 5, DEC_CROP, TILE // 8, seed)
+    wall = time.perf_counter() - t0
+    total = enc_s * tiles * clips + dec_s * dec_tasks
+    return {"seconds": total, "encoder_item_s": enc_s, "decoder_task_s": dec_s, "sample_wall_s": wall,
+            "encoder_sample": enc_info, "decoder_sample": dec_info, "cores": torch.get_num_threads(),
+            "items": {"encoder": tiles * clips, "decoder": dec_tasks}}
+
+
+def cpu_models():
+    """Host copies of the bench runtime's encoder and decoder (same configs and seeds, so the same
+    random-init weights)."""
+    from h3vae_b200.model import DecoderConfig, EncoderConfig, H3Decoder, H3Encoder
+    return (H3Encoder(EncoderConfig(), device="cpu", seed=0),
+            H3Decoder(DecoderConfig(), device="cpu", seed=1, int8=True))
+
+
+def _round_trip_items(cfg=None, dcfg=None) -> tuple[int, int, int]:
+    from h3vae_b200 import tiling
+    from h3vae_b200.model import DecoderConfig, EncoderConfig
+    cfg = cfg or EncoderConfig()
+    dcfg = dcfg or DecoderConfig()
+    b, c, t, h, w = VIDEO_SHAPE
+    plan = tiling.TilePlan.build(h, w, TILE, OVERLAP, cfg.spatial_ratio)
+    clips = -(-t // 17)
+    lplan = plan.scaled(2 ** sum(dcfg.up_spatial))
+    return plan.rows * plan.cols, clips, lplan.rows * lplan.cols * clips
+
+
+def _cpu_baseline_line(sample: dict) -> dict:
+    return {"value": sample["seconds"], "unit": UNIT, "cores": sample["cores"], "kind": "port",
+            "cpu": cpu_model_name(),
+            "sample": (f"extrapolated: one encoder work item (1 tile x 1 17-frame clip, timed on a {ENC_CROP}x{ENC_CROP} "
+                       f"crop, {sample['encoder_item_s']:.2f} s scaled) x {sample['items']['encoder']} + one decoder "
+                       f"tile task (timed on a {DEC_CROP}x{DEC_CROP} latent crop, {sample['decoder_task_s']:.2f} s "
+                       f"scaled) x {sample['items']['decoder']}, oracle.cpu_model (reference CPU arithmetic) on "
+                       f"{sample['cores']} threads; {sample['sample_wall_s']:.1f} s of CPU work per sample")}
 
 
 # ---------------------------------------------------------------------------
@@ -245,30 +292,33 @@ def barrier(pg):
 
 
 def run_reference(args):
-    """The reference arm: the reference's own CPU implementation of the path is not runnable as a
-    whole (its model code is not distributed and its kernels are Triton/CK), so the oracle port of
-    its INT8 conv arithmetic is timed on the host cores on a bounded sample and extrapolated to the
-    round trip's INT8 op count."""
+    """The reference arm.  The reference's own implementation of this path is Triton/CK GPU code with no
+    CPU implementation, and its model code is not distributed, so the arm times the CPU restatement of its
+    arithmetic (oracle.cpu_model) on the host cores, on the same config-5 workload, model config and
+    weights as the b200 arm: every step is one encoder work item and one decoder tile task (bounded
+    spatial samples, scaled by op count) extrapolated to the round trip's item counts.  Under torchrun
+    rank 0 alone runs it."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    samples = []
+    enc, dec = cpu_models()
+    tiles, clips, dec_tasks = _round_trip_items()
     for _ in range(args.warmup):
-        cpu_conv_sample(2.0)
-    for _ in range(args.steps):
-        samples.append(cpu_conv_sample(5.0))
-    ops_s = statistics.median(s["ops_per_s"] for s in samples)
-    int8_ops, attn = int8_ops_per_round_trip()
-    value = (int8_ops + attn) / ops_s
+        cpu_round_trip_sample(enc, dec, tiles, clips, dec_tasks)
+    samples = [cpu_round_trip_sample(enc, dec, tiles, clips, dec_tasks, seed=k) for k in range(args.steps)]
+    value = statistics.mean(sm["seconds"] for sm in samples)
+    cpu = _cpu_baseline_line(samples[0])
+    cpu["value"] = value
     line = {"impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": value * 1e3, "higher_is_better": False,
-            "scaling": "strong", "vs_baseline": None, "dtype": "int8/fp16", "data": "synthetic",
-            "config": {"workload": "config5 full-video round trip (extrapolated from a CPU sample)",
-                       "video": list(VIDEO_SHAPE)},
-            "cpu_baseline": {"value": value, "unit": UNIT, "cores": samples[0]["cores"], "kind": "port",
-                             "sample": "oracle INT8 conv (per-tensor quant + exact int conv + epilogue) on the "
-                                       "config-1 tensor [1,128,9,64,64], extrapolated by the round trip's "
-                                       f"{int8_ops / 1e15:.3f} POP INT8 + {attn / 1e15:.3f} PFLOP attention"},
+            "scaling": "strong", "vs_baseline": None, "dtype": "int8 (dequantized fp32 CPU arithmetic), fp16",
+            "data": "synthetic (random-init H3-structured weights, seeded)",
+            "config": {"workload": "config5 full-video round trip (encode config3 tiles + decode config4 tiles), "
+                                   "extrapolated from one encoder work item and one decoder tile task per step",
+                       "video": list(VIDEO_SHAPE), "tile": TILE, "overlap_min": OVERLAP, "clip": 17,
+                       "encoder_items": tiles * clips, "decoder_tasks": dec_tasks},
+            "samples_s": [sm["seconds"] for sm in samples],
+            "cpu_baseline": cpu,
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -308,6 +358,99 @@ def run_tile(args):
                       "decoder_tile_ms": statistics.mean(dec), "steps": args.steps, "warmup": args.warmup}))
 
 
+# Reference timings (RTX PRO 5000, SM120) of the same operations, from the reference's own notes:
+# docs/int8_norm_producer_2026-10-02.md:94-97 (CK INT8 GEMMs at M = 7188),
+# docs/encoder_int8_analysis_2026-10-02.md:40-41 (INT8 conv op including its activation quantization).
+REF_SM120_MS = {"gemm_qkv": 0.398, "gemm_attn_out": 0.143, "gemm_ffn_up": 1.018, "gemm_ffn_down": 0.473,
+                "conv_c128": 4.222, "conv_c256": 3.403}
+
+
+def _time_launches(fn, steps: int, warmup: int, flush: torch.Tensor) -> list[float]:
+    """Milliseconds of each launch, CUDA events around the launch only; the L2 is flushed (a write
+    larger than its 126 MB) before every launch."""
+    for _ in range(warmup):
+        fn()
+    out = []
+    for _ in range(steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        fn()
+        e1.record()
+        torch.cuda.synchronize()
+        out.append(e0.elapsed_time(e1))
+    return out
+
+
+def run_kernels(args):
+    """The decoder GEMMs and attention at the real H3 shapes (4 tiles x 1797 tokens = 7188 rows, hidden
+    2048, 32 heads x 64, FFN 2 x 8192) and the encoder conv calls at the reference's published shapes,
+    beside the reference's SM120 timings of the same operations."""
+    from h3vae_b200 import kernels as K
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(0)
+    flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
+    steps, warmup = max(args.steps, 5), max(args.warmup, 3)
+    m, d, heads, ffn, tokens = 7188, 2048, 32, 8192, 1797
+    rows = []
+
+    def record(name, shape, ms_list, ops, unit="TOPS"):
+        ms = statistics.median(ms_list)
+        row = {"name": name, "shape": shape, "ms": ms, unit.lower(): ops / (ms * 1e-3) / 1e12}
+        if name in REF_SM120_MS:
+            row["ref_sm120_ms"] = REF_SM120_MS[name]
+        rows.append(row)
+
+    def i8(*shape):
+        return torch.randint(-127, 128, shape, generator=g, device=dev, dtype=torch.int8)
+
+    q = i8(m, d)
+    s = torch.rand((m, 1), generator=g, device=dev) * 0.02 + 0.001
+    for name, n, k, kind in (("gemm_qkv", 3 * d, d, "linear"), ("gemm_attn_out", d, d, "linear"),
+                             ("gemm_ffn_up", 2 * ffn, d, "linear"), ("gemm_ffn_down", d, ffn, "linear"),
+                             ("gemm_ffn_up_swiglu", 2 * ffn, d, "swiglu"), ("gemm_qkv_qknorm_rope", 3 * d, d, "qkv")):
+        a = q if k == d else i8(m, k)
+        w = i8(n, k)
+        ws = torch.rand(n, generator=g, device=dev) * 1e-3 + 1e-4
+        b = (torch.randn(n, generator=g, device=dev) * 0.02).half()
+        if kind == "linear":
+            fn = lambda a=a, w=w, ws=ws, b=b: K.gemm_i8(a, s, w, ws, b)          # noqa: E731
+        elif kind == "swiglu":
+            fn = lambda a=a, w=w, ws=ws, b=b: K.gemm_i8_swiglu(a, s, w, ws, b)   # noqa: E731
+        else:
+            ang = torch.rand((4, tokens, 1, 48), generator=g, device=dev) * 6.28
+            cos, sin = ang.cos().half(), ang.sin().half()
+            fn = lambda a=a, w=w, ws=ws, b=b: K.gemm_i8_qkv_rope(a, s, w, ws, b, 4, tokens, heads, cos, sin, 1e-6)  # noqa: E731
+        record(name, [m, n, k], _time_launches(fn, steps, warmup, flush), 2.0 * m * n * k)
+    qa, ka, va = (torch.randn((4, heads, tokens, 64), generator=g, device=dev).half() for _ in range(3))
+    flops = 4.0 * 4 * heads * tokens * tokens * 64
+    record("attention_tc", [4, heads, tokens, 64], _time_launches(lambda: K.attention_f16(qa, ka, va, 0.125), steps,
+                                                                  warmup, flush), flops, "TFLOPS")
+    sdpa = torch.nn.functional.scaled_dot_product_attention
+    record("attention_torch_sdpa", [4, heads, tokens, 64],
+           _time_launches(lambda: sdpa(qa, ka, va, scale=0.125), steps, warmup, flush), flops, "TFLOPS")
+    # encoder INT8 conv calls incl. their activation quantization (the norm producer), reference shapes
+    for name, c, hw in (("conv_c128", 128, 256), ("conv_c256", 256, 128)):
+        x = (torch.randn((1, c, 17, hw, hw), generator=g, device=dev)).half().contiguous(
+            memory_format=torch.channels_last_3d)
+        gam = torch.ones(c, device=dev, dtype=torch.float16)
+        bet = torch.zeros(c, device=dev, dtype=torch.float16)
+        w = i8(c, 27 * c)
+        ws = torch.rand(c, generator=g, device=dev) * 1e-3 + 1e-4
+
+        def conv_call(x=x, gam=gam, bet=bet, w=w, ws=ws):
+            qx, sx = K.norm_pad_quant(x, gam, bet, 1e-6)
+            return K.conv3d_i8(qx, sx, w, ws, None, (3, 3, 3), causal_zero_frames=2)
+        ops = 2.0 * hw * hw * c * c * 9 * sum(min(t + 1, 3) for t in range(17))
+        record(name, [1, c, 17, hw, hw], _time_launches(conv_call, steps, warmup, flush), ops)
+    print(json.dumps({"workload": "kernels", "device": torch.cuda.get_device_name(dev), "steps": steps,
+                      "warmup": warmup, "l2": "flushed (256 MB write) before every timed launch",
+                      "ref_source": "RTX PRO 5000 (SM120): docs/int8_norm_producer_2026-10-02.md:94-97, "
+                                    "docs/encoder_int8_analysis_2026-10-02.md:40-41",
+                      "kernels": rows}), flush=True)
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
@@ -315,6 +458,9 @@ def main():
         return
     if args.workload == "tile":
         run_tile(args)
+        return
+    if args.workload == "kernels":
+        run_kernels(args)
         return
     from h3vae_b200 import kernels as K
     from h3vae_b200.runtime import H3VAEPyOptRuntime
@@ -409,14 +555,28 @@ def main():
                "h2d_bytes_per_step": int(video.numel() * video.element_size()) if rank == 0 else 0,
                "d2h_bytes_per_step": int(host_out.numel() * 4) if rank == 0 else 0}
 
+    # ---- quality (north_star): INT8 round trip against the fp16 round trip of the same weights ----
+    quality = None
+    if world == 1 and not args.no_quality:
+        out8 = runtime.decode(fp16(runtime.encode(video)))
+        rt16 = H3VAEPyOptRuntime(device=str(dev), tile_batch=4, encoder_staged_batch=4, log_calls=False,
+                                 compile_decoder=False, compile_encoder=False, decoder_tile_size=TILE,
+                                 tile_overlap_min=OVERLAP)
+        out16 = rt16.decode(fp16(rt16.encode(video)))
+        mse = float(((out8 - out16).double() ** 2).mean())
+        quality = {"psnr_db": 10.0 * __import__("math").log10(1.0 / max(mse, 1e-20)),
+                   "against": "fp16 encode + fp16 decode of the same weights (int8_encode / int8_decode off)",
+                   "unclamped_fraction": float(((out16 > 0) & (out16 < 1)).float().mean()),
+                   "frames": int(out8.shape[2])}
+        del rt16, out8, out16
+        torch.cuda.empty_cache()
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        s = cpu_conv_sample(15.0)
-        int8_ops, attn = int8_ops_per_round_trip(runtime.encoder.cfg, runtime.decoder.cfg)
-        cpu = {"value": (int8_ops + attn) / s["ops_per_s"], "unit": UNIT, "cores": s["cores"], "kind": "port",
-               "sample": f"oracle INT8 conv on the config-1 tensor [1,128,9,64,64] ({s['samples']} runs, "
-                         f"{s['seconds_per_sample']:.2f} s each), extrapolated to the round trip's "
-                         f"{int8_ops / 1e15:.3f} POP INT8 + {attn / 1e15:.3f} PFLOP attention"}
+        tiles, clips, dec_tasks = _round_trip_items(runtime.encoder.cfg, runtime.decoder.cfg)
+        enc_cpu, dec_cpu = cpu_models()
+        cpu_round_trip_sample(enc_cpu, dec_cpu, tiles, clips, dec_tasks)     # warm-up
+        cpu = _cpu_baseline_line(cpu_round_trip_sample(enc_cpu, dec_cpu, tiles, clips, dec_tasks))
 
     if rank == 0:
         cl = clocks.summary()
@@ -442,7 +602,7 @@ def main():
                          "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum, conv launches of a "
                                            "tile-batch-1 encoder call scaled x4 (bytes per launch)",
                          "launches": conv_launches, "ms_total": conv_ms},
-            "e2e": e2e, "cpu_baseline": cpu, "clocks": cl, "gpu_launches": launches,
+            "e2e": e2e, "cpu_baseline": cpu, "clocks": cl, "gpu_launches": launches, "quality": quality,
         }
         print(json.dumps(line), flush=True)
     if pg is not None:

@@ -49,6 +49,11 @@ __device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
   asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
 }
+__device__ __forceinline__ uint64_t f2_sub(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("sub.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
@@ -59,6 +64,47 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
   return d;
 }
+
+// Base-2 exponentials of a pair of scores on the FMA pipe (packed f32x2), for
+// the share of the softmax that does not go to the SFU: Cody-Waite reduction
+// x = j + f with j = rint(x) (the 1.5 * 2^23 addition), f in [-1/2, 1/2], then
+// 2^f by a degree-3 polynomial and 2^j added into the exponent field.  The
+// coefficients are a minimax fit (Lawson's iteratively reweighted least
+// squares, relative error) of 2^f on [-1/2, 1/2] made for this kernel: max
+// relative error 7.5e-5, a sixth of an fp16 half-ulp, so P (rounded to fp16)
+// is unaffected in all but rare rounding ties.  x is clamped to >= -125 so
+// j + the polynomial's exponent stays a normal float (2^-125 rounds to 0 in
+// fp16, like the SFU's flushed result).
+__device__ __forceinline__ void ex2_poly_pair(uint64_t x, float& lo, float& hi) {
+  constexpr float kMagic = 12582912.0f;
+  float x0, x1;
+  f2_unpack(x, x0, x1);
+  const uint64_t xc = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t t = f2_add(xc, f2_pack(kMagic, kMagic));
+  const uint64_t fr = f2_sub(xc, f2_sub(t, f2_pack(kMagic, kMagic)));
+  uint64_t poly = f2_fma(f2_pack(0.05517132207751274f, 0.05517132207751274f), fr,
+                         f2_pack(0.24261054396629333f, 0.24261054396629333f));
+  poly = f2_fma(poly, fr, f2_pack(0.6932609677314758f, 0.6932609677314758f));
+  poly = f2_fma(poly, fr, f2_pack(0.9999281167984009f, 0.9999281167984009f));
+  float p0, p1, t0, t1;
+  f2_unpack(poly, p0, p1);
+  f2_unpack(t, t0, t1);
+  lo = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  hi = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Pairs of scores (out of every 8) whose exponentials run on the FMA pipe; the
+// rest use the SFU's ex2.approx.  The SFU issues 16 results per clock per SM,
+// the bound of a head-dim-64 softmax; moving a share to the FMA pipe balances
+// the two.
+#ifndef H3B_FA_EMU
+#define H3B_FA_EMU 3
+#endif
+// 1: the two query tiles' softmax warps take turns on the SFU (named-barrier
+// ping-pong); 0: both exponentiate whenever their scores are ready.
+#ifndef H3B_FA_PINGPONG
+#define H3B_FA_PINGPONG 1
+#endif
 
 constexpr int kFaM = 128;       // queries per tile
 constexpr int kFaTiles = 2;     // query tiles per CTA
@@ -218,13 +264,14 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // every barrier completes as often as it is waited on.
     constexpr int kSoftmaxThreads = 32 * kFaSoftmaxWarps * kFaTiles;
     auto exp_turn_begin = [&]() {
-      asm volatile("bar.sync %0, %1;" ::"r"(tile == 0 ? 1 : 2), "r"(kSoftmaxThreads) : "memory");
+      if (H3B_FA_PINGPONG)
+        asm volatile("bar.sync %0, %1;" ::"r"(tile == 0 ? 1 : 2), "r"(kSoftmaxThreads) : "memory");
     };
     auto exp_turn_end = [&](int jj) {
-      if (tile == 0 || jj + 1 < n_blocks)
+      if (H3B_FA_PINGPONG && (tile == 0 || jj + 1 < n_blocks))
         asm volatile("bar.arrive %0, %1;" ::"r"(tile == 0 ? 2 : 1), "r"(kSoftmaxThreads) : "memory");
     };
-    if (tile == 1) asm volatile("bar.arrive 1, %0;" ::"r"(kSoftmaxThreads) : "memory");
+    if (H3B_FA_PINGPONG && tile == 1) asm volatile("bar.arrive 1, %0;" ::"r"(kSoftmaxThreads) : "memory");
     for (int j = 0; j < n_blocks; ++j) {
       ok = __all_sync(0xffffffffu, ok && mbar_wait_u32(bar_s_full, j & 1, abort_flag));
       const int valid = p.kv_len - j * kFaN;
@@ -274,8 +321,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const int k = q * 8 + 2 * e;
-          const float p0 = ex2_approx(__fmaf_rn(__uint_as_float(sv_[k]), p.scale_log2, negm));
-          const float p1 = ex2_approx(__fmaf_rn(__uint_as_float(sv_[k + 1]), p.scale_log2, negm));
+          float p0, p1;
+          if (((q * 4 + e) & 7) < H3B_FA_EMU) {
+            ex2_poly_pair(f2_fma(f2_pack(__uint_as_float(sv_[k]), __uint_as_float(sv_[k + 1])),
+                                 f2_pack(p.scale_log2, p.scale_log2), f2_pack(negm, negm)),
+                          p0, p1);
+          } else {
+            p0 = ex2_approx(__fmaf_rn(__uint_as_float(sv_[k]), p.scale_log2, negm));
+            p1 = ex2_approx(__fmaf_rn(__uint_as_float(sv_[k + 1]), p.scale_log2, negm));
+          }
           sums[e] += p0 + p1;
           hv[e] = __floats2half2_rn(p0, p1);
         }

@@ -14,7 +14,6 @@
 //                       interior, INT8 with the per-tensor scale, or fp16 output.
 //   residual_pack_kernel, quantize kernels, finalize_pixels_kernel,
 //   blend_accumulate_kernel (one tile's weighted term added into the blend canvas).
-#include <mutex>
 
 #include "common.cuh"
 
@@ -894,15 +893,15 @@ int h3b_norm_pad_quant_token(const void* x, int64_t B, int64_t C, int64_t D, int
 // partials, per-frame statistics, per-channel min/max words and the absmax
 // word) lives in one file-scope device array instead of a caller workspace.
 // The host never passes the array's name to a kernel (in host code that name
-// is only a stand-in): the device address is resolved once per device with
-// cudaGetSymbolAddress while that device is current, and cached.
+// is only a stand-in): every call resolves the array's device address with
+// cudaGetSymbolAddress while the calling device is current.  Nothing is
+// cached, so the address stays right after a cudaDeviceReset or a primary
+// context re-creation reloads the module (the lookup is a table access once
+// the module is loaded; the first call on a device loads it).
 // ---------------------------------------------------------------------------
 namespace {
 constexpr size_t kNormStaticScratchBytes = size_t(4) << 20;  // 4 MiB, held by every device that loads the library
 __device__ __align__(256) unsigned char g_norm_static_scratch[kNormStaticScratchBytes];
-std::mutex g_norm_static_mutex;
-constexpr int kMaxDevices = 128;
-void* g_norm_static_ptr[kMaxDevices] = {};
 }  // namespace
 
 int h3b_norm_pad_quant_noalloc(const void* x, int64_t B, int64_t C, int64_t D, int64_t H, int64_t W,
@@ -923,21 +922,13 @@ int h3b_norm_pad_quant_noalloc(const void* x, int64_t B, int64_t C, int64_t D, i
                                name, need, kNormStaticScratchBytes);
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+  if (e != cudaSuccess || dev < 0)
     return h3b_host::set_error(H3B_ECUDA, "%s: no usable current device (%s)", name, cudaGetErrorString(e));
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(g_norm_static_mutex);
-    if (g_norm_static_ptr[dev] == nullptr) {
-      void* ptr = nullptr;
-      e = cudaGetSymbolAddress(&ptr, g_norm_static_scratch);
-      if (e != cudaSuccess || ptr == nullptr)
-        return h3b_host::set_error(H3B_ECUDA, "%s: cudaGetSymbolAddress of the static scratch failed: %s", name,
-                                   cudaGetErrorString(e));
-      g_norm_static_ptr[dev] = ptr;
-    }
-    scratch = g_norm_static_ptr[dev];
-  }
+  e = cudaGetSymbolAddress(&scratch, g_norm_static_scratch);
+  if (e != cudaSuccess || scratch == nullptr)
+    return h3b_host::set_error(H3B_ECUDA, "%s: cudaGetSymbolAddress of the static scratch failed: %s", name,
+                               cudaGetErrorString(e));
   // h3b_norm_pad_quant clears the min / max / absmax words on the stream before
   // use and fully rewrites the partials and statistics, so stale contents from
   // an earlier call never leak into this one.

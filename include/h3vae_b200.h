@@ -191,9 +191,11 @@ int h3b_norm_pad_quant(const void* x, int64_t B, int64_t C, int64_t D, int64_t H
  * every GPU loading the library holds until exit; shapes whose
  * h3b_norm_workspace_size() exceeds 4 MiB are rejected with H3B_EUNSUPPORTED
  * (e.g. B=4, C=128, D=17, 256x256 needs about 1.2 MiB and fits).
- * The first call on a device resolves the array's address for that device
- * (cudaGetSymbolAddress with the device current); make that first call before
- * any stream capture.  All calls share the one array: calls that overlap on
+ * Every call resolves the array's address on the current device
+ * (cudaGetSymbolAddress; nothing is cached, so a device reset does not leave
+ * a stale address); the first call on a device also loads the module there,
+ * so make that first call before any stream capture.  All calls share the one
+ * array, which keeps the last call's contents: calls that overlap on
  * the GPU (other streams, other host threads) race on it, so serialize them.
  * No cudaMalloc / cudaFree or allocating library routine is called.
  * No counterpart in the reference: its producer always allocates its scratch

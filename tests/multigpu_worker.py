@@ -1,6 +1,7 @@
 """torchrun worker for tests/test_multigpu_gpu.py: every rank builds the same seeded runtime, runs
-one encode + decode of a seeded video with the tile work split over the ranks, and rank 0 saves
-the latents and pixels.  Not collected by pytest (no test_ prefix)."""
+one encode + decode of a seeded video with the tile work split over the ranks (device-resident, then
+through pinned host buffers on rank 0), and rank 0 saves the latents and pixels.  Not collected by
+pytest (no test_ prefix)."""
 from __future__ import annotations
 
 import datetime
@@ -40,8 +41,16 @@ def main():
         video = make_video(dev) if dist.get_rank() == 0 else None
         lat = run.encode(video)
         pix = run.decode(None if lat is None else lat.half())
+        # the host-buffer path: a pinned host video in, pixels into a pinned host buffer
+        host_video = video.cpu().pin_memory() if dist.get_rank() == 0 else None
+        lat_h = run.encode(host_video)
+        buf = None
         if dist.get_rank() == 0:
-            torch.save({"lat": lat.cpu(), "pix": pix.cpu()}, out)
+            buf = torch.empty(run.decode_output_shape(lat_h.shape), dtype=torch.float32).pin_memory()
+        res = run.decode(None if lat_h is None else lat_h.half(), output_buffer=buf)
+        if dist.get_rank() == 0:
+            assert res is buf
+            torch.save({"lat": lat.cpu(), "pix": pix.cpu(), "lat_host": lat_h.cpu(), "pix_host": buf.clone()}, out)
         torch.cuda.synchronize()
         dist.barrier()
     finally:
