@@ -98,7 +98,7 @@ __device__ __forceinline__ void ex2_poly_pair(uint64_t x, float& lo, float& hi) 
 // the bound of a head-dim-64 softmax; moving a share to the FMA pipe balances
 // the two.
 #ifndef H3B_FA_EMU
-#define H3B_FA_EMU 3
+#define H3B_FA_EMU 0
 #endif
 // 1: the two query tiles' softmax warps take turns on the SFU (named-barrier
 // ping-pong); 0: both exponentiate whenever their scores are ready.
