@@ -22,9 +22,11 @@ opt/decoder_fused_qk_rope.py:56-74, opt/decoder_final_norm.py:35-72):
      -> INT8 FFN-up GEMM with fused SwiGLU -> row INT8 -> INT8 down-proj
   final residual + LayerNorm -> causal conv3d upsampling stages (fp16) -> RGB.
 
-INT8 convolutions and linears run on the tcgen05 kernels; the fp16 convolutions outside the
-INT8 scope (conv_in, strided downsamples, 1x1x1 shortcuts, conv_out and the decoder's
-upsampling convs, which the reference also leaves in fp16) use cuDNN through torch.
+INT8 convolutions and linears run on the tcgen05 kernels, and so do the fp16 convolutions outside
+the INT8 scope (the encoder's input conv, strided downsamples, 1x1x1 shortcuts, conv_out and the
+decoder's upsampling and RGB convs, which the reference leaves in fp16 on cuDNN).  Two narrow convs
+stay on cuDNN through torch: the decoder's 16-channel latent conv-in and the encoder's 32-channel
+1x1x1 quant conv, whose inputs are narrower than one 128-byte K row of the tcgen05 kernels.
 """
 from __future__ import annotations
 
@@ -372,13 +374,14 @@ class H3Decoder:
         return f
 
     def _rope(self, b, t, h, w):
-        key = (t, h, w)
+        """cos, sin fp16 [b, n, 1, rot_dims] for a (t, h, w) token grid, built once per shape."""
+        key = (b, t, h, w)
         if key not in self._rope_cache:
-            self._rope_cache[key] = rope_tables(t, h, w, self.cfg.rot_dims, self.device)
-        cos, sin = self._rope_cache[key]
-        n = t * h * w
-        return (cos.view(1, n, 1, -1).expand(b, n, 1, cos.shape[-1]).contiguous(),
-                sin.view(1, n, 1, -1).expand(b, n, 1, sin.shape[-1]).contiguous())
+            cos, sin = rope_tables(t, h, w, self.cfg.rot_dims, self.device)
+            n = t * h * w
+            self._rope_cache[key] = (cos.view(1, n, 1, -1).expand(b, n, 1, cos.shape[-1]).contiguous(),
+                                     sin.view(1, n, 1, -1).expand(b, n, 1, sin.shape[-1]).contiguous())
+        return self._rope_cache[key]
 
     def transformer_fp16(self, x: torch.Tensor, grid: tuple[int, int, int]) -> torch.Tensor:
         """fp16 profile of the block chain (ref: opt/int8_norm_quant.py:106-124 block structure;
@@ -387,19 +390,25 @@ class H3Decoder:
         b, n, d = x.shape
         cos, sin = self._rope(b, *grid)
         x = x.reshape(b * n, d).contiguous()
-        for blk in self.blocks:
-            n1 = K.rms_norm_f16(x, blk.norm1_w, cfg.eps)
+        h, out, prev_scale2 = x, None, None
+        for i, blk in enumerate(self.blocks):
+            if i == 0:
+                n1 = K.rms_norm_f16(x, blk.norm1_w, cfg.eps)
+            else:
+                # x = h + out * scale2 (in place) and its RMSNorm in one pass
+                h, _, _, n1 = K.residual_rms_quant(h, out, prev_scale2, blk.norm1_w, cfg.eps, h_out=h,
+                                                   return_norm=True)
+                x = h
             qkv = K.gemm_f16(n1, blk.qkv_w, blk.qkv_b).view(b, n, 3 * d)
             q, k = K.qk_rope(qkv, cos, sin, cfg.heads, cfg.qk_eps)
             v = qkv.view(b, n, cfg.heads, 192)[..., 128:]
             y = K.attention_f16(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), 1.0 / 8.0)
             a = K.gemm_f16(y.transpose(1, 2).reshape(b * n, d), blk.out_w, blk.out_b)
-            h = torch.addcmul(x.float(), a.float(), blk.scale1.float()).half()
-            n2 = K.rms_norm_f16(h, blk.norm2_w, cfg.eps)
+            h, _, _, n2 = K.residual_rms_quant(x, a, blk.scale1, blk.norm2_w, cfg.eps, return_norm=True)
             act = K.gemm_f16_swiglu(n2, blk.up_w, blk.up_b)
             out = K.gemm_f16(act, blk.down_w, blk.down_b)
-            x = torch.addcmul(h.float(), out.float(), blk.scale2.float()).half()
-        y = F.layer_norm(x.float(), (d,), self.ln_w.float(), self.ln_b.float(), cfg.eps).half()
+            prev_scale2 = blk.scale2
+        y = K.final_residual_layernorm(h, out, prev_scale2, self.ln_w, self.ln_b, cfg.eps)
         return y.view(b, n, d)
 
     def transformer(self, x: torch.Tensor, grid: tuple[int, int, int]) -> torch.Tensor:

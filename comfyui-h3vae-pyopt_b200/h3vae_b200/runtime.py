@@ -458,16 +458,23 @@ class H3VAEPyOptRuntime(torch.nn.Module):
                 arrived[g] = None
             py, px = plan.ys[i] - origin[1], plan.xs[j] - origin[2]
             tile_px = xv[..., py:py + plan.hs[i], px:px + plan.ws[j]]
-            batch = []
-            for bi in range(b):
-                for c in cs:
-                    f0 = c * clip_len - origin[0]
-                    clip = tile_px[bi:bi + 1, :, f0:f0 + clip_len]
-                    if clip.shape[2] < clip_len:   # pad the last clip by repeating its last frame
-                        rep = clip[:, :, -1:].expand(-1, -1, clip_len - clip.shape[2], -1, -1)
-                        clip = torch.cat([clip, rep], dim=2)
-                    batch.append(clip)
-            clip_batch = torch.cat(batch, 0)
+            f_first = cs[0] * clip_len - origin[0]
+            if b == 1 and tile_px.shape[2] - f_first >= len(cs) * clip_len:
+                # whole consecutive clips of one video: a strided view [clips, 3, clip, h, w] of the
+                # tile (batch stride = one clip of frames), no copy
+                v = tile_px[0, :, f_first:f_first + len(cs) * clip_len]
+                clip_batch = v.unflatten(1, (len(cs), clip_len)).transpose(0, 1)
+            else:
+                batch = []
+                for bi in range(b):
+                    for c in cs:
+                        f0 = c * clip_len - origin[0]
+                        clip = tile_px[bi:bi + 1, :, f0:f0 + clip_len]
+                        if clip.shape[2] < clip_len:   # pad the last clip by repeating its last frame
+                            rep = clip[:, :, -1:].expand(-1, -1, clip_len - clip.shape[2], -1, -1)
+                            clip = torch.cat([clip, rep], dim=2)
+                        batch.append(clip)
+                clip_batch = torch.cat(batch, 0)
             if clip_batch.dtype == torch.float16:
                 # normalization fused into the encoder's input conv
                 moments = self.encoder(clip_batch, norm=(self._img_mean, self._img_std))

@@ -1,7 +1,7 @@
 """Generate tests/golden/golden_v1.npz from the reference's own CPU functions.
 
 Run once in a container where the reference checkout (fishelegs/ComfyUI-H3VAE-PyOpt 0.2.0) is
-available, e.g.  python tests/golden/make_golden.py /path/to/reference
+available; the checkout path is a required argument:  python tests/golden/make_golden.py <checkout>
 The GPU box never runs this script; the tests read only the committed .npz.
 
 Vectors produced (all seeded):
@@ -95,4 +95,6 @@ def main(ref_root: str) -> None:
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: make_golden.py <path-to-reference-checkout>")
+    main(sys.argv[1])
