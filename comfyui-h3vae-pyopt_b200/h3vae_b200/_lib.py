@@ -58,6 +58,11 @@ _SIGNATURES = {
                             c_void_p, c_int64, c_void_p, c_void_p]),
     "h3b_gemm_i8_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
                                    c_void_p, c_void_p]),
+    "h3b_gemm_i8_residual_parts": (c_int64, [c_int64]),
+    "h3b_gemm_i8_residual": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,
+                                     c_void_p, c_void_p, c_int, c_void_p, c_int64, c_void_p, c_void_p]),
+    "h3b_rms_quant_parts": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_int64, c_int64, c_float, c_void_p,
+                                    c_void_p, c_void_p, c_void_p]),
     "h3b_gemm_f16": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
     "h3b_gemm_f16_swiglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "h3b_gemm_i8_qkv_rope": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64,

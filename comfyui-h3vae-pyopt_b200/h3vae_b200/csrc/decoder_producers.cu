@@ -436,6 +436,80 @@ __global__ void __launch_bounds__(256) residual_rms_quant_fast_kernel(
   row_quant_fast_store<WPR>(hv, amax, valid, row, wr, lane, q, s, K, red);
 }
 
+// Sum of a row's partial sums of squares in a fixed order (the residual GEMM
+// epilogue wrote nparts of them), then inv = rsqrt(sum / K + eps).
+__device__ __forceinline__ float row_inv_from_parts(const float* __restrict__ parts, int nparts, int K, float eps) {
+  float ss = 0.0f;
+  for (int i = 0; i < nparts; ++i) ss = __fadd_rn(ss, __ldg(parts + i));
+  return rsqrtf(__fadd_rn(__fmul_rn(ss, 1.0f / static_cast<float>(K)), eps));
+}
+
+// act = fp16(h * inv * w) and row quantization, for h written by the residual
+// GEMM epilogue together with the row's partial sums of squares (K a multiple
+// of 1024: WPR warps per row as in the other fast row kernels).
+template <int WPR>
+__global__ void __launch_bounds__(256) rms_quant_parts_fast_kernel(const __half* __restrict__ h,
+                                                                   const float* __restrict__ parts, int nparts,
+                                                                   const __half* __restrict__ w, int64_t M, int K,
+                                                                   float eps, int8_t* __restrict__ q,
+                                                                   float* __restrict__ s,
+                                                                   __half* __restrict__ norm_out) {
+  __shared__ float red[8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int wr = warp % WPR;
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * (8 / WPR) + warp / WPR;
+  const bool valid = row < M;
+  const float inv = valid ? row_inv_from_parts(parts + row * nparts, nparts, K, eps) : 0.0f;
+  uint4 act[kFastV];
+  float amax = 0.0f;
+#pragma unroll
+  for (int v = 0; v < kFastV; ++v) {
+    const int vec = (v * WPR + wr) * 32 + lane;
+    const uint4 hr = valid ? __ldg(reinterpret_cast<const uint4*>(h + row * K) + vec) : make_uint4(0, 0, 0, 0);
+    const uint4 wr4 = __ldg(reinterpret_cast<const uint4*>(w) + vec);
+    const __half2* hh = reinterpret_cast<const __half2*>(&hr);
+    const __half2* wh = reinterpret_cast<const __half2*>(&wr4);
+    uint32_t ow[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 t = f2x_mul(f2x_mul(__half22float2(hh[e]), make_float2(inv, inv)), __half22float2(wh[e]));
+      const __half2 r = __floats2half2_rn(t.x, t.y);
+      ow[e] = *reinterpret_cast<const uint32_t*>(&r);
+    }
+    act[v] = make_uint4(ow[0], ow[1], ow[2], ow[3]);
+    amax = absmax_h8(act[v], amax);
+    if (valid && norm_out != nullptr) reinterpret_cast<uint4*>(norm_out + row * K)[vec] = act[v];
+  }
+  row_quant_fast_store<WPR>(act, amax, valid, row, wr, lane, q, s, K, red);
+}
+
+// The same for any width: one CTA per row.
+template <int MAXV>
+__global__ void __launch_bounds__(kRowThreads) rms_quant_parts_kernel(const __half* __restrict__ h,
+                                                                      const float* __restrict__ parts, int nparts,
+                                                                      const __half* __restrict__ w, int K, float eps,
+                                                                      int8_t* __restrict__ q, float* __restrict__ s,
+                                                                      __half* __restrict__ norm_out) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const int nvec = K / 8;
+  const float inv = row_inv_from_parts(parts + row * nparts, nparts, K, eps);
+  float act[MAXV][8];
+#pragma unroll
+  for (int i = 0; i < MAXV; ++i) {
+    const int v = threadIdx.x + i * kRowThreads;
+    if (v < nvec) {
+      float hv[8], wv[8];
+      ld8(h + row * K + v * 8, hv);
+      ld8(w + v * 8, wv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) act[i][j] = round_fp16(__fmul_rn(__fmul_rn(hv[j], inv), wv[j]));
+      if (norm_out != nullptr) st8(norm_out + row * K + v * 8, act[i]);
+    }
+  }
+  row_quantize_store<MAXV>(act, nvec, q + row * K, s + row, red);
+}
+
 // Standalone QK RMSNorm + rotary: one thread per (token, head).
 __global__ void qk_rope_kernel(const __half* __restrict__ qkv, const __half* __restrict__ cos_t,
                                const __half* __restrict__ sin_t, int64_t rows, int heads, int R, float eps,
@@ -515,6 +589,15 @@ struct LaunchResidualRms {
     residual_rms_quant_kernel<V><<<(unsigned)M, kRowThreads, 0, st>>>(x, a, g, w, K, eps, round_stats, h, q, s,
                                                                       norm_out);
     return h3b_host::check_launch("h3b_residual_rms_quant");
+  }
+};
+
+template <int V>
+struct LaunchRmsParts {
+  static int run(const __half* h, const float* parts, int nparts, const __half* w, int64_t M, int K, float eps,
+                 int8_t* q, float* s, __half* norm_out, cudaStream_t st) {
+    rms_quant_parts_kernel<V><<<(unsigned)M, kRowThreads, 0, st>>>(h, parts, nparts, w, K, eps, q, s, norm_out);
+    return h3b_host::check_launch("h3b_rms_quant_parts");
   }
 };
 
@@ -605,6 +688,38 @@ int h3b_residual_rms_quant(const void* x, const void* a, const void* g, const vo
                                           static_cast<const __half*>(g), static_cast<const __half*>(w), M, (int)K, eps,
                                           round_stats, static_cast<__half*>(h), q, s, static_cast<__half*>(norm_out),
                                           reinterpret_cast<cudaStream_t>(stream));
+}
+
+int h3b_rms_quant_parts(const void* h, const float* row_sumsq, int64_t parts, const void* w, int64_t M, int64_t K,
+                        float eps, int8_t* q, float* s, void* norm_out, h3b_stream_t stream) {
+  const char* name = "h3b_rms_quant_parts";
+  if (!h || !row_sumsq || !w || !q || !s) return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  int rc = row_check(M, K, name);
+  if (rc) return rc;
+  if (parts <= 0 || parts > 4096) return h3b_host::set_error(H3B_EINVAL, "%s: parts must be in [1, 4096]", name);
+  for (const void* p : std::initializer_list<const void*>{h, w})
+    if (!al16(p)) return h3b_host::set_error(H3B_EINVAL, "%s: tensors must be 16-byte aligned", name);
+  if (norm_out && !al16(norm_out)) return h3b_host::set_error(H3B_EINVAL, "%s: norm_out must be 16-byte aligned", name);
+  const cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const __half* hh = static_cast<const __half*>(h);
+  const __half* wh = static_cast<const __half*>(w);
+  __half* nh = static_cast<__half*>(norm_out);
+  if (fast_row_width(K) && al16(q)) {
+    const int np = (int)parts;
+    switch (K / 1024) {
+      case 1: rms_quant_parts_fast_kernel<1><<<fast_row_grid(M, 1), 256, 0, st>>>(hh, row_sumsq, np, wh, M, (int)K,
+                                                                                    eps, q, s, nh); break;
+      case 2: rms_quant_parts_fast_kernel<2><<<fast_row_grid(M, 2), 256, 0, st>>>(hh, row_sumsq, np, wh, M, (int)K,
+                                                                                    eps, q, s, nh); break;
+      case 4: rms_quant_parts_fast_kernel<4><<<fast_row_grid(M, 4), 256, 0, st>>>(hh, row_sumsq, np, wh, M, (int)K,
+                                                                                    eps, q, s, nh); break;
+      default: rms_quant_parts_fast_kernel<8><<<fast_row_grid(M, 8), 256, 0, st>>>(hh, row_sumsq, np, wh, M, (int)K,
+                                                                                     eps, q, s, nh); break;
+    }
+    return h3b_host::check_launch(name);
+  }
+  return dispatch_maxv<LaunchRmsParts>(K, hh, static_cast<const float*>(row_sumsq), (int)parts, wh, M, (int)K, eps, q,
+                                       s, nh, st);
 }
 
 int h3b_rms_norm_f16(const void* x, const void* gamma, int64_t M, int64_t K, float eps, void* y, h3b_stream_t stream) {

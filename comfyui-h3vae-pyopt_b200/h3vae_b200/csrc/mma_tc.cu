@@ -33,7 +33,11 @@
 namespace h3b {
 
 enum class AMode : int { kGemm2D = 0, kConv5D = 1 };
-enum class Epi : int { kLinear = 0, kConv = 1, kSwiGLU = 2, kQkvRope = 3 };
+enum class Epi : int { kLinear = 0, kConv = 1, kSwiGLU = 2, kQkvRope = 3, kResidual = 4 };
+
+// fp32 column constants staged per tile: weight scale and bias, plus the
+// residual gate for the residual epilogue.
+__host__ __device__ constexpr int cst_arrays(Epi ep) { return ep == Epi::kResidual ? 3 : 2; }
 
 struct MmaParams {
   int M, N, K;          // GEMM view (conv: N = out channels)
@@ -54,7 +58,12 @@ struct MmaParams {
   int64_t ldo;           // GEMM row stride of out
   int64_t osB, osD, osH, osW;
   int32_t* acc_out;
-  const __half* residual;  // conv: optional fp16 tensor added after the fp16 rounding (same strides as out)
+  const __half* residual;  // conv: optional fp16 tensor added after the fp16 rounding (same strides as out);
+                           // residual GEMM: the block input x [M, ldo]
+  // residual GEMM (attention-out + residual + RMS statistics)
+  const __half* gate;      // per-column residual gate g [N]
+  float* row_sumsq;        // [M, 2 * n_tiles] per-row partial sums of raw^2 (or h^2 with round_stats)
+  int round_stats;
   // SwiGLU
   int F;
   // QKV + RoPE
@@ -270,7 +279,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                   const MmaParams p) {
   static_assert(MT == 1 || MT == 2, "one or two M tiles per CTA tile");
   static_assert(MT == 1 || EP == Epi::kConv || EP == Epi::kLinear, "paired M tiles: conv / linear epilogues only");
-  static_assert(!F16 || EP != Epi::kQkvRope, "fp16 operands: conv, linear and SwiGLU epilogues");
+  static_assert(!F16 || (EP != Epi::kQkvRope && EP != Epi::kResidual), "fp16 operands: conv, linear and SwiGLU epilogues");
+  static_assert(EP != Epi::kResidual || (MT == 1 && AM == AMode::kGemm2D), "residual epilogue: GEMM, one M tile");
+  constexpr int kCstArrays = cst_arrays(EP);
   constexpr int kKE = F16 ? 64 : 128;   // K elements per 128-byte k-block
   constexpr uint32_t kBTileBytes = BN * kBK;
   constexpr uint32_t kAStageBytes = MT * kATileBytes;
@@ -290,10 +301,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty_bar = bars + 2 * STAGES + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-  // [2 buffers][scale | bias][BN] fp32 column constants of the epilogue, then
-  // one 2 KB load/store staging buffer per epilogue warp
+  // [2 buffers][scale | bias (| gate)][BN] fp32 column constants of the
+  // epilogue, then one 2 KB load/store staging buffer per epilogue warp
   float* cst = reinterpret_cast<float*>(smem + STAGES * kStageBytes + 256);
-  const uint32_t stage_base = smem_u32(cst + 2 * 2 * BN);
+  const uint32_t stage_base = smem_u32(cst + 2 * kCstArrays * BN);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -462,9 +473,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     // weight scale and bias of column etid of the tile's N range (SwiGLU: gate
     // columns in [0, BN/2), the matching up columns in [BN/2, BN)).  They are
     // loaded one tile ahead so the global-load latency hides behind a tile.
-    auto load_column = [&](int tile, float& w, float& bv) {
+    auto load_column = [&](int tile, float& w, float& bv, float& gv) {
       w = 1.0f;
       bv = 0.0f;
+      gv = 0.0f;
       if (tile >= num_tiles || etid >= BN) return;
       const int n_tile = tile % p.n_tiles;
       int col;
@@ -480,9 +492,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!in) return;
       if constexpr (!F16) w = __ldg(p.w_scale + col);
       if (p.bias != nullptr) bv = __half2float(p.bias[col]);
+      if constexpr (EP == Epi::kResidual) gv = __half2float(p.gate[col]);
     };
-    float next_w, next_b;
-    load_column(blockIdx.x, next_w, next_b);
+    float next_w, next_b, next_g;
+    load_column(blockIdx.x, next_w, next_b, next_g);
     uint32_t local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int m_group = tile / p.n_tiles;
@@ -492,17 +505,19 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Double-buffered constants: every epilogue warp has passed the barrier
       // of tile local-1, hence finished tile local-2, before buffer local&1 is
       // rewritten here.
-      float* cw = cst + (local & 1u) * (2 * BN);
+      float* cw = cst + (local & 1u) * (kCstArrays * BN);
       float* cb = cw + BN;
+      float* cg = cb + BN;   // residual gate (residual epilogue only)
       if (etid < BN) {
         cw[etid] = next_w;
         cb[etid] = next_b;
+        if constexpr (EP == Epi::kResidual) cg[etid] = next_g;
       }
-      load_column(tile + gridDim.x, next_w, next_b);
+      load_column(tile + gridDim.x, next_w, next_b, next_g);
       // Row data that does not come from the MMA is fetched before the wait.
       float sx_pre = 0.0f;
       int64_t m_pre = 0;
-      if constexpr (EP == Epi::kLinear || EP == Epi::kSwiGLU || EP == Epi::kQkvRope) {
+      if constexpr (EP == Epi::kLinear || EP == Epi::kSwiGLU || EP == Epi::kQkvRope || EP == Epi::kResidual) {
         m_pre = static_cast<int64_t>(m_group * MT) * kBM + row;
         if (!F16 && MT == 1 && m_pre < p.M) sx_pre = __ldg(p.a_scale + m_pre);
       }
@@ -594,6 +609,71 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
+      } else if constexpr (EP == Epi::kResidual) {
+        // Attention-out + residual: a = fp16(fma(acc * sx, ws, b)) (the linear's
+        // fp16 output), raw = fma(a, g, x), h = fp16(raw) is written in place of
+        // a, and the row's sum of raw^2 over the columns this warp handles goes
+        // to row_sumsq[m, 2 * n_tile + half]; the RMSNorm + row quantization
+        // kernel adds the row's partials in a fixed order.
+        const uint32_t t_row = t_acc;
+        const int64_t m = m_pre;
+        const bool valid = m < p.M;
+        const float sx = sx_pre;
+        const bool vec_ok = (p.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(p.out) & 15u) == 0 &&
+                            (reinterpret_cast<uintptr_t>(p.residual) & 15u) == 0;
+        const int64_t m_warp = m - lane;
+        const int valid_rows = static_cast<int>(p.M - m_warp < 32 ? p.M - m_warp : 32);
+        float ss = 0.0f;
+#pragma unroll 1
+        for (int c = half; c < BN / 32; c += 2) {
+          uint32_t r[32];
+          tmem_ld32(t_row + c * 32, r);
+          tmem_ld_wait();
+          const int n0 = n_tile * BN + c * 32;
+          const int valid_cols = p.N - n0;
+          if (valid_cols >= 32 && vec_ok && valid_rows > 0) {
+            float v[32];
+            dequant_chunk<false>(r, sx, cw + c * 32, cb + c * 32, v);
+            uint4 xr[4];
+            load_chunk32_staged(stage, p.residual + m_warp * p.ldo + n0, p.ldo, valid_rows, xr);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const __half2* xh = reinterpret_cast<const __half2*>(&xr[k]);
+              const float4 g0 = *reinterpret_cast<const float4*>(cg + c * 32 + k * 8);
+              const float4 g1 = *reinterpret_cast<const float4*>(cg + c * 32 + k * 8 + 4);
+              const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float2 xf = __half22float2(xh[j]);
+                const float2 raw = f2x_fma(make_float2(round_fp16(v[k * 8 + 2 * j]), round_fp16(v[k * 8 + 2 * j + 1])),
+                                           make_float2(gg[2 * j], gg[2 * j + 1]), xf);
+                const float2 hf = __half22float2(__floats2half2_rn(raw.x, raw.y));
+                const float2 st = p.round_stats ? hf : raw;
+                ss = __fmaf_rn(st.x, st.x, ss);
+                ss = __fmaf_rn(st.y, st.y, ss);
+                v[k * 8 + 2 * j] = hf.x;
+                v[k * 8 + 2 * j + 1] = hf.y;
+              }
+            }
+            uint4 row[4];
+            pack_row32(v, row);
+            store_chunk32_staged(stage, row, p.out + m_warp * p.ldo + n0, p.ldo, valid_rows);
+          } else if (valid && valid_cols > 0) {
+            float v[32];
+            dequant_chunk<false>(r, sx, cw + c * 32, cb + c * 32, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < valid_cols) {
+                const float raw = __fmaf_rn(round_fp16(v[j]), cg[c * 32 + j], __half2float(p.residual[m * p.ldo + n0 + j]));
+                const float hf = round_fp16(raw);
+                const float st = p.round_stats ? hf : raw;
+                ss = __fmaf_rn(st, st, ss);
+                p.out[m * p.ldo + n0 + j] = __float2half_rn(hf);
+              }
+            }
+          }
+        }
+        if (valid) p.row_sumsq[m * (2 * p.n_tiles) + 2 * n_tile + half] = ss;
       } else if constexpr (EP == Epi::kSwiGLU) {
         const uint32_t t_row = t_acc;
         const int64_t m = m_pre;
@@ -985,8 +1065,8 @@ using namespace h3b;
 template <int BN, int STAGES, AMode AM, Epi EP, int MT = 1, bool F16 = false>
 int launch_mma(const CUtensorMap& ma, const CUtensorMap& mb, const MmaParams& p, cudaStream_t stream,
                const char* name) {
-  constexpr size_t smem =
-      STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256 + 2 * 2 * BN * sizeof(float) + kEpiWarps * 2048;
+  constexpr size_t smem = STAGES * (MT * kATileBytes + BN * kBK) + 1024 + 256 +
+                         2 * cst_arrays(EP) * BN * sizeof(float) + kEpiWarps * 2048;
   static_assert(smem <= 232448, "shared memory budget");
   auto kern = mma_tc_kernel<BN, STAGES, AM, EP, MT, F16>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
@@ -1315,6 +1395,33 @@ int h3b_gemm_i8(const int8_t* qa, const float* a_scale, const int8_t* qw, const 
   rc = make_gemm_maps(&ma, &mb, qa, M, K, qw, N, 128);
   if (rc) return rc;
   return launch_mma<128, 6, AMode::kGemm2D, Epi::kLinear>(ma, mb, p, st, name);
+}
+
+int64_t h3b_gemm_i8_residual_parts(int64_t N) { return N > 0 ? 2 * ((N + 127) / 128) : 0; }
+
+int h3b_gemm_i8_residual(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale,
+                         const void* bias, int64_t M, int64_t N, int64_t K, const void* x, const void* gate,
+                         int round_stats, void* h, int64_t ldh, float* row_sumsq, h3b_stream_t stream) {
+  const char* name = "h3b_gemm_i8_residual";
+  int rc = check_gemm_common(qa, a_scale, qw, w_scale, M, N, K, name);
+  if (rc) return rc;
+  if (!x || !gate || !h || !row_sumsq || ldh < N) return h3b_host::set_error(H3B_EINVAL, "%s: bad x / gate / h", name);
+  MmaParams p{};
+  p.M = (int)M; p.N = (int)N; p.K = (int)K;
+  p.k_blocks = (int)((K + kBK - 1) / kBK);
+  p.m_tiles = (int)((M + kBM - 1) / kBM);
+  p.m_groups = p.m_tiles;
+  p.n_tiles = (int)((N + 127) / 128);
+  p.a_scale = a_scale; p.w_scale = w_scale; p.bias = static_cast<const __half*>(bias);
+  p.out = static_cast<__half*>(h); p.ldo = ldh;
+  p.residual = static_cast<const __half*>(x);
+  p.gate = static_cast<const __half*>(gate);
+  p.row_sumsq = row_sumsq;
+  p.round_stats = round_stats ? 1 : 0;
+  CUtensorMap ma, mb;
+  rc = make_gemm_maps(&ma, &mb, qa, M, K, qw, N, 128);
+  if (rc) return rc;
+  return launch_mma<128, 6, AMode::kGemm2D, Epi::kResidual>(ma, mb, p, reinterpret_cast<cudaStream_t>(stream), name);
 }
 
 int h3b_gemm_i8_swiglu(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale,

@@ -440,6 +440,54 @@ def gemm_i8(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, weight_
     return out
 
 
+def gemm_i8_residual(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, weight_scale: torch.Tensor,
+                     bias: torch.Tensor | None, x: torch.Tensor, gate: torch.Tensor, *, round_stats: bool = False,
+                     h_out: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """Attention-out INT8 GEMM with the residual fused into its epilogue: h = fp16(fma(a, gate, x)) for
+    a = fp16(linear), written instead of a, plus per-row partial sums of squares for rms_quant_parts.
+    Returns (h [M, N] fp16, row_sumsq [M, parts] fp32)."""
+    dev = _require_cuda(q, scale, qweight, weight_scale, bias, x, gate, h_out)
+    _require(q, I8, "q")
+    _require(qweight, I8, "qweight")
+    _require(scale, F32, "scale")
+    _require(weight_scale, F32, "weight_scale")
+    _require(bias, F16, "bias")
+    _require(x, F16, "x")
+    _require(gate, F16, "gate")
+    m, k = _rows(q)
+    n = qweight.shape[0]
+    if x.shape[-1] != n or x.numel() != m * n or gate.shape != (n,):
+        raise ValueError("x must be [M, N] and gate [N] for an [N, K] weight")
+    lib = _lib.load()
+    h = torch.empty((m, n), device=dev, dtype=F16) if h_out is None else h_out
+    parts = int(lib.h3b_gemm_i8_residual_parts(n))
+    sums = torch.empty((m, parts), device=dev, dtype=F32)
+    _lib.check(lib.h3b_gemm_i8_residual(q.data_ptr(), scale.data_ptr(), qweight.data_ptr(), weight_scale.data_ptr(),
+                                        _ptr(bias), m, n, k, x.data_ptr(), gate.data_ptr(), 1 if round_stats else 0,
+                                        h.data_ptr(), n, sums.data_ptr(), _stream(dev)))
+    _count(1)
+    return h, sums
+
+
+def rms_quant_parts(h: torch.Tensor, row_sumsq: torch.Tensor, w: torch.Tensor, eps: float, *,
+                    return_norm: bool = False):
+    """act = fp16(h * rsqrt(sum(row_sumsq[m]) / K + eps) * w) and CK row quantization -> (q, s[, act])."""
+    dev = _require_cuda(h, row_sumsq, w)
+    _require(h, F16, "h")
+    _require(w, F16, "w")
+    _require(row_sumsq, F32, "row_sumsq")
+    m, k = _rows(h)
+    if w.shape != (k,) or row_sumsq.shape[0] != m:
+        raise ValueError("w must be [K] and row_sumsq [M, parts]")
+    q = torch.empty((m, k), device=dev, dtype=I8)
+    s = torch.empty((m, 1), device=dev, dtype=F32)
+    norm = torch.empty_like(h) if return_norm else None
+    _lib.check(_lib.load().h3b_rms_quant_parts(h.data_ptr(), row_sumsq.data_ptr(), row_sumsq.shape[1], w.data_ptr(),
+                                               m, k, float(eps), q.data_ptr(), s.data_ptr(), _ptr(norm), _stream(dev)))
+    _count(1)
+    return (q, s, norm) if return_norm else (q, s)
+
+
 def gemm_i8_swiglu(q: torch.Tensor, scale: torch.Tensor, qweight: torch.Tensor, weight_scale: torch.Tensor,
                    bias: torch.Tensor | None = None) -> torch.Tensor:
     """FFN-up INT8 GEMM with the SwiGLU epilogue: returns fp16 act [M, F] for a [2F, K] weight."""

@@ -433,8 +433,10 @@ class H3Decoder:
                                          cfg.qk_eps)
             y = K.attention_f16(q, k, v, 1.0 / 8.0)            # [B, n, H, 64] storage
             qy, sy = K.row_quant(y.transpose(1, 2).reshape(b * n, d))
-            a = K.gemm_i8(qy, sy, blk.out_q, blk.out_s, blk.out_b)
-            h_state, q2, s2 = K.residual_rms_quant(x, a, blk.scale1, blk.norm2_w, cfg.eps)
+            # attention-out GEMM with the residual (h = x + a * scale1) and norm2's sums of squares in
+            # its epilogue, then norm2 + the FFN-up's row quantization
+            h_state, sumsq = K.gemm_i8_residual(qy, sy, blk.out_q, blk.out_s, blk.out_b, x, blk.scale1)
+            q2, s2 = K.rms_quant_parts(h_state, sumsq, blk.norm2_w, cfg.eps)
             act = K.gemm_i8_swiglu(q2, s2, blk.up_q, blk.up_s, blk.up_b)
             qf, sf = K.row_quant(act)
             out = K.gemm_i8(qf, sf, blk.down_q, blk.down_s, blk.down_b)

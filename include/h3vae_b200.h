@@ -248,6 +248,31 @@ int h3b_gemm_i8(const int8_t* qa, const float* a_scale, const int8_t* qw, const 
                 const void* bias, int64_t M, int64_t N, int64_t K, void* out, int64_t ldo,
                 int32_t* acc_out, h3b_stream_t stream);
 
+/* Attention-out GEMM with the residual and the RMS statistics of the next
+ * norm fused into its epilogue.  Per element of row m, column n:
+ *   a   = fp16( fma(acc * a_scale[m], w_scale[n], bias[n]) )   (the linear)
+ *   raw = fma(a, gate[n], x[m, n]);   h[m, n] = fp16(raw)
+ * h is written instead of a (row stride ldh; h may alias x: every element is
+ * read before it is written, by the same thread), and the sum of raw^2 (h^2
+ * with round_stats) over each half of each 128-column tile goes to
+ * row_sumsq[m, 0 .. h3b_gemm_i8_residual_parts(N)) (fp32, caller-provided).
+ * h3b_rms_quant_parts then finishes the norm and the row quantization without
+ * reading a.  ref: opt/int8_attention_out.py (out_linear: prequantized_linear,
+ * opt/int8_swiglu_fused.py:78-107) followed by opt/int8_norm_quant.py:23-70
+ * (residual_quant, the residual + RMSNorm + row quantization of norm2) */
+int64_t h3b_gemm_i8_residual_parts(int64_t N);
+int h3b_gemm_i8_residual(const int8_t* qa, const float* a_scale, const int8_t* qw, const float* w_scale,
+                         const void* bias, int64_t M, int64_t N, int64_t K, const void* x, const void* gate,
+                         int round_stats, void* h, int64_t ldh, float* row_sumsq, h3b_stream_t stream);
+
+/* The rest of residual_quant for an h and its partial sums from
+ * h3b_gemm_i8_residual: inv = rsqrt(sum of the row's `parts` partials / K +
+ * eps) (summed in index order), act = fp16(h * inv * w), CK row quantization
+ * -> q int8 [M,K], s fp32 [M]; norm_out (fp16 act) optional.
+ * ref: opt/int8_norm_quant.py:23-44 (from the inv step on) */
+int h3b_rms_quant_parts(const void* h, const float* row_sumsq, int64_t parts, const void* w, int64_t M, int64_t K,
+                        float eps, int8_t* q, float* s, void* norm_out, h3b_stream_t stream);
+
 /* FFN-up GEMM with the SwiGLU epilogue.  qw is the unmodified [2F, K] weight
  * (rows 0..F-1 gate, F..2F-1 up); per column j:
  *   g = fp16(fma(acc_g*s, ws[j], b[j])), u = fp16(fma(acc_u*s, ws[F+j], b[F+j]))

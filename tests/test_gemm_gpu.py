@@ -128,3 +128,34 @@ def test_gemm_f16_rejects_bad_arguments(cuda_lib):
     with pytest.raises(ValueError):   # int8 operand
         K.gemm_f16(torch.zeros(4, 64, dtype=torch.int8, device="cuda"),
                    torch.zeros(8, 64, dtype=torch.float16, device="cuda"))
+
+
+@pytest.mark.parametrize("m,n,k", [(4096, 1024, 1024), (300, 1024, 1024), (129, 2048, 2048), (200, 256, 256),
+                                   (77, 200, 512)])
+@pytest.mark.parametrize("round_stats", [False, True])
+def test_gemm_i8_residual_then_rms_quant(cuda_lib, m, n, k, round_stats):
+    """Attention-out GEMM with the residual in its epilogue (h = fp16(fma(fp16(linear), g, x)) and the
+    row's partial sums of squares), then norm2 + row quantization from those sums, against the oracle's
+    prequantized_linear followed by residual_rms_quant (ref opt/int8_norm_quant.py:23-44)."""
+    from h3vae_b200 import kernels as K
+    rng = np.random.default_rng(m * 7 + n + k)
+    q, s, w, ws, b = _rand_operands(rng, m, n, k)
+    x = rng.standard_normal((m, n)).astype(np.float16)
+    g = (0.5 + 0.1 * rng.standard_normal(n)).astype(np.float16)
+    nw = (1.0 + 0.1 * rng.standard_normal(n)).astype(np.float16)
+    cu = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+    h, sums = K.gemm_i8_residual(cu(q), cu(s), cu(w), cu(ws), cu(b), cu(x), cu(g), round_stats=round_stats)
+    qq, ss, act = K.rms_quant_parts(h, sums, cu(nw), 1e-5, return_norm=True)
+    a = O.prequantized_linear(q, s, w, ws, b)
+    ref_h, ref_q, ref_s, ref_act = O.residual_rms_quant(x, a, g, nw, 1e-5, round_stats=round_stats)
+    got_h = h.cpu().numpy()
+    _close(got_h, ref_h)
+    assert np.count_nonzero(got_h != ref_h) <= max(2, 1e-3 * got_h.size)
+    _close(act.cpu().numpy(), ref_act)
+    dq = np.abs(qq.cpu().numpy().astype(np.int32) - ref_q.astype(np.int32))
+    assert dq.max() <= 1 and np.count_nonzero(dq) <= max(2, 1e-3 * dq.size)
+    assert np.allclose(ss.cpu().numpy(), ref_s, rtol=1e-5, atol=0)
+    # in place: h written over x
+    xin = cu(x)
+    h2, _ = K.gemm_i8_residual(cu(q), cu(s), cu(w), cu(ws), cu(b), xin, cu(g), round_stats=round_stats, h_out=xin)
+    assert h2 is xin and torch.equal(h2, h)
