@@ -265,6 +265,15 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         dist.broadcast(t, src=self._src(), group=self.process_group)
         return t
 
+    def _p2p(self, op, tensor, peer_group_rank: int) -> list:
+        """One point-to-point send or receive, always posted through batch_isend_irecv so that every
+        transfer of the runtime goes through the group's own communicator (PyTorch gives lone
+        send/recv calls separate two-rank communicators and batched ones the group's; mixing the two
+        styles between a sender and its receiver would never match)."""
+        import torch.distributed as dist
+        peer = dist.get_global_rank(self.process_group, peer_group_rank)
+        return dist.batch_isend_irecv([dist.P2POp(op, tensor, peer, self.process_group)])
+
     @staticmethod
     def _frame_major(shape5, device, dtype=torch.float32):
         """A zeroed blend canvas with frames outermost after the batch ([B, T, C, H, W] storage),
@@ -282,10 +291,9 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         if self.world == 1:
             return []
         import torch.distributed as dist
-        src = self._src()
         if self.rank != 0:
             # frame-major contiguous storage of the slab is what crosses the link
-            return [dist.isend(slab.permute(0, 2, 1, 3, 4).contiguous(), dst=src, group=self.process_group)]
+            return self._p2p(dist.isend, slab.permute(0, 2, 1, 3, 4).contiguous(), 0)
         ops, bufs = [], {}
         for r in range(1, self.world):
             t0, t1, y0, y1, x0, x1 = boxes[r]
@@ -533,8 +541,7 @@ class H3VAEPyOptRuntime(torch.nn.Module):
                                 if cs[0] * clip_len < t1 and min((cs[-1] + 1) * clip_len, t) > t0:
                                     side.wait_event(arrived[g])
                         win = x[:, :, t0:t1, y0:y1, x0:x1].contiguous()
-                        sends.append(dist.isend(win, dst=dist.get_global_rank(self.process_group, q),
-                                                group=self.process_group))
+                        sends += self._p2p(dist.isend, win, q)
                 if side is not None:
                     x.record_stream(side)
             return x, (0, 0, 0), arrived, sends
@@ -542,7 +549,8 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         t0, t1, y0, y1, x0, x1 = px_boxes[self.rank]
         win = torch.empty((b, c, t1 - t0, y1 - y0, x1 - x0), dtype=dtype, device=self.dev)
         if t1 > t0:
-            dist.irecv(win, src=self._src(), group=self.process_group).wait()
+            for work in self._p2p(dist.irecv, win, 0):
+                work.wait()
         return win, (t0, y0, x0), None, []
 
     def _upload_clip_batches(self, x_host, cbatches, t, clip_len=CLIP_LENGTH):
