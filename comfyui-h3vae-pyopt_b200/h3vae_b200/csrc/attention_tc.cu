@@ -150,10 +150,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   const int lane = threadIdx.x & 31;
   const int qt0 = blockIdx.x * kFaTiles, h = blockIdx.y, b = blockIdx.z;
   const int n_blocks = (p.kv_len + kFaN - 1) / kFaN;
-  // Query tiles of this CTA that hold rows (the last CTA of an odd tile count
-  // has one): an empty tile gets no Q load, no MMAs and no softmax.
-  const int q_tiles = (p.q_len + kFaM - 1) / kFaM;
-  const int active_tiles = q_tiles - qt0 < kFaTiles ? q_tiles - qt0 : kFaTiles;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -187,8 +183,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   if (warp == 0) {
     // ---------------------------------- TMA ----------------------------------
     if (elect_one_sync()) {
-      mbar_arrive_expect_tx(q_full, active_tiles * kFaQBytes);
-      for (int t = 0; t < active_tiles; ++t) tma_load_4d(sq + t * kFaQBytes, &mq, q_full, 0, (qt0 + t) * kFaM, h, b);
+      mbar_arrive_expect_tx(q_full, kFaTiles * kFaQBytes);
+      for (int t = 0; t < kFaTiles; ++t) tma_load_4d(sq + t * kFaQBytes, &mq, q_full, 0, (qt0 + t) * kFaM, h, b);
       uint32_t issued = 0;
       for (int j = 0; j < n_blocks; ++j, ++issued) {
         const int s = j % kFaStages;
@@ -224,13 +220,13 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         tc_commit(&s_full[t]);
         return true;
       };
-      for (int t = 0; t < active_tiles && ok; ++t) ok = issue_s(0, t);
+      for (int t = 0; t < kFaTiles && ok; ++t) ok = issue_s(0, t);
       for (int j = 0; j < n_blocks && ok; ++j) {
         const int s = j % kFaStages;
         // S_{j+1}(t) as soon as the softmax of tile t has copied S_j(t) into its
         // registers, so it overlaps that softmax's exponentials.
-        for (int t = 0; t < active_tiles && ok && j + 1 < n_blocks; ++t) ok = issue_s(j + 1, t);
-        for (int t = 0; t < active_tiles && ok; ++t) {
+        for (int t = 0; t < kFaTiles && ok && j + 1 < n_blocks; ++t) ok = issue_s(j + 1, t);
+        for (int t = 0; t < kFaTiles && ok; ++t) {
           // P_j(t) written; O(t) holds the sum over the blocks before j,
           // already rescaled if the reference max moved.
           if (!mbar_poll(&p_full[t], j & 1, abort_flag)) { ok = false; break; }
@@ -248,7 +244,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         tc_commit(&kv_empty[s]);
       }
     }
-  } else if (warp - 2 < kFaSoftmaxWarps * active_tiles) {
+  } else {
     // ------------------------------ softmax warps ------------------------------
     const int sw = warp - 2;
     const int tile = sw / kFaSoftmaxWarps;
@@ -266,18 +262,16 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // tile 0 syncs on 1 and arrives on 2, tile 1 the reverse.  Tile 1 hands
     // tile 0 the first turn and skips its hand-back after the last block, so
     // every barrier completes as often as it is waited on.
-    // With one active tile there is no partner to take turns with.
     constexpr int kSoftmaxThreads = 32 * kFaSoftmaxWarps * kFaTiles;
-    const bool pingpong = H3B_FA_PINGPONG && active_tiles == kFaTiles;
     auto exp_turn_begin = [&]() {
-      if (pingpong)
+      if (H3B_FA_PINGPONG)
         asm volatile("bar.sync %0, %1;" ::"r"(tile == 0 ? 1 : 2), "r"(kSoftmaxThreads) : "memory");
     };
     auto exp_turn_end = [&](int jj) {
-      if (pingpong && (tile == 0 || jj + 1 < n_blocks))
+      if (H3B_FA_PINGPONG && (tile == 0 || jj + 1 < n_blocks))
         asm volatile("bar.arrive %0, %1;" ::"r"(tile == 0 ? 2 : 1), "r"(kSoftmaxThreads) : "memory");
     };
-    if (pingpong && tile == 1) asm volatile("bar.arrive 1, %0;" ::"r"(kSoftmaxThreads) : "memory");
+    if (H3B_FA_PINGPONG && tile == 1) asm volatile("bar.arrive 1, %0;" ::"r"(kSoftmaxThreads) : "memory");
     for (int j = 0; j < n_blocks; ++j) {
       ok = __all_sync(0xffffffffu, ok && mbar_wait_u32(bar_s_full, j & 1, abort_flag));
       const int valid = p.kv_len - j * kFaN;
@@ -323,13 +317,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
       float sums[4] = {0.0f, 0.0f, 0.0f, 0.0f};
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        if (valid < kFaN && q * 8 >= valid) {
-          // keys past the end of the sequence (only in the last block): P = 0
-          // without exponentials (V's rows there are the TMA zero fill)
-          if (ok)
-            st_shared_v4(prow + (q >> 3) * (kFaPBytes / 2) + (((q & 7) ^ (row & 7)) << 4), make_uint4(0, 0, 0, 0));
-          continue;
-        }
         __align__(16) __half2 hv[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {

@@ -154,7 +154,9 @@ def test_gemm_i8_residual_then_rms_quant(cuda_lib, m, n, k, round_stats):
     _close(act.cpu().numpy(), ref_act)
     dq = np.abs(qq.cpu().numpy().astype(np.int32) - ref_q.astype(np.int32))
     assert dq.max() <= 1 and np.count_nonzero(dq) <= max(2, 1e-3 * dq.size)
-    assert np.allclose(ss.cpu().numpy(), ref_s, rtol=1e-5, atol=0)
+    # the row scale follows the row's largest |act|, which can sit one fp16 ulp away when the partial sums
+    # (added in another order than the oracle's) move inv by a last-bit rounding
+    assert np.allclose(ss.cpu().numpy(), ref_s, rtol=1e-3, atol=0)
     # in place: h written over x
     xin = cu(x)
     h2, _ = K.gemm_i8_residual(cu(q), cu(s), cu(w), cu(ws), cu(b), xin, cu(g), round_stats=round_stats, h_out=xin)
