@@ -409,7 +409,8 @@ def run_kernels(args):
     s = torch.rand((m, 1), generator=g, device=dev) * 0.02 + 0.001
     for name, n, k, kind in (("gemm_qkv", 3 * d, d, "linear"), ("gemm_attn_out", d, d, "linear"),
                              ("gemm_ffn_up", 2 * ffn, d, "linear"), ("gemm_ffn_down", d, ffn, "linear"),
-                             ("gemm_ffn_up_swiglu", 2 * ffn, d, "swiglu"), ("gemm_qkv_qknorm_rope", 3 * d, d, "qkv")):
+                             ("gemm_ffn_up_swiglu", 2 * ffn, d, "swiglu"), ("gemm_qkv_qknorm_rope", 3 * d, d, "qkv"),
+                             ("gemm_attn_out_residual", d, d, "residual")):
         a = q if k == d else i8(m, k)
         w = i8(n, k)
         ws = torch.rand(n, generator=g, device=dev) * 1e-3 + 1e-4
@@ -418,6 +419,10 @@ def run_kernels(args):
             fn = lambda a=a, w=w, ws=ws, b=b: K.gemm_i8(a, s, w, ws, b)          # noqa: E731
         elif kind == "swiglu":
             fn = lambda a=a, w=w, ws=ws, b=b: K.gemm_i8_swiglu(a, s, w, ws, b)   # noqa: E731
+        elif kind == "residual":
+            xres = torch.randn((m, n), generator=g, device=dev).half()
+            gate = (0.5 + 0.1 * torch.randn(n, generator=g, device=dev)).half()
+            fn = lambda a=a, w=w, ws=ws, b=b, xres=xres, gate=gate: K.gemm_i8_residual(a, s, w, ws, b, xres, gate)  # noqa: E731
         else:
             ang = torch.rand((4, tokens, 1, 48), generator=g, device=dev) * 6.28
             cos, sin = ang.cos().half(), ang.sin().half()
