@@ -59,12 +59,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// Two base-2 exponentials in one SFU instruction on packed fp16 arguments.
-__device__ __forceinline__ __half2 ex2_h2(__half2 x) {
-  uint32_t y;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(y) : "r"(*reinterpret_cast<const uint32_t*>(&x)));
-  return *reinterpret_cast<const __half2*>(&y);
-}
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
   float d;
   asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
@@ -106,17 +100,6 @@ __device__ __forceinline__ void ex2_poly_pair(uint64_t x, float& lo, float& hi) 
 #ifndef H3B_FA_EMU
 #define H3B_FA_EMU 0
 #endif
-// 1: P = ex2 of fp16 arguments, two per SFU instruction (packed fp16); 0: fp32
-// arguments, one per instruction.
-#ifndef H3B_FA_EX2H
-#define H3B_FA_EX2H 0
-#endif
-__device__ __forceinline__ float2 f2x_fma2(float a, float b, float s, float c) {
-  float lo, hi;
-  f2_unpack(f2_fma(f2_pack(a, b), f2_pack(s, s), f2_pack(c, c)), lo, hi);
-  return make_float2(lo, hi);
-}
-
 // 1: the two query tiles' softmax warps take turns on the SFU (named-barrier
 // ping-pong); 0: both exponentiate whenever their scores are ready.
 #ifndef H3B_FA_PINGPONG
@@ -339,16 +322,6 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         for (int e = 0; e < 4; ++e) {
           const int k = q * 8 + 2 * e;
           float p0, p1;
-#if H3B_FA_EX2H
-          {
-            const float2 xa = f2x_fma2(__uint_as_float(sv_[k]), __uint_as_float(sv_[k + 1]), p.scale_log2, negm);
-            const __half2 ph = ex2_h2(__floats2half2_rn(xa.x, xa.y));
-            const float2 pf = __half22float2(ph);
-            sums[e] += pf.x + pf.y;
-            hv[e] = ph;
-            continue;
-          }
-#endif
           if (((q * 4 + e) & 7) < H3B_FA_EMU) {
             ex2_poly_pair(f2_fma(f2_pack(__uint_as_float(sv_[k]), __uint_as_float(sv_[k + 1])),
                                  f2_pack(p.scale_log2, p.scale_log2), f2_pack(negm, negm)),
