@@ -226,15 +226,31 @@ def _qk_rope(qkv, cos, sin, heads, eps):
 def decoder_forward(dec, z, *, acc_dtype=torch.float32, timer=None):
     """z: fp16 [B, latent, t, h, w] (de-normalized latents) -> raw fp16-valued pixels [B, 3, T, H, W]."""
     timer = timer or _NoTimer()
-    cfg = dec.cfg
     b, _, t, hh, ww = z.shape
-    d = cfg.hidden
     with timer("linear"):
-        feat = conv_f16(_reflect_causal_pad(z.to(torch.float32)), dec.conv_in_w, dec.conv_in_b)
-        n = t * hh * ww
-        x = feat.permute(0, 2, 3, 4, 1).reshape(b * n, d)
+        tokens = decoder_tokens(dec, z)
+    y = decoder_blocks(dec, tokens, (t, hh, ww), acc_dtype=acc_dtype, timer=timer)
+    return decoder_upsample(dec, y, (t, hh, ww), timer=timer)
+
+
+def decoder_tokens(dec, z):
+    """Latent conv-in: fp16-valued tokens [B, t*h*w, hidden]."""
+    b, _, t, hh, ww = z.shape
+    feat = conv_f16(_reflect_causal_pad(z.to(torch.float32)), dec.conv_in_w, dec.conv_in_b)
+    return feat.permute(0, 2, 3, 4, 1).reshape(b, t * hh * ww, dec.cfg.hidden)
+
+
+@torch.no_grad()
+def decoder_blocks(dec, tokens, grid, *, acc_dtype=torch.float32, timer=None):
+    """The INT8 block chain and the final residual + LayerNorm: tokens [B, n, hidden] -> [B, n, hidden]."""
+    timer = timer or _NoTimer()
+    cfg = dec.cfg
+    b, n, d = tokens.shape
+    t, hh, ww = grid
+    with timer("linear"):
+        x = tokens.to(torch.float32).reshape(b * n, d)
         cos, sin = (_t(v).view(1, n, 1, -1) for v in dec._rope(1, t, hh, ww))
-        cos, sin = cos[:, :, :, :].expand(b, n, 1, -1), sin.expand(b, n, 1, -1)
+        cos, sin = cos.expand(b, n, 1, -1), sin.expand(b, n, 1, -1)
     h_state, out, prev = x, None, None
     for i, blk in enumerate(dec.blocks):
         with timer("linear"):
@@ -265,8 +281,19 @@ def decoder_forward(dec, z, *, acc_dtype=torch.float32, timer=None):
             prev = blk.scale2
     with timer("linear"):
         raw = torch.addcmul(h_state, out, _t(prev))
-        y = _f16(F.layer_norm(raw, (d,), _t(dec.ln_w), _t(dec.ln_b), cfg.eps))
-        x = y.view(b, t, hh, ww, d).permute(0, 4, 1, 2, 3)
+        return _f16(F.layer_norm(raw, (d,), _t(dec.ln_w), _t(dec.ln_b), cfg.eps)).view(b, n, d)
+
+
+@torch.no_grad()
+def decoder_upsample(dec, y, grid, *, timer=None):
+    """After the blocks: [B, n, hidden] tokens of a (t, h, w) grid -> raw pixels [B, 3, T, H, W] through the
+    upsampling stages (GroupNorm + SiLU + pad of the upsampled tensor, fp16 conv) and the RGB conv."""
+    timer = timer or _NoTimer()
+    cfg = dec.cfg
+    b, n, d = y.shape
+    t, hh, ww = grid
+    with timer("linear"):
+        x = y.to(torch.float32).reshape(b, t, hh, ww, d).permute(0, 4, 1, 2, 3)
         gns = [(gw, gb) for gw, gb, _, _ in dec.up] + [(dec.out_gn_w, dec.out_gn_b)]
         pending, up_s, up_t = None, False, False
         for k_, (gw, gb, wt, bs) in enumerate(dec.up):
@@ -311,5 +338,5 @@ def cpu_threads() -> int:
     return torch.get_num_threads()
 
 
-__all__ = ["OpTimer", "encoder_forward", "decoder_forward", "encoder_item_seconds", "decoder_task_seconds",
-           "scale_sample", "cpu_threads", "math"]
+__all__ = ["OpTimer", "encoder_forward", "decoder_forward", "decoder_tokens", "decoder_blocks", "decoder_upsample",
+           "encoder_item_seconds", "decoder_task_seconds", "scale_sample", "cpu_threads", "math"]
