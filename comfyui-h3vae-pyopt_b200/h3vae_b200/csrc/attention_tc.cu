@@ -13,18 +13,22 @@
 //               (its TMEM lane).  The row's 128 scores come out of TMEM in one
 //               round trip, after which the S columns are released so the MMA
 //               warp computes S_{j+1} while this block is exponentiated.
-//               P_j = exp2(S_j * scale*log2e - m) is rounded to
-//               fp16 into 128-byte-swizzled shared memory and the running row
-//               sum stays in a register.  O accumulates in TMEM across key
-//               blocks.  The reference max m only moves when a block's max
-//               exceeds it by more than 8 (log2 units; P stays <= 256, well
-//               inside fp16); then the rows' O in TMEM is rescaled by
+//               P_j = exp2(S_j * scale*log2e - m) (score pairs scaled by
+//               one packed f32x2 FMA) is rounded to fp16 into 128-byte-swizzled
+//               shared memory.  O accumulates in TMEM across key blocks; V is
+//               extended by a shared-memory block of fp16 ones (P V at N = 80),
+//               so O's column 64 accumulates the row sum of the rounded P in
+//               fp32 and the exponential loop carries no additions.  The
+//               reference max m only moves when a block's max exceeds it by
+//               more than 8 (log2 units; P stays <= 256, well inside fp16);
+//               then the rows' O and row sums in TMEM are rescaled by
 //               exp2(m_old - m_new) before the next P V accumulates.  One
 //               division by the row sum at the end.
 // The base-2 exponentials (16K per tile and key block, one SFU op each) are
 // the bound; the two tiles take turns on the SFU (named-barrier ping-pong) so
-// one tile's exponentials overlap the other's TMEM reads and waits.  Every mbarrier wait is bounded (see common.cuh); its outcome is
-// made warp-uniform before any warp-collective TMEM access.
+// one tile's exponentials overlap the other's TMEM reads, maximum and waits.
+// Every mbarrier wait is bounded (see common.cuh); its outcome is made
+// warp-uniform before any warp-collective TMEM access.
 #include "common.cuh"
 
 namespace h3b {
@@ -105,6 +109,16 @@ __device__ __forceinline__ void ex2_poly_pair(uint64_t x, float& lo, float& hi) 
 #ifndef H3B_FA_PINGPONG
 #define H3B_FA_PINGPONG 1
 #endif
+// 1: the row sums come from the tensor core -- V is extended by a block of
+// ones (P V at N = 80), so O's column 64 accumulates sum_k P[r,k] in fp32 and
+// the exponential loop loses its additions; 0: the softmax warps add P up.
+#ifndef H3B_FA_ONES
+#define H3B_FA_ONES 1
+#endif
+// 1: scale and shift pairs of scores with one packed f32x2 FMA.
+#ifndef H3B_FA_FMA2
+#define H3B_FA_FMA2 1
+#endif
 
 constexpr int kFaM = 128;       // queries per tile
 constexpr int kFaTiles = 2;     // query tiles per CTA
@@ -116,8 +130,11 @@ constexpr int kFaThreads = 64 + 32 * kFaSoftmaxWarps * kFaTiles;
 constexpr uint32_t kFaQBytes = kFaM * kFaD * 2;   // 16 KB per tile
 constexpr uint32_t kFaKVBytes = kFaN * kFaD * 2;  // 16 KB each for K and V
 constexpr uint32_t kFaPBytes = kFaM * kFaN * 2;   // 32 KB per tile (two 16 KB swizzle columns of 64 keys)
-constexpr uint32_t kFaTmemCols = 512;             // per tile: S (128) | O (64), at tile * 256
-constexpr uint32_t kFaSmemBytes = kFaTiles * kFaQBytes + 2 * kFaStages * kFaKVBytes + kFaTiles * kFaPBytes + 1024 + 256;
+constexpr uint32_t kFaTmemCols = 512;             // per tile: S (128) | O (64, + 16 row-sum columns), at tile * 256
+constexpr int kFaDO = H3B_FA_ONES ? kFaD + 16 : kFaD;   // P V output columns
+constexpr uint32_t kFaOnesBytes = H3B_FA_ONES ? kFaN * 128 : 0;   // 128 key rows x 64 fp16 ones
+constexpr uint32_t kFaSmemBytes =
+    kFaTiles * kFaQBytes + 2 * kFaStages * kFaKVBytes + kFaTiles * kFaPBytes + kFaOnesBytes + 1024 + 256;
 
 struct FaParams {
   int q_len, kv_len;
@@ -135,7 +152,8 @@ __global__ void __launch_bounds__(kFaThreads, 1)
   uint8_t* sk = sq + kFaTiles * kFaQBytes;             // [stage]
   uint8_t* sv = sk + kFaStages * kFaKVBytes;           // [stage]
   uint8_t* sp = sv + kFaStages * kFaKVBytes;           // [tile]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sp + kFaTiles * kFaPBytes);
+  uint8_t* sones = sp + kFaTiles * kFaPBytes;          // fp16 ones, the row-sum columns of V
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sones + kFaOnesBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;
   uint64_t* kv_empty = kv_full + kFaStages;
@@ -175,6 +193,11 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     tmem_alloc(tmem_slot, kFaTmemCols);
     tmem_relinquish();
   }
+  if (H3B_FA_ONES) {
+    for (uint32_t i = threadIdx.x; i < kFaOnesBytes / 16; i += kFaThreads)
+      st_shared_v4(smem_u32(sones) + 16 * i, make_uint4(0x3c003c00u, 0x3c003c00u, 0x3c003c00u, 0x3c003c00u));
+    fence_proxy_async_smem();   // the tensor core reads them through the async proxy
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -204,7 +227,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
     // ------------------------------- MMA issuer -------------------------------
     if (elect_one_sync()) {
       constexpr uint32_t idesc_qk = make_idesc_f16(kFaM, kFaN);
-      constexpr uint32_t idesc_pv = make_idesc_f16(kFaM, kFaD) | (1u << 16);  // B (V) is MN-major
+      constexpr uint32_t idesc_pv = make_idesc_f16(kFaM, kFaDO) | (1u << 16);  // B (V) is MN-major
       bool ok = mbar_poll(q_full, 0, abort_flag);
       // S_j(t) into tile t's S columns; requires K_j resident and S_{j-1}(t) read out.
       auto issue_s = [&](int j, int t) -> bool {
@@ -233,10 +256,15 @@ __global__ void __launch_bounds__(kFaThreads, 1)
           tc_fence_after();
           const uint32_t pbase = smem_u32(sp + t * kFaPBytes);
           const uint32_t vbase = smem_u32(sv + s * kFaKVBytes);
+          // V is MN-major with 64 dims = one 128-byte swizzle atom per key row;
+          // at N = 80 the second atom column (the ones) sits at the leading
+          // byte offset, the same distance from every 16-key step.
+          const uint64_t lbo = H3B_FA_ONES ? static_cast<uint64_t>(((smem_u32(sones) - vbase) >> 4) & 0x3FFFu) << 16 : 0;
 #pragma unroll
           for (int k = 0; k < kFaN / 16; ++k) {
             const uint64_t pdesc = make_sw128_desc(pbase + (k >> 2) * (kFaPBytes / 2)) + 2 * (k & 3);
-            const uint64_t vdesc = make_sw128_desc(vbase + k * 16 * 128);
+            uint64_t vdesc = make_sw128_desc(vbase + k * 16 * 128);
+            if (H3B_FA_ONES) vdesc = (vdesc & ~(uint64_t(0x3FFFu) << 16)) | lbo;
             mma_f16(tmem + t * 256 + kFaN, pdesc, vdesc, idesc_pv, (j > 0 || k > 0) ? 1u : 0u);
           }
           tc_commit(&o_full[t]);
@@ -326,11 +354,18 @@ __global__ void __launch_bounds__(kFaThreads, 1)
             ex2_poly_pair(f2_fma(f2_pack(__uint_as_float(sv_[k]), __uint_as_float(sv_[k + 1])),
                                  f2_pack(p.scale_log2, p.scale_log2), f2_pack(negm, negm)),
                           p0, p1);
+          } else if (H3B_FA_FMA2) {
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(sv_[k]), __uint_as_float(sv_[k + 1])),
+                             f2_pack(p.scale_log2, p.scale_log2), f2_pack(negm, negm)),
+                      x0, x1);
+            p0 = ex2_approx(x0);
+            p1 = ex2_approx(x1);
           } else {
             p0 = ex2_approx(__fmaf_rn(__uint_as_float(sv_[k]), p.scale_log2, negm));
             p1 = ex2_approx(__fmaf_rn(__uint_as_float(sv_[k + 1]), p.scale_log2, negm));
           }
-          sums[e] += p0 + p1;
+          if (!H3B_FA_ONES) sums[e] += p0 + p1;
           hv[e] = __floats2half2_rn(p0, p1);
         }
         // keys q*8..q*8+7: swizzle column q/8, 16-byte chunk q%8 of this row
@@ -346,7 +381,7 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         tc_fence_after();
         if (__any_sync(0xffffffffu, move)) {
 #pragma unroll
-          for (int c = 0; c < 2; ++c) {
+          for (int c = 0; c < (H3B_FA_ONES ? 3 : 2); ++c) {   // O and, with the ones, its row sums
             uint32_t r[32];
             tmem_ld32(t_o + c * 32, r);
             tmem_ld_wait();
@@ -362,11 +397,18 @@ __global__ void __launch_bounds__(kFaThreads, 1)
         fence_proxy_async_smem();
         mbar_arrive_u32(bar_p_full);
       }
-      l = __fmaf_rn(l, alpha, (sums[0] + sums[1]) + (sums[2] + sums[3]));
+      if (!H3B_FA_ONES) l = __fmaf_rn(l, alpha, (sums[0] + sums[1]) + (sums[2] + sums[3]));
       m = m_new;
     }
     if (n_blocks > 0) ok = __all_sync(0xffffffffu, ok && mbar_wait_u32(bar_o_full, (n_blocks - 1) & 1, abort_flag));
     const int qrow = (qt0 + tile) * kFaM + row;
+    if (H3B_FA_ONES && ok) {
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld32(t_o + kFaD, r);
+      tmem_ld_wait();
+      l = __uint_as_float(r[0]);
+    }
     const float inv = l > 0.0f ? 1.0f / l : 0.0f;
     __half* dst = p.out + b * p.os[0] + h * p.os[1] + static_cast<int64_t>(qrow) * p.os[2];
     if (ok) tc_fence_after();

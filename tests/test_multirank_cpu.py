@@ -1,5 +1,6 @@
-"""The N>1 runtime path on CPU: two gloo ranks run the same encode/decode call, each takes its
-contiguous block of (tile, clip) work items, and one reduce sums the blend canvases on rank 0.
+"""The N>1 runtime path on CPU: 2, 3 or 8 gloo ranks run the same encode/decode call, each takes
+its contiguous block of (tile, clip) work items (at 8 ranks some ranks get none), rank 0 sends each
+rank the pixel window its items read, and every rank sends rank 0 the canvas slab its items cover.
 
 The encoder/decoder are replaced by small linear stand-ins (the sharding, blending, broadcast and
 reduce logic is what is under test; the kernels have their own GPU tests).  The sharded result
@@ -132,7 +133,7 @@ def _run(world, mode):
     return results
 
 
-@pytest.mark.parametrize("world", [2, 3])
+@pytest.mark.parametrize("world", [2, 3, 8])
 def test_multi_rank_encode_decode_equals_single_process(monkeypatch, world):
     """Rank 0 sends each rank only its pixel window and adds the ranks' canvas slabs; with 3 ranks
     the shard boundaries fall inside clip batches and temporal chunks, so slabs overlap and are
