@@ -543,6 +543,10 @@ def main():
                                                  VIDEO_SHAPE[3] // 8, VIDEO_SHAPE[4] // 8))
         host_out = torch.empty(out_shape, dtype=torch.float32).pin_memory() if rank == 0 else None
         e2e_ms = []
+        # one untimed pass through the host-buffer path first (its staging buffers and streams)
+        lat = runtime.encode(host_video)
+        runtime.decode(fp16(lat), output_buffer=host_out)
+        torch.cuda.synchronize()
         barrier(pg)
         for _ in range(max(1, args.steps)):
             t0 = torch.cuda.Event(enable_timing=True)
@@ -556,7 +560,7 @@ def main():
             e2e_ms.append(t0.elapsed_time(t1))
         barrier(pg)
         e2e_s = max_over_ranks(statistics.mean(e2e_ms) / 1e3, pg)
-        e2e = {"value": e2e_s, "unit": UNIT,
+        e2e = {"value": e2e_s, "unit": UNIT, "step_s": [round(t / 1e3, 4) for t in e2e_ms],
                "h2d_bytes_per_step": int(video.numel() * video.element_size()) if rank == 0 else 0,
                "d2h_bytes_per_step": int(host_out.numel() * 4) if rank == 0 else 0}
 
