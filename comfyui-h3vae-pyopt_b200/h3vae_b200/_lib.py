@@ -40,6 +40,7 @@ _SIGNATURES = {
     "h3b_conv_in_workspace_size": (c_size_t, [c_int64] * 4),
     "h3b_conv_in_f16": (c_int, [c_void_p, _i64p, _i64p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p, c_void_p,
                                 c_void_p, c_size_t, c_void_p]),
+    "h3b_im2col_causal_f16": (c_int, [c_void_p, _i64p, _i64p, c_void_p, c_void_p]),
     "h3b_quantize_tensor_workspace_size": (c_size_t, []),
     "h3b_quantize_tensor_i8": (c_int, [c_void_p, _i64p, _i64p, c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
     "h3b_norm_workspace_size": (c_size_t, [c_int64] * 5),

@@ -279,9 +279,74 @@ __global__ void __launch_bounds__(kCinThreads, 2)
   if (warp == kCinWorkers) tmem_dealloc(tmem_base, 256);
 }
 
+
+// Rows of the causal 3x3x3 conv as a GEMM operand (the decoder's latent conv-in:
+// 16 channels are narrower than one 128-byte K row of the implicit-GEMM conv,
+// so its input is unrolled and multiplied by the library's fp16 GEMM).  Thread
+// i -> (position m = i / 27, tap = i % 27): out[m, tap*C .. tap*C + C) holds
+// the C channels of input frame t + kd - 2 (zero before frame 0: the two causal
+// zero frames), row y + kh - 1 and column x + kw - 1, reflected at the edges
+// (zero-padded instead when H or W is 1), exactly the padded tensor the conv
+// reads.  Column order (kd, kh, kw, c) matches a [N, 3, 3, 3, C] weight.
+__global__ void im2col_causal_kernel(const __half* __restrict__ x, int B, int C, int T, int H, int W, int64_t sB,
+                                     int64_t sC, int64_t sT, int64_t sH, int64_t sW, int reflect, __half* out) {
+  const int64_t total = static_cast<int64_t>(B) * T * H * W * 27;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int tap = static_cast<int>(i % 27);
+    int64_t m = i / 27;
+    const int xw = static_cast<int>(m % W);
+    int64_t r = m / W;
+    const int y = static_cast<int>(r % H);
+    r /= H;
+    const int t = static_cast<int>(r % T);
+    const int b = static_cast<int>(r / T);
+    const int kd = tap / 9, kh = (tap / 3) % 3, kw = tap % 3;
+    const int ts = t + kd - 2;
+    int ys = y + kh - 1, xs = xw + kw - 1;
+    bool in = ts >= 0;
+    if (reflect) {
+      ys = ys < 0 ? -ys : (ys >= H ? 2 * H - 2 - ys : ys);
+      xs = xs < 0 ? -xs : (xs >= W ? 2 * W - 2 - xs : xs);
+    } else {
+      in = in && ys >= 0 && ys < H && xs >= 0 && xs < W;
+    }
+    __half* dst = out + m * (27 * static_cast<int64_t>(C)) + tap * C;
+    const __half* src = x + b * sB + static_cast<int64_t>(ts) * sT + static_cast<int64_t>(ys) * sH +
+                        static_cast<int64_t>(xs) * sW;
+    for (int c0 = 0; c0 < C; c0 += 8) {
+      __align__(16) __half v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = in ? src[(c0 + k) * sC] : __float2half_rn(0.0f);
+      *reinterpret_cast<uint4*>(dst + c0) = *reinterpret_cast<const uint4*>(v);
+    }
+  }
+}
+
 }  // namespace h3b
 
 extern "C" {
+
+int h3b_im2col_causal_f16(const void* x, const int64_t* dims5, const int64_t* strides5, void* out,
+                          h3b_stream_t stream) {
+  const char* name = "h3b_im2col_causal_f16";
+  if (!x || !dims5 || !strides5 || !out) return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
+  const int64_t B = dims5[0], C = dims5[1], T = dims5[2], H = dims5[3], W = dims5[4];
+  if (B <= 0 || C <= 0 || T <= 0 || H <= 0 || W <= 0) return h3b_host::set_error(H3B_EINVAL, "%s: empty input", name);
+  if (C % 8 != 0) return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: channels must be a multiple of 8, got %lld", name,
+                                             (long long)C);
+  if (B * T * H * W * 27 >= (int64_t(1) << 40) || C > 4096 || B > (int64_t(1) << 30) || T > (int64_t(1) << 30) ||
+      H > (int64_t(1) << 30) || W > (int64_t(1) << 30))
+    return h3b_host::set_error(H3B_EUNSUPPORTED, "%s: input too large", name);
+  if (reinterpret_cast<uintptr_t>(out) & 15u) return h3b_host::set_error(H3B_EINVAL, "%s: out must be 16-byte aligned", name);
+  const int reflect = (H > 1 && W > 1) ? 1 : 0;
+  const int64_t total = B * T * H * W * 27;
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, static_cast<int64_t>(h3b_host::num_sms()) * 16);
+  h3b::im2col_causal_kernel<<<static_cast<unsigned>(blocks), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      static_cast<const __half*>(x), (int)B, (int)C, (int)T, (int)H, (int)W, strides5[0], strides5[1], strides5[2],
+      strides5[3], strides5[4], reflect, static_cast<__half*>(out));
+  return h3b_host::check_launch(name);
+}
 
 size_t h3b_conv_in_workspace_size(int64_t B, int64_t T, int64_t H, int64_t W) {
   if (B <= 0 || T <= 0 || H <= 0 || W <= 0) return 0;

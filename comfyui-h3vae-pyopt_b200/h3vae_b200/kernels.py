@@ -252,6 +252,27 @@ def conv_in_f16(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
     return out
 
 
+def im2col_causal_f16(x: torch.Tensor) -> torch.Tensor:
+    """GEMM rows of a causal 3x3x3 conv: x fp16 [B, C, T, H, W] (any strides, C % 8 == 0) ->
+    fp16 [B*T*H*W, 27*C], column (kd, kh, kw, c), the two causal zero frames in front and reflect
+    padding 1 in H/W (zero when H or W is 1).  Times a [N, 27*C] weight it is the conv."""
+    dev = _require_cuda(x)
+    if x.ndim != 5 or x.dtype != F16:
+        raise ValueError("x must be fp16 [B,C,T,H,W]")
+    b, c, t, h, w = x.shape
+    out = torch.empty((b * t * h * w, 27 * c), device=dev, dtype=F16)
+    _lib.check(_lib.load().h3b_im2col_causal_f16(x.data_ptr(), _lib.i64_array(x.shape), _lib.i64_array(x.stride()),
+                                                 out.data_ptr(), _stream(dev)))
+    _count(1)
+    return out
+
+
+def conv_weight_rows(weight: torch.Tensor) -> torch.Tensor:
+    """fp16 [N, C, kd, kh, kw] conv weight -> [N, kd*kh*kw*C] rows in (kd, kh, kw, c) order."""
+    n = weight.shape[0]
+    return weight.detach().permute(0, 2, 3, 4, 1).reshape(n, -1).contiguous()
+
+
 def quantize_tensor_i8(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
     """Per-tensor half-away INT8 quantization of fp16 [B,C,D,H,W] (any strides) to NDHWC int8."""
     dev = _require_cuda(x)

@@ -24,9 +24,11 @@ opt/decoder_fused_qk_rope.py:56-74, opt/decoder_final_norm.py:35-72):
 
 INT8 convolutions and linears run on the tcgen05 kernels, and so do the fp16 convolutions outside
 the INT8 scope (the encoder's input conv, strided downsamples, 1x1x1 shortcuts, conv_out and the
-decoder's upsampling and RGB convs, which the reference leaves in fp16 on cuDNN).  Two narrow convs
-stay on cuDNN through torch: the decoder's 16-channel latent conv-in and the encoder's 32-channel
-1x1x1 quant conv, whose inputs are narrower than one 128-byte K row of the tcgen05 kernels.
+decoder's upsampling and RGB convs, which the reference leaves in fp16 on cuDNN).  The two convs
+whose inputs are narrower than one 128-byte K row of the implicit-GEMM conv run as tcgen05 fp16
+GEMMs: the decoder's 16-channel latent conv-in on rows unrolled by h3b_im2col_causal_f16, the
+encoder's 32-channel 1x1x1 quant conv on the channels-last moments as they are.  cuDNN (through
+torch) remains only for conv geometries outside these kernels' contracts (none in the H3 configs).
 """
 from __future__ import annotations
 
@@ -70,7 +72,8 @@ def quantize_rowwise_weight(weight: torch.Tensor) -> tuple[torch.Tensor, torch.T
 
 
 # ---------------------------------------------------------------------------
-# fp16 helpers (cuDNN convolutions outside the INT8 scope)
+# fp16 helpers: padding and the cuDNN reference conv for geometries outside the kernels' contracts;
+# the narrow-input convs as tcgen05 GEMMs
 # ---------------------------------------------------------------------------
 def causal_reflect_pad(x: torch.Tensor) -> torch.Tensor:
     """Reflect pad 1 in H/W, two zero frames in front (the causal 3x3x3 conv input)."""
@@ -82,12 +85,30 @@ def conv_f16(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None, stride=(1
     return F.conv3d(x, w, b, stride=stride).contiguous(memory_format=CL3)
 
 
+def conv1x1_f16(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor | None) -> torch.Tensor:
+    """1x1x1 conv of a channels-last fp16 [B, C, T, H, W] tensor as one tcgen05 fp16 GEMM
+    (positions x C times the [O, C] weight); returns channels-last [B, O, T, H, W]."""
+    bsz, c, t, h, w_ = x.shape
+    o = w.shape[0]
+    rows = x.permute(0, 2, 3, 4, 1).reshape(-1, c)        # a view of channels-last storage
+    y = K.gemm_f16(rows.contiguous(), w.reshape(o, c), b)
+    return y.view(bsz, t, h, w_, o).permute(0, 4, 1, 2, 3)
+
+
+def causal_conv3_rows_f16(z: torch.Tensor, w_rows: torch.Tensor, b: torch.Tensor | None) -> torch.Tensor:
+    """Causal 3x3x3 conv (two zero frames in front, reflect 1 in H/W) of fp16 [B, C, T, H, W] with
+    C % 8 == 0 as unrolled rows times the [O, 27*C] weight rows: fp16 [B*T*H*W, O], rows in
+    (b, t, h, w) order -- the input conv of the 16-channel latents, narrower than one 128-byte K
+    row of the implicit-GEMM conv."""
+    return K.gemm_f16(K.im2col_causal_f16(z), w_rows, b)
+
+
 class Conv3dF16:
     """One fp16 valid conv of the model.  Input channel counts that are a multiple of 64 with at
     least 16 outputs run on the tcgen05 fp16 implicit-GEMM kernel (bias and an optional residual
     add fused, stride-2 through TMA element strides); the 3-channel RGB output conv runs on the
-    tap-packing kernel (h3b_conv3d_rgb_f16).  The narrow-input ones stay on cuDNN: 16-channel
-    latents and the 32-channel quant conv (inputs narrower than one 128-byte K row)."""
+    tap-packing kernel (h3b_conv3d_rgb_f16).  Other geometries (none in the H3 configurations)
+    fall back to cuDNN through torch."""
 
     def __init__(self, w: torch.Tensor, b: torch.Tensor | None, stride=(1, 1, 1)):
         self.w, self.b, self.stride = w, b, tuple(stride)
@@ -257,7 +278,7 @@ class H3Encoder:
                 h = down(h, causal=True)
         y = K.norm_pad_f16(h, self.norm_out_w, self.norm_out_b, self.cfg.eps)
         moments = self.conv_out(y, causal=True)
-        return conv_f16(moments, self.quant_w, self.quant_b)
+        return conv1x1_f16(moments, self.quant_w, self.quant_b)
 
 
 # ---------------------------------------------------------------------------
@@ -336,6 +357,7 @@ class H3Decoder:
         lc, d = cfg.latent_channels, cfg.hidden
         self.conv_in_w = _randn(gen, (d, lc, 3, 3, 3), 1.0 / math.sqrt(lc * 27), device).contiguous(memory_format=CL3)
         self.conv_in_b = _randn(gen, (d,), 0.02, device)
+        self._conv_in_rows: tuple[torch.Tensor, torch.Tensor] | None = None
         self.blocks = [_DecoderBlock(cfg, gen, device) for _ in range(cfg.blocks)]
         self.ln_w = (1.0 + 0.1 * torch.randn(d, generator=gen)).half().to(device)
         self.ln_b = (0.1 * torch.randn(d, generator=gen)).half().to(device)
@@ -444,6 +466,12 @@ class H3Decoder:
         y = K.final_residual_layernorm(h_state, out, prev_scale2, self.ln_w, self.ln_b, cfg.eps)
         return y.view(b, n, d)
 
+    def conv_in_rows(self) -> torch.Tensor:
+        """The conv-in weight as [hidden, 27*latent] GEMM rows, rebuilt only when conv_in_w is replaced."""
+        if self._conv_in_rows is None or self._conv_in_rows[0] is not self.conv_in_w:
+            self._conv_in_rows = (self.conv_in_w, K.conv_weight_rows(self.conv_in_w))
+        return self._conv_in_rows[1]
+
     @torch.no_grad()
     def __call__(self, z: torch.Tensor) -> torch.Tensor:
         """z: fp16 [B, latent, t, h, w] -> raw decoder output fp16 [B, 3, T, H, W] (before finalize)."""
@@ -451,8 +479,7 @@ class H3Decoder:
             raise RuntimeError("H3Decoder requires CUDA input (no CPU fallback)")
         cfg = self.cfg
         b, _, t, h, w = z.shape
-        feat = conv_f16(causal_reflect_pad(z.half()), self.conv_in_w, self.conv_in_b)   # NDHWC [B,d,t,h,w]
-        tokens = feat.permute(0, 2, 3, 4, 1).reshape(b, t * h * w, cfg.hidden)        # a view of NDHWC storage
+        tokens = causal_conv3_rows_f16(z.half(), self.conv_in_rows(), self.conv_in_b).view(b, t * h * w, cfg.hidden)
         y = self.transformer(tokens, (t, h, w))
         x = y.view(b, t, h, w, cfg.hidden).permute(0, 4, 1, 2, 3)                      # NDHWC logical [B,d,t,h,w]
         # Each stage: GN + SiLU + pad -> conv (its bias is carried as the next producer's pre_bias,

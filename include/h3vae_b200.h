@@ -119,6 +119,18 @@ int h3b_conv_in_f16(const void* x, const int64_t* dims5, const int64_t* strides5
                     const float* norm_std, const void* w, int64_t out_channels, const void* bias,
                     void* out, void* workspace, size_t workspace_bytes, h3b_stream_t stream);
 
+/* Decoder latent conv-in operand: the causal 3x3x3 conv's input unrolled into
+ * GEMM rows.  x fp16 logical [B, C, T, H, W] (element strides5, C % 8 == 0) ->
+ * out fp16 [B*T*H*W, 27*C] (16-byte aligned), row (b, t, y, x), column
+ * (kd*9 + kh*3 + kw)*C + c = x[b, c, t+kd-2, y+kh-1, x+kw-1] with the two
+ * causal zero frames in front and reflect padding 1 in H/W (zero padding when
+ * H or W is 1).  out times a [N, 27*C] weight (h3b_gemm_f16) is the conv.
+ * ref: the decoder's first causal conv on the latent (klvae module, built by
+ *      h3vae_runtime.py:218-247; not in the checkout) with the causal padding
+ *      of opt/encoder_internal_padding.py:27-36 */
+int h3b_im2col_causal_f16(const void* x, const int64_t* dims5, const int64_t* strides5, void* out,
+                          h3b_stream_t stream);
+
 /* Decoder output conv to RGB: 3x3x3 valid conv from C channels (C % 64 == 0,
  * C <= 256) to 3, fp32 accumulate, + bias.  The 27 taps are packed into the
  * MMA's N dimension (see conv_rgb.cu) so each input row is read once per

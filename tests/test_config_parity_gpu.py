@@ -223,7 +223,7 @@ def test_config3_encoder_call_layer_by_layer(cuda_lib):
     and this random-init network amplifies any perturbation about 5x per stage -- the same amplification
     that turns INT8 quantization noise into the 37 dB encoder PSNR.  Layer by layer every kernel matches."""
     from h3vae_b200 import kernels as K
-    from h3vae_b200.model import EncoderConfig, H3Encoder, conv_f16
+    from h3vae_b200.model import EncoderConfig, H3Encoder, conv1x1_f16
     from oracle import cpu_model as C
     enc = H3Encoder(EncoderConfig(), device="cuda", seed=0)
     g = torch.Generator().manual_seed(8)
@@ -273,7 +273,8 @@ def test_config3_encoder_call_layer_by_layer(cuda_lib):
     check("norm_out", y, C._reflect_causal_pad(C.norm_silu(cpu(h), enc.norm_out_w, enc.norm_out_b, enc.cfg.eps)))
     mo = enc.conv_out(y, causal=True)
     check("conv_out", mo, C.conv_f16(cpu(y), enc.conv_out_w, enc.conv_out_b))
-    out = conv_f16(mo, enc.quant_w, enc.quant_b)
+    out = conv1x1_f16(mo, enc.quant_w, enc.quant_b)
+    check("quant_conv", out, C.conv_f16(cpu(mo), enc.quant_w, enc.quant_b))
     assert torch.equal(out, enc(x.cuda(), norm=(mean, std)))        # the walk is the model's call
     end_to_end = _rel(out, C.encoder_forward(enc, x, IMG_MEAN, IMG_STD, acc_dtype=torch.float64))
     print("config-3 encoder call, worst layer rel L2: "
@@ -287,7 +288,7 @@ def test_config4_decoder_call_layer_by_layer(cuda_lib):
     layer by layer (each producer and conv against the oracle on its GPU input); and the walk's output
     equal bit for bit to the model's own call."""
     from h3vae_b200 import kernels as K
-    from h3vae_b200.model import DecoderConfig, H3Decoder, causal_reflect_pad, conv_f16
+    from h3vae_b200.model import DecoderConfig, H3Decoder, causal_conv3_rows_f16
     from oracle import cpu_model as C
     dec = H3Decoder(DecoderConfig(), device="cuda", seed=1, int8=True)
     cfg = dec.cfg
@@ -302,9 +303,10 @@ def test_config4_decoder_call_layer_by_layer(cuda_lib):
         assert r < bar, (name, r)
 
     b, _, t, hh, ww = z.shape
-    feat = conv_f16(causal_reflect_pad(z.cuda()), dec.conv_in_w, dec.conv_in_b)
+    rows = causal_conv3_rows_f16(z.cuda(), dec.conv_in_rows(), dec.conv_in_b)        # [b*t*h*w, hidden]
+    feat = rows.view(b, t, hh, ww, cfg.hidden).permute(0, 4, 1, 2, 3)
     check("conv_in", feat, C.conv_f16(C._reflect_causal_pad(z.float()), dec.conv_in_w, dec.conv_in_b))
-    tokens = feat.permute(0, 2, 3, 4, 1).reshape(b, t * hh * ww, cfg.hidden)
+    tokens = rows.view(b, t * hh * ww, cfg.hidden)
     y = dec.transformer(tokens, (t, hh, ww))
     ref_blocks = torch.from_numpy(_oracle_int8_chain(dec, cpu(tokens).half().numpy(), (t, hh, ww)).astype(np.float32))
     # six blocks of INT8 requantization amplify last-bit differences (1.2e-3 after one block, 3e-3 after

@@ -144,3 +144,42 @@ def test_conv_rgb_matches_fp32_reference(cuda_lib, shape, with_bias):
                          None if b is None else b.cuda())
     assert y.is_contiguous()
     _close(y.cpu(), _ref(x, w, b, (1, 1, 1)))
+
+
+@pytest.mark.parametrize("shape,channels_last", [((1, 16, 5, 8, 8), False), ((2, 16, 7, 12, 20), True),
+                                                 ((1, 8, 1, 9, 6), False), ((1, 16, 3, 1, 7), True)])
+def test_latent_conv_in_rows_match_fp32_reference(cuda_lib, shape, channels_last):
+    """The decoder's 16-channel latent conv-in as unrolled rows (h3b_im2col_causal_f16: two causal
+    zero frames, reflect pad 1 in H/W, zero pad when H or W is 1) times the weight rows on the
+    tcgen05 fp16 GEMM vs PyTorch fp32 on the padded input; also the unrolled rows themselves against
+    the padded tensor, bit for bit."""
+    from h3vae_b200 import kernels as K
+    from h3vae_b200.model import causal_conv3_rows_f16, causal_reflect_pad
+    g = torch.Generator().manual_seed(sum(shape))
+    b_, c, t, h, w_ = shape
+    z = torch.randn(shape, generator=g).half()
+    wt = (torch.randn((256, c, 3, 3, 3), generator=g) / (27 * c) ** 0.5).half()
+    bias = (torch.randn(256, generator=g) * 0.1).half()
+    zc = z.cuda().contiguous(memory_format=torch.channels_last_3d) if channels_last else z.cuda()
+    cols = K.im2col_causal_f16(zc).cpu()
+    padded = causal_reflect_pad(z.float())                                   # [B, C, T+2, H+2, W+2]
+    unfold = padded.unfold(2, 3, 1).unfold(3, 3, 1).unfold(4, 3, 1)        # [B, C, T, H, W, 3, 3, 3]
+    ref_cols = unfold.permute(0, 2, 3, 4, 5, 6, 7, 1).reshape(b_ * t * h * w_, 27 * c)
+    assert torch.equal(cols.float(), ref_cols)
+    rows = causal_conv3_rows_f16(zc, K.conv_weight_rows(wt.cuda()), bias.cuda())
+    got = rows.view(b_, t, h, w_, 256).permute(0, 4, 1, 2, 3).cpu()
+    ref = F.conv3d(padded, wt.float(), bias.float()).half().float()
+    _close(got, ref)
+
+
+def test_quant_conv_1x1_matches_fp32_reference(cuda_lib):
+    """The encoder's 32-channel 1x1x1 quant conv as one tcgen05 fp16 GEMM on the channels-last moments
+    (a [positions, 32] matrix as stored) vs PyTorch fp32."""
+    from h3vae_b200.model import conv1x1_f16
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn((2, 32, 5, 9, 13), generator=g).half()
+    w = (torch.randn((32, 32, 1, 1, 1), generator=g) / 32 ** 0.5).half()
+    b = (torch.randn(32, generator=g) * 0.1).half()
+    y = conv1x1_f16(x.cuda().contiguous(memory_format=torch.channels_last_3d), w.cuda(), b.cuda())
+    assert y.shape == x.shape and y.is_contiguous(memory_format=torch.channels_last_3d)
+    _close(y.cpu(), F.conv3d(x.float(), w.float(), b.float()).half().float())

@@ -25,7 +25,7 @@ def test_library_exports_every_header_symbol():
     build_lib.build()
     lib = _lib.load()
     symbols = _header_symbols()
-    assert len(symbols) == 37
+    assert len(symbols) == 38
     missing = [s for s in symbols if not hasattr(lib, s)]
     assert not missing, f"declared in the header but not exported: {missing}"
     assert set(symbols) == set(_lib._SIGNATURES), "ctypes signature table out of sync with the header"
