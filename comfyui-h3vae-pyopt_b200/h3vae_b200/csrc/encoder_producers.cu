@@ -638,27 +638,30 @@ __global__ void tensor_quant_kernel(const __half* __restrict__ x, Strided5 t, in
 // Pixel finalization: clamp(x*std + mean, 0, 1) without FMA, NaN preserved.
 // ---------------------------------------------------------------------------
 template <typename T>
-__global__ void finalize_pixels_kernel(const T* __restrict__ x, Strided5 t, int64_t total,
-                                       const float* __restrict__ std3, const float* __restrict__ mean3,
-                                       float* __restrict__ out, int contiguous) {
-  const int64_t thw = t.n[2] * t.n[3] * t.n[4];
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int c = static_cast<int>((i / thw) % 3);
-    int64_t off = i;
-    if (!contiguous) {
-      const int64_t w = i % t.n[4];
-      const int64_t h = (i / t.n[4]) % t.n[3];
-      const int64_t d = (i / (t.n[4] * t.n[3])) % t.n[2];
-      const int64_t b = i / (thw * 3);
-      off = b * t.s[0] + c * t.s[1] + d * t.s[2] + h * t.s[3] + w * t.s[4];
+__global__ void finalize_pixels_kernel(const T* __restrict__ x, Strided5 t, const float* __restrict__ std3,
+                                       const float* __restrict__ mean3, float* __restrict__ out) {
+  // One (b, c, frame, row) per block iteration: its source and destination offsets are formed once,
+  // the threads stream the row's columns (unit stride on both sides for the decoder canvases).
+  const int64_t rows = t.n[0] * 3 * t.n[2] * t.n[3];
+  const int64_t width = t.n[4];
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const int64_t h = r % t.n[3];
+    int64_t q = r / t.n[3];
+    const int64_t d = q % t.n[2];
+    q /= t.n[2];
+    const int c = static_cast<int>(q % 3);
+    const int64_t b = q / 3;
+    const T* src = x + b * t.s[0] + c * t.s[1] + d * t.s[2] + h * t.s[3];
+    float* dst = out + r * width;
+    const float sd = std3[c], mn = mean3[c];
+    for (int64_t w = threadIdx.x; w < width; w += blockDim.x) {
+      float v;
+      if constexpr (sizeof(T) == 2) v = __half2float(src[w * t.s[4]]);
+      else v = src[w * t.s[4]];
+      float value = __fadd_rn(__fmul_rn(v, sd), mn);
+      value = value < 0.0f ? 0.0f : (value > 1.0f ? 1.0f : value);
+      dst[w] = value;
     }
-    float v;
-    if constexpr (sizeof(T) == 2) v = __half2float(x[off]);
-    else v = x[off];
-    float value = __fadd_rn(__fmul_rn(v, std3[c]), mean3[c]);
-    value = value < 0.0f ? 0.0f : (value > 1.0f ? 1.0f : value);
-    out[i] = value;
   }
 }
 
@@ -1026,26 +1029,19 @@ int h3b_finalize_pixels(const void* x, int x_is_fp16, const int64_t* dims5, cons
     return h3b_host::set_error(H3B_EINVAL, "%s: NULL argument", name);
   if (dims5[1] != 3) return h3b_host::set_error(H3B_EINVAL, "%s: nonempty B,3,T,H,W tensor required", name);
   Strided5 t{};
-  int64_t total = 1;
   for (int i = 0; i < 5; ++i) {
     t.n[i] = dims5[i];
     t.s[i] = strides5[i];
     if (dims5[i] <= 0) return h3b_host::set_error(H3B_EINVAL, "%s: nonempty B,3,T,H,W tensor required", name);
-    total *= dims5[i];
-  }
-  int64_t expect = 1;
-  int contiguous = 1;
-  for (int i = 4; i >= 0; --i) {
-    if (t.n[i] != 1 && t.s[i] != expect) contiguous = 0;
-    expect *= t.n[i];
   }
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t rows = t.n[0] * 3 * t.n[2] * t.n[3];
+  const int threads = t.n[4] >= 256 ? 256 : 128;
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, static_cast<int64_t>(h3b_host::num_sms()) * 16));
   if (x_is_fp16)
-    finalize_pixels_kernel<__half><<<grid_for(total, 256), 256, 0, st>>>(static_cast<const __half*>(x), t, total, std3,
-                                                                          mean3, out, contiguous);
+    finalize_pixels_kernel<__half><<<grid, threads, 0, st>>>(static_cast<const __half*>(x), t, std3, mean3, out);
   else
-    finalize_pixels_kernel<float><<<grid_for(total, 256), 256, 0, st>>>(static_cast<const float*>(x), t, total, std3,
-                                                                         mean3, out, contiguous);
+    finalize_pixels_kernel<float><<<grid, threads, 0, st>>>(static_cast<const float*>(x), t, std3, mean3, out);
   return h3b_host::check_launch(name);
 }
 

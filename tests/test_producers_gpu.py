@@ -138,6 +138,12 @@ def test_finalize_pixels(cuda_lib):
         got = out.cpu().numpy()
         assert np.array_equal(np.isnan(got), np.isnan(ref))
         assert np.array_equal(np.nan_to_num(got), np.nan_to_num(ref))
+    # a frame-major fp32 canvas ([b, t, c, h, w] storage viewed as [b, c, t, h, w]), two batch
+    # entries, rows wider than one pass of the block's threads
+    fm = (torch.randn(2, 5, 3, 7, 300, generator=g) * 3).permute(0, 2, 1, 3, 4)
+    out = K.finalize_pixels(fm.cuda(), std.cuda(), mean.cuda())
+    assert out.is_contiguous()
+    assert np.array_equal(out.cpu().numpy(), O.finalize_pixels(fm.numpy(), std.numpy(), mean.numpy()))
 
 
 @pytest.mark.parametrize("m,k", [(1, 2048), (17, 1024), (129, 2048), (7188, 2048), (64, 8192), (3, 16384),
