@@ -282,13 +282,18 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         b, c, t, h, w = shape5
         return torch.zeros((b, t, c, h, w), dtype=dtype, device=device).permute(0, 2, 1, 3, 4)
 
-    def _aux_stream(self):
-        """The runtime's side stream (uploads, window cut-outs, chunk downloads), created once: the
-        caching allocator reuses a freed block only on the stream it was allocated on, so a fresh
-        stream per call would make every call allocate its windows and staging anew."""
-        if getattr(self, "_aux", None) is None:
-            self._aux = torch.cuda.Stream(self.dev)
-        return self._aux
+    def _aux_stream(self, role: str):
+        """The runtime's side stream for one role ("copy": host uploads and chunk downloads;
+        "scatter": window cut-outs sent to the other ranks), created once: the caching allocator
+        reuses a freed block only on the stream it was allocated on, so a fresh stream per call
+        would make every call allocate its windows and staging anew.  Separate roles keep a window
+        from queueing behind the upload of frames it does not read."""
+        streams = getattr(self, "_aux", None)
+        if streams is None:
+            streams = self._aux = {}
+        if role not in streams:
+            streams[role] = torch.cuda.Stream(self.dev)
+        return streams[role]
 
     def _gather_slabs(self, canvas, slab, boxes, on_slab=None) -> list:
         """Bring every rank's blend slab to rank 0.  Rank r > 0 accumulated its work items into
@@ -535,7 +540,7 @@ class H3VAEPyOptRuntime(torch.nn.Module):
             sends = []
             if self.world > 1:
                 import torch.distributed as dist
-                side = self._aux_stream() if self.dev.type == "cuda" else None
+                side = self._aux_stream("scatter") if self.dev.type == "cuda" else None
                 if side is not None:
                     side.wait_stream(torch.cuda.current_stream(self.dev))
                 for q in range(1, self.world):
@@ -565,7 +570,7 @@ class H3VAEPyOptRuntime(torch.nn.Module):
         """Issue the host->device copy of each clip batch's frames on a side stream (one contiguous
         copy per (batch entry, channel) plane).  Returns the device video and one event per clip batch."""
         x_dev = torch.empty(x_host.shape, dtype=x_host.dtype, device=self.dev)
-        copy_stream = self._aux_stream()
+        copy_stream = self._aux_stream("copy")
         copy_stream.wait_stream(torch.cuda.current_stream(self.dev))
         events = []
         with torch.cuda.stream(copy_stream):
@@ -641,7 +646,7 @@ class H3VAEPyOptRuntime(torch.nn.Module):
                     and self.dev.type == "cuda" and output_buffer.is_pinned()
                     and output_buffer.dtype == torch.float32 and output_buffer.is_contiguous()
                     and tuple(output_buffer.shape) == (b, 3, frames, pplan.height, pplan.width))
-        copy_stream = self._aux_stream() if streamed else None
+        copy_stream = self._aux_stream("copy") if streamed else None
         pending = {}
         for (bi, c, _, _) in tasks:
             pending[(bi, c)] = pending.get((bi, c), 0) + 1
